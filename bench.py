@@ -1,0 +1,490 @@
+#!/usr/bin/env python
+"""Benchmark of the dequant-fused quantized matmul (the BASELINE.json metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl nxq|reference]
+
+Workload (one "step"): BASELINE.json config 2 - the Q4_K GEMV over a
+Llama-3-8B MLP, gate and up (K=4096, N=14336) and down (K=14336, N=4096), at
+every decode batch M in {1, 4, 8, 16, 32}: 15 quantized matmuls per step,
+fp16 activations, fp32 output, fp32 accumulation.  Weights are synthetic
+(seeded; nxq.synth) and HBM-resident; every call reads a different weight
+replica, and the replicas of each projection span more than 4x the 126 MB L2,
+so each call streams its weights from HBM.
+
+value      = algorithmic bytes of all calls (packed weight blocks + x + y) over
+             the device time of the K timed steps (CUDA events, max over ranks)
+e2e        = the same workload through the drop-in host entry point
+             nxq_qmatmul_host (fp32 host activations in, fp32 host output out,
+             copies inside the timed region), wall clock
+roofline   = the dominant kernel's algorithmic GB/s against the measured HBM
+             copy bandwidth in MEASURED_PEAKS.json
+prefill    = BASELINE.json config 4: Q4_K GEMM at M in {512, 2048, 8192},
+             K=4096, N=14336, bf16 activations and bf16 output, TFLOP/s
+cpu_baseline = the reference's CPU path (its own decoders from
+             oracle/_ref when built, else the oracle restatement, plus fp32
+             dot products) on a bounded row sample of the same workload
+
+With --gpus N > 1 (torchrun, one process per GPU) every rank runs the same
+per-GPU workload (weak scaling); the tensor-parallel config-5 layer is
+reported as "tp".  --impl reference times the reference CPU path instead, on
+rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import datetime
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "nexus-inference-engine-_b200"))
+
+METRIC = "Q4_K dequant-GEMV achieved HBM GB/s vs ~8 TB/s; prefill GEMM TFLOP/s"
+GEMV_MS = [1, 4, 8, 16, 32]
+PROJ = [("gate", 4096, 14336), ("up", 4096, 14336), ("down", 14336, 4096)]  # name, K, N
+PREFILL_MS = [512, 2048, 8192]
+Q4_K = 12
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def weight_bytes(K: int, N: int) -> int:
+    return N * (K // 256) * 144
+
+
+def call_bytes(M: int, K: int, N: int, x_size: int = 2, y_size: int = 4) -> int:
+    return weight_bytes(K, N) + M * K * x_size + M * N * y_size
+
+
+# ---------------------------------------------------------------- distributed
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world <= 1:
+        return 0, 1, 0
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ["RANK"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world <= 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples of this GPU's clocks and throttle reasons while running."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        import torch
+
+        self.proc = None
+        self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            gid = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-i", gid,
+                 "-lms", "100"], stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except Exception as e:  # noqa: BLE001
+            log("clock sampling unavailable:", e)
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.tmp.flush()
+        self.tmp.seek(0)
+        rows = [r for r in csv.reader(io.StringIO(self.tmp.read())) if len(r) >= 9]
+        os.unlink(self.tmp.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+
+        def num(s):
+            try:
+                return float(s.strip())
+            except ValueError:
+                return None
+
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        loaded = [v for v in sm if mx and v >= 0.5 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- CPU reference path
+def cpu_reference_sample(seconds: float, rows_frac: int = 32, threads: int | None = None) -> dict:
+    """The reference CPU path on a row sample of the config-2 workload:
+    every projection's first N/rows_frac rows, every M, repeated for ~seconds."""
+    from nxq import synth
+    from oracle import loader
+
+    kind = "reference" if loader.ref() is not None else "port"
+    threads = threads or os.cpu_count() or 1
+    cases = []
+    for name, K, N in PROJ:
+        n_s = N // rows_frac
+        blocks = synth.make_blocks(Q4_K, n_s, K, seed=900 + [p[0] for p in PROJ].index(name))
+        for M in GEMV_MS:
+            x = synth.make_activations(M, K, seed=M, dtype=np.float16).astype(np.float32)
+            cases.append((blocks, n_s, K, x, M))
+    total_b = 0
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        for blocks, n_s, K, x, M in cases:
+            loader.qmatmul(Q4_K, blocks, n_s, K, x, which="ref" if kind == "reference" else "port",
+                           nthreads=threads)
+            total_b += call_bytes(M, K, n_s)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return {"value": total_b / el / 1e9, "unit": "GB/s", "cores": threads, "kind": kind,
+            "sample": (f"config-2 workload on the first 1/{rows_frac} of each projection's rows "
+                       f"(gate/up {14336 // rows_frac} rows, down {4096 // rows_frac} rows, all K), "
+                       f"M in {GEMV_MS}, {reps} pass(es), {el:.1f} s; decode by "
+                       f"{'the reference decoders (gguf_importer.cpp, oracle/_ref)' if kind == 'reference' else 'the oracle restatement'}"
+                       " + fp32 dot products"),
+            "seconds": el}
+
+
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return 0
+    steps, warmup = args.steps, args.warmup
+    from nxq import synth
+    from oracle import loader
+
+    kind = "reference" if loader.ref() is not None else "port"
+    threads = os.cpu_count() or 1
+    rows_frac = 4
+    cases = []
+    for name, K, N in PROJ:
+        n_s = N // rows_frac
+        blocks = synth.make_blocks(Q4_K, n_s, K, seed=900 + [p[0] for p in PROJ].index(name))
+        for M in GEMV_MS:
+            x = synth.make_activations(M, K, seed=M, dtype=np.float16).astype(np.float32)
+            cases.append((blocks, n_s, K, x, M))
+
+    def step():
+        b = 0
+        for blocks, n_s, K, x, M in cases:
+            loader.qmatmul(Q4_K, blocks, n_s, K, x, which="ref" if kind == "reference" else "port",
+                           nthreads=threads)
+            b += call_bytes(M, K, n_s)
+        return b
+
+    for _ in range(warmup):
+        step()
+    t0 = time.perf_counter()
+    tb = sum(step() for _ in range(steps))
+    el = time.perf_counter() - t0
+    v = tb / el / 1e9
+    sample = (f"each step: the config-2 workload on the first 1/{rows_frac} of each projection's rows, "
+              f"all K, M in {GEMV_MS}")
+    line = {"metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": el / steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": "BASELINE config 2: Q4_K GEMV, Llama-3-8B MLP gate/up/down, M in {1,4,8,16,32}",
+                       "sample": sample},
+            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
+            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- GPU arm
+def traffic_lookup(kernel: str, shape: str):
+    p = ROOT / "profiles" / "dram_traffic.txt"
+    if not p.exists():
+        return None
+    for ln in p.read_text().splitlines():
+        parts = ln.split()
+        if len(parts) >= 3 and not ln.startswith("#") and parts[0] == kernel and parts[1] == shape:
+            try:
+                return float(parts[2])
+            except ValueError:
+                return None
+    return None
+
+
+def run_gpu_arm(args, rank, world, local):
+    import torch
+
+    import nxq
+    from nxq import synth
+
+    torch.cuda.set_device(local)
+    nxq.init(local)
+    pk, pk_kind = peaks()
+    dev = torch.device("cuda", local)
+
+    # --- weights: R replicas per projection, R * bytes(proj) > 4 x L2 --------
+    reps = max(2, -(-4 * L2_BYTES // weight_bytes(4096, 14336)) + 1)
+    weights = {}
+    for name, K, N in PROJ:
+        blocks = synth.make_blocks(Q4_K, N, K, seed=1000 + K + N + rank)
+        weights[name] = [nxq.Weight.register(blocks, Q4_K, N, K) for _ in range(reps)]
+        del blocks
+    xs = {M: {K: torch.randn(M, K, generator=torch.Generator().manual_seed(M * 7 + K), dtype=torch.float32)
+              .to(torch.float16).to(dev) for K in (4096, 14336)} for M in GEMV_MS}
+    ys = {M: {N: torch.empty(M, N, dtype=torch.float32, device=dev) for N in (4096, 14336)} for M in GEMV_MS}
+    calls = []  # (weight list, K, N, M)
+    for M in GEMV_MS:
+        for name, K, N in PROJ:
+            calls.append((name, K, N, M))
+    step_bytes = sum(call_bytes(M, K, N) for _, K, N, M in calls)
+    names = {(name, M): nxq.kernel_name(weights[name][0], M, nxq.F16, nxq.F32) for name, K, N, M in calls}
+    counter = [0]
+
+    def step(events=None):
+        for i, (name, K, N, M) in enumerate(calls):
+            w = weights[name][counter[0] % reps]
+            if events is not None:
+                events[i][0].record()
+            nxq.qmatmul(w, xs[M][K], out=ys[M][N])
+            if events is not None:
+                events[i][1].record()
+            if name == "down":
+                pass
+        counter[0] += 1
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    nxq.stream_sync()
+
+    # --- timed region --------------------------------------------------------
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in calls] for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    l0 = nxq.launch_count()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    for s in range(args.steps):
+        step(ev[s])
+    t_end.record()
+    torch.cuda.synchronize()
+    launches = nxq.launch_count() - l0
+    barrier(world)
+    clk = clocks.stop()
+    nxq.stream_sync()
+    ms = t_start.elapsed_time(t_end)
+    ms_max = max_over_ranks(ms, world)
+    value = step_bytes * args.steps * world / (ms_max / 1e3) / 1e9
+
+    # per-call and per-kernel accounting
+    per_kernel = {}
+    per_case = {}
+    for s in range(args.steps):
+        for i, (name, K, N, M) in enumerate(calls):
+            d = ev[s][i][0].elapsed_time(ev[s][i][1])
+            kname = names[(name, M)]
+            k = per_kernel.setdefault(kname, {"ms": 0.0, "bytes": 0, "launches": 0, "shapes": set()})
+            k["ms"] += d
+            k["bytes"] += call_bytes(M, K, N)
+            k["launches"] += 1
+            k["shapes"].add(f"K{K}xN{N}xM{M}")
+            c = per_case.setdefault(f"{name}_M{M}", {"ms": 0.0, "bytes": 0})
+            c["ms"] += d
+            c["bytes"] += call_bytes(M, K, N)
+    total_k = sum(k["ms"] for k in per_kernel.values())
+    dom_name, dom = max(per_kernel.items(), key=lambda kv: kv[1]["ms"])
+    achieved = dom["bytes"] / (dom["ms"] / 1e3) / 1e9
+    dom_shape = sorted(dom["shapes"])[0] if len(dom["shapes"]) == 1 else "mixed"
+    traffic = traffic_lookup(dom_name, dom_shape)
+    roofline = {"bound": "hbm", "kernel": dom_name, "achieved": achieved, "peak": pk["hbm_gbs"],
+                "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": traffic,
+                "peak_source": f"{pk_kind} hbm_gbs", "share_of_step": dom["ms"] / total_k,
+                "algorithmic_bytes_per_launch": dom["bytes"] / dom["launches"],
+                "avg_launch_us": dom["ms"] / dom["launches"] * 1e3}
+    cases_out = {k: round(v["bytes"] / (v["ms"] / 1e3) / 1e9, 1) for k, v in per_case.items()}
+    kernels_out = {k: {"launches": v["launches"], "ms": round(v["ms"], 3),
+                       "GB/s": round(v["bytes"] / (v["ms"] / 1e3) / 1e9, 1),
+                       "share": round(v["ms"] / total_k, 4)} for k, v in per_kernel.items()}
+
+    # --- e2e through the host drop-in ------------------------------------------
+    e2e = None
+    if not args.no_e2e:
+        hx = {M: {K: torch.randn(M, K, generator=torch.Generator().manual_seed(M + K)).to(torch.float16)
+                  .float().pin_memory().numpy() for K in (4096, 14336)} for M in GEMV_MS}
+        hy = {M: {N: torch.empty(M, N, dtype=torch.float32).pin_memory().numpy() for N in (4096, 14336)}
+              for M in GEMV_MS}
+        e2e_steps = max(1, min(args.steps, 10))
+        h2d = sum(M * K * 4 for _, K, N, M in calls)
+        d2h = sum(M * N * 4 for _, K, N, M in calls)
+        e2e_bytes = sum(call_bytes(M, K, N, x_size=4) for _, K, N, M in calls)
+
+        def host_step():
+            for name, K, N, M in calls:
+                nxq.qmatmul_host(weights[name][counter[0] % reps], hx[M][K], out=hy[M][N])
+            counter[0] += 1
+
+        for _ in range(2):
+            host_step()
+        barrier(world)
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            host_step()
+        el = max_over_ranks(time.perf_counter() - t0, world)
+        e2e = {"value": e2e_bytes * e2e_steps * world / el / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "api": "nxq_qmatmul_host (fp32 host x/y, weights resident)", "steps": e2e_steps,
+               "ms_per_step": el / e2e_steps * 1e3}
+
+    for name in weights:
+        for w in weights[name]:
+            w.release()
+    torch.cuda.empty_cache()
+
+    # --- prefill GEMM (config 4) ------------------------------------------------
+    prefill = None
+    if not args.no_prefill:
+        K, N = 4096, 14336
+        blocks = synth.make_blocks(Q4_K, N, K, seed=4000)
+        w = nxq.Weight.register(blocks, Q4_K, N, K)
+        del blocks
+        prefill = {"kernel": None, "cases": {}}
+        for M in PREFILL_MS:
+            x = torch.randn(M, K, generator=torch.Generator().manual_seed(M), dtype=torch.float32).to(
+                torch.bfloat16).to(dev)
+            y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+            prefill["kernel"] = nxq.kernel_name(w, M, nxq.BF16, nxq.BF16)
+            for _ in range(3):
+                nxq.qmatmul(w, x, out=y)
+            torch.cuda.synchronize()
+            iters = 5 if M <= 2048 else 3
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            barrier(world)
+            a.record()
+            for _ in range(iters):
+                nxq.qmatmul(w, x, out=y)
+            b.record()
+            torch.cuda.synchronize()
+            t = max_over_ranks(a.elapsed_time(b) / iters, world)
+            tf = 2.0 * M * N * K / (t / 1e3) / 1e12
+            prefill["cases"][f"M{M}"] = {"ms": t, "TFLOP/s": tf,
+                                         "frac_of_bf16_burst": tf / pk["bf16_tflops"],
+                                         "frac_of_bf16_sustained": tf / pk["bf16_tflops_sustained"]}
+            del x, y
+        nxq.stream_sync()
+        w.release()
+        prefill["unit"] = "TFLOP/s"
+        prefill["workload"] = "BASELINE config 4: Q4_K GEMM K=4096 N=14336, bf16 x, bf16 y, fp32 accumulate"
+        prefill["peak_source"] = f"{pk_kind} bf16_tflops / bf16_tflops_sustained"
+
+    # --- CPU baseline (rank 0, N=1) -------------------------------------------------
+    cpu = None
+    if world == 1 and not args.no_cpu:
+        cpu = cpu_reference_sample(args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "accumulate": "f32",
+            "data": "synthetic",
+            "config": {"workload": "BASELINE config 2: Q4_K GEMV over a Llama-3-8B MLP, gate/up K=4096 "
+                                   "N=14336 and down K=14336 N=4096, M in {1,4,8,16,32}; 15 calls per step "
+                                   "(per GPU)",
+                       "weights": "Q4_K, d/dmin fp16 U(1e-4,1e-3), codes uniform (seeded)",
+                       "x": "fp16 N(0,1)", "y": "fp32",
+                       "l2": f"inputs larger than L2: {reps} weight replicas per projection "
+                             f"({reps * weight_bytes(4096, 14336) / 2**20:.0f} MiB each), rotated every call",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+            "roofline": roofline, "kernels": kernels_out, "per_case_GBps": cases_out,
+            "gpu_launches": launches, "clocks": clk, "e2e": e2e, "prefill": prefill,
+            "cpu_baseline": cpu, "nominal_hbm_frac": value / world / 8000.0,
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["nxq", "reference"], default="nxq")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        log("warmup raised to 3 (minimum)")
+        args.warmup = 3
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        return run_reference_arm(args, rank, world)
+    rank, world, local = dist_setup()
+    try:
+        return run_gpu_arm(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,204 @@
+/* nxq.h — C ABI of the B200 quantized-matmul library (libnxq.so).
+ *
+ * Drop-in replacement for the NEXUS engine's quantized-matmul operator path:
+ *   ComputeDispatch::gemm_int4 / gemv_int4   nexus/src/compute/compute_dispatch.h:47-61
+ *   MetalBackend::gemv_int4_nr8 / gemm_int4_gpu / wrap_pointer
+ *                                            nexus/src/compute/metal/metal_backend.h:60-87
+ * applied to GGUF block-quantized weights (Q4_0, Q8_0, Q4_K, Q3_K, ...) whose
+ * values are defined by nexus/src/import/gguf_importer.cpp:677-1000.
+ *
+ * Conventions
+ *   - Plain C types only; every call returns an nxq_status (0 = ok, < 0 error)
+ *     and records a message readable with nxq_last_error().
+ *   - A weight W is logically [N][K] (N output rows, K reduction), row-major,
+ *     blocks contiguous along K: the GGUF tensor order, used by the reference
+ *     as gemm_f32(..., transB=true) (nexus/src/model/transformer.cpp:249-253).
+ *   - y[M][N] = x[M][K] * W^T, fp32 accumulation.
+ *   - "device" pointers are CUDA device pointers on the current nxq device;
+ *     `stream` is a cudaStream_t (NULL = the legacy default stream).
+ *   - One context per process per device (nxq_init); calls on distinct streams
+ *     may run concurrently; weight registration and release are serialized
+ *     internally.
+ */
+#ifndef NXQ_H
+#define NXQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define NXQ_API __attribute__((visibility("default")))
+#else
+#define NXQ_API
+#endif
+
+#define NXQ_ABI_VERSION 1
+
+/* Status codes.  The reference returns void from ComputeDispatch and silently
+ * zero-fills on failure (compute_dispatch.cpp:174-176); here every failure is a
+ * negative code, and zero-filling is only an opt-in of the C++ shim. */
+typedef enum {
+    NXQ_OK = 0,
+    NXQ_ERR_ARG = -1,         /* null pointer, negative size, bad enum value   */
+    NXQ_ERR_CODEC = -2,       /* block type not supported by this entry point  */
+    NXQ_ERR_SHAPE = -3,       /* K not a multiple of the block, bytes mismatch */
+    NXQ_ERR_CUDA = -4,        /* a CUDA runtime/driver call failed             */
+    NXQ_ERR_TIMEOUT = -5,     /* a bounded device-side wait ran out            */
+    NXQ_ERR_NOMEM = -6,       /* device or host allocation failed              */
+    NXQ_ERR_STATE = -7,       /* not initialised / wrong device / TP not set up */
+    NXQ_ERR_NCCL = -8,        /* NCCL unavailable or a collective failed       */
+    NXQ_ERR_UNSUPPORTED = -9  /* no GPU of the required architecture           */
+} nxq_status;
+
+/* Block types: the GGUF type ids of nexus/src/import/gguf_importer.h:28-57. */
+typedef enum {
+    NXQ_TYPE_Q4_0 = 2,
+    NXQ_TYPE_Q4_1 = 3,
+    NXQ_TYPE_Q8_0 = 8,
+    NXQ_TYPE_Q2_K = 10,
+    NXQ_TYPE_Q3_K = 11,
+    NXQ_TYPE_Q4_K = 12,
+    NXQ_TYPE_Q5_K = 13,
+    NXQ_TYPE_Q6_K = 14
+} nxq_type;
+
+/* Activation / output element types: nexus::DType F32=0, F16=1, BF16=2
+ * (nexus/src/core/config.h:39-46). */
+typedef enum { NXQ_F32 = 0, NXQ_F16 = 1, NXQ_BF16 = 2 } nxq_dtype;
+
+/* Tensor-parallel split of one projection (north-star TP; the reference has no
+ * multi-device path).  COL: rank r owns output rows [r*N/T, (r+1)*N/T).  ROW:
+ * rank r owns reduction columns [r*K/T, (r+1)*K/T) of every row and the
+ * partial outputs are summed with an allreduce. */
+typedef enum { NXQ_SPLIT_COL = 0, NXQ_SPLIT_ROW = 1 } nxq_split;
+
+/* Opaque handle to HBM-resident packed weights.  Replaces the reference's
+ * MetalBackend::buffer_id from wrap_pointer over mmap'd chunks
+ * (metal_backend.h:40, metal_backend.mm:814-834; compute_dispatch.cpp:147-154). */
+typedef struct nxq_weight_s* nxq_weight_t;
+
+/* ---- context -------------------------------------------------------------- */
+
+/* Select `device`, check it is sm_100, create the context.  Replaces
+ * ComputeDispatch::init_gpu (compute_dispatch.cpp:47).  Idempotent per device. */
+NXQ_API int nxq_init(int device);
+
+/* Release every registered weight, scratch buffer and TP communicator. */
+NXQ_API int nxq_shutdown(void);
+
+/* Copy the calling thread's last error message (NUL-terminated, truncated to n). */
+NXQ_API int nxq_last_error(char* buf, size_t n);
+
+/* NXQ_ABI_VERSION of the loaded library. */
+NXQ_API int nxq_abi_version(void);
+
+/* Block geometry of `type`: elements per block and bytes per block
+ * (gguf_importer.cpp:291-345, with Q3_K's decoder size of 110 bytes, :797). */
+NXQ_API int nxq_block_geometry(int type, int* block_elems, int* block_bytes);
+
+/* ---- weight residency ----------------------------------------------------- */
+
+/* Upload `bytes` of GGUF blocks (N rows of K/QK blocks) from host memory and
+ * keep them resident in HBM in the library's tiled layout.  Replaces
+ * wrap_pointer + wrapped_buffer_cache_ (compute_dispatch.cpp:147-154): the
+ * device owns the copy and the host buffer may be freed after return.
+ * bytes must equal N * (K/QK) * block_bytes. */
+NXQ_API int nxq_weight_register(const void* host_blocks, size_t bytes, int type,
+                                int64_t N, int64_t K, nxq_weight_t* out);
+
+/* As nxq_weight_register, from GGUF blocks already in device memory (for
+ * loaders that stage on the GPU).  Stream-ordered on `stream`; returns after
+ * the tiled copy is complete. */
+NXQ_API int nxq_weight_register_device(const void* dev_blocks, size_t bytes, int type,
+                                       int64_t N, int64_t K, void* stream,
+                                       nxq_weight_t* out);
+
+/* Register only this rank's shard of a full host weight for tensor parallelism:
+ * COL keeps rows [r*N/T, (r+1)*N/T); ROW keeps, for every row, the blocks of
+ * columns [r*K/T, (r+1)*K/T).  N/T (COL) or K/T (ROW) must divide evenly and
+ * K/T must be a multiple of the block size. */
+NXQ_API int nxq_weight_register_shard(const void* host_blocks, size_t bytes, int type,
+                                      int64_t N, int64_t K, int split, int rank,
+                                      int world, nxq_weight_t* out);
+
+/* Host-only (no GPU needed): copy rank `rank`'s shard of a full GGUF weight
+ * into `out` (out_bytes must be bytes / world), still in GGUF row-major block
+ * order, under the same COL/ROW rules as nxq_weight_register_shard.  For
+ * loaders that slice before upload or ship shards to other hosts. */
+NXQ_API int nxq_shard_extract(const void* host_blocks, size_t bytes, int type, int64_t N,
+                              int64_t K, int split, int rank, int world, void* out,
+                              size_t out_bytes);
+
+/* Free the HBM copy (ComputeDispatch::clear_buffer_cache, compute_dispatch.cpp:853-860). */
+NXQ_API int nxq_weight_release(nxq_weight_t w);
+
+/* Shape and footprint of a registered weight (any pointer may be NULL). */
+NXQ_API int nxq_weight_info(nxq_weight_t w, int* type, int64_t* N, int64_t* K,
+                            size_t* packed_bytes, size_t* device_bytes);
+
+/* ---- compute ---------------------------------------------------------------- */
+
+/* Decode the whole weight to fp32 y_dev[N][K], bit-identical to
+ * dequant_gguf_to_fp32 (gguf_importer.cpp:958-1000).  Stream-ordered. */
+NXQ_API int nxq_dequant(nxq_weight_t w, float* y_dev, void* stream);
+
+/* y_dev[M][N] = x_dev[M][K] * W^T on `stream`, fp32 accumulation.
+ * x_dtype, y_dtype in nxq_dtype.  Device-resident form of
+ * MetalBackend::gemm_int4_gpu (metal_backend.h:86-87) with M honoured and the
+ * block codec taken from the weight.  M >= 1; any M is accepted (decode and
+ * prefill shapes share this entry point). */
+NXQ_API int nxq_qmatmul(nxq_weight_t w, const void* x_dev, int x_dtype, void* y_dev,
+                        int y_dtype, int64_t M, void* stream);
+
+/* Host-buffer form, synchronous: the drop-in for ComputeDispatch::gemm_int4
+ * (compute_dispatch.h:59-61, .cpp:142-176) - fp32 activations [M][K] in, fp32
+ * output [M][N] out, weights resident.  The reference ignores M
+ * (compute_dispatch.cpp:156-164); here every row of x is used. */
+NXQ_API int nxq_qmatmul_host(nxq_weight_t w, const float* x_host, float* y_host, int64_t M);
+
+/* Block until all work nxq queued on `stream` is done; reports any device-side
+ * error flag raised by a bounded wait as NXQ_ERR_TIMEOUT. */
+NXQ_API int nxq_stream_sync(void* stream);
+
+/* Name of the kernel nxq_qmatmul would launch for (w, M, dtypes), e.g.
+ * "tc_gemv<Q4_K,n32>" or "simt<Q3_K,mb8>".  Profiling aid; the reference's
+ * counterpart is the pipeline-name log of metal_context_impl.h:77-78. */
+NXQ_API int nxq_qmatmul_kernel_name(nxq_weight_t w, int64_t M, int x_dtype, int y_dtype,
+                                    char* buf, size_t n);
+
+/* Number of kernels libnxq has launched in this process so far. */
+NXQ_API int nxq_launch_count(uint64_t* out);
+
+/* ---- tensor parallelism (NCCL over NVLink) -------------------------------- */
+
+/* Size in bytes of the opaque id nxq_tp_unique_id writes (ncclUniqueId). */
+NXQ_API int nxq_tp_unique_id_size(void);
+
+/* Rank 0 creates the id and shares it out of band (e.g. torch.distributed). */
+NXQ_API int nxq_tp_unique_id(void* out, size_t n);
+
+/* Join the TP group (ncclCommInitRank) on the current nxq device. */
+NXQ_API int nxq_tp_init(int rank, int world, const void* unique_id, size_t n);
+
+/* Tear down the TP communicator. */
+NXQ_API int nxq_tp_shutdown(void);
+
+/* One sharded projection on `stream`.
+ *   COL: x_dev is the full [M][K]; y_dev receives this rank's [M][N/T] slice.
+ *   ROW: x_dev is this rank's [M][K/T] slice; y_dev receives the full [M][N]
+ *        sum over ranks (in-place NCCL allreduce of the fp32 partials).
+ * y_dtype NXQ_F32 only for ROW (the allreduce runs in fp32). */
+NXQ_API int nxq_tp_qmatmul(nxq_weight_t shard, const void* x_dev, int x_dtype, void* y_dev,
+                           int y_dtype, int64_t M, int split, void* stream);
+
+/* Sum `count` fp32 values across the TP group in place on `stream`. */
+NXQ_API int nxq_tp_allreduce_f32(float* buf_dev, int64_t count, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NXQ_H */

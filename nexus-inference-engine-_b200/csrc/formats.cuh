@@ -1,0 +1,300 @@
+// Block formats and the HBM residency layout.
+//
+// Block semantics follow nexus/src/import/gguf_importer.cpp (decoders at
+// :679-954); the byte offsets of every field are the reference's.  What changes
+// is where those bytes sit in HBM.  The reference wraps mmap'd GGUF/NXF chunks
+// as GPU buffers (metal_backend.mm:814-834); here registration re-tiles the
+// blocks once so that every kernel streams contiguous, 16-byte aligned tiles:
+//
+//   tile      = 128 consecutive weight rows (TILE_ROWS)
+//   chunk     = 256 consecutive reduction elements (CHUNK_K)
+//   tile-chunk = TILE_ROWS x CHUNK_K weights = TILE_ROWS "row records" of
+//                crb bytes (crb = (CHUNK_K / QK) * block_bytes); stored
+//                contiguously at ((tile * chunks_per_row) + chunk) * TILE_ROWS * crb.
+//
+// Inside a tile-chunk each format keeps a row's bytes in "planes" so a thread
+// that owns row r reads 16-byte aligned words (see place_block() below).
+// Rows beyond N and blocks beyond K are zero bytes, which every format decodes
+// to zero.  No byte is transformed: decoding the tiled copy gives exactly the
+// values of decoding the GGUF bytes.
+#pragma once
+#include <cstdint>
+#include <cuda_fp16.h>
+
+namespace nxq {
+
+constexpr int TILE_ROWS = 128;
+constexpr int CHUNK_K = 256;
+
+enum BlockType : int {
+    T_Q4_0 = 2, T_Q4_1 = 3, T_Q8_0 = 8, T_Q2_K = 10, T_Q3_K = 11,
+    T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14
+};
+
+struct Geometry {
+    int qk;    // elements per block
+    int bb;    // bytes per block
+    int crb;   // bytes per row record (one row of one tile-chunk)
+};
+
+__host__ __device__ inline bool geometry_of(int type, Geometry* g) {
+    int qk = 0, bb = 0;
+    switch (type) {
+        case T_Q4_0: qk = 32; bb = 18; break;
+        case T_Q4_1: qk = 32; bb = 20; break;
+        case T_Q8_0: qk = 32; bb = 34; break;
+        case T_Q2_K: qk = 256; bb = 84; break;
+        case T_Q3_K: qk = 256; bb = 110; break;
+        case T_Q4_K: qk = 256; bb = 144; break;
+        case T_Q5_K: qk = 256; bb = 176; break;
+        case T_Q6_K: qk = 256; bb = 210; break;
+        default: return false;
+    }
+    g->qk = qk;
+    g->bb = bb;
+    g->crb = (CHUNK_K / qk) * bb;
+    return true;
+}
+
+// Tiled-copy geometry of one registered weight.
+struct TiledShape {
+    int type;
+    int64_t N, K;
+    int64_t tiles;            // ceil(N / TILE_ROWS)
+    int64_t chunks;           // ceil(K / CHUNK_K) per row
+    int64_t tile_chunk_bytes; // TILE_ROWS * crb
+    Geometry g;
+    __host__ __device__ int64_t chunk_offset(int64_t tile, int64_t chunk) const {
+        return (tile * chunks + chunk) * tile_chunk_bytes;
+    }
+    __host__ __device__ int64_t total_bytes() const { return tiles * chunks * tile_chunk_bytes; }
+};
+
+inline bool make_tiled_shape(int type, int64_t N, int64_t K, TiledShape* s) {
+    Geometry g;
+    if (!geometry_of(type, &g) || N <= 0 || K <= 0 || K % g.qk) return false;
+    s->type = type;
+    s->N = N;
+    s->K = K;
+    s->g = g;
+    s->tiles = (N + TILE_ROWS - 1) / TILE_ROWS;
+    s->chunks = (K + CHUNK_K - 1) / CHUNK_K;
+    s->tile_chunk_bytes = (int64_t)TILE_ROWS * g.crb;
+    return true;
+}
+
+// ---------------------------------------------------------------------------
+// Byte placement of one GGUF block inside a tile-chunk.
+//   r = row within the tile (0..127), j = block index within the row record
+//   (0..CHUNK_K/QK-1).  Each format lists (source offset, length, destination)
+//   segments; planes are laid out so per-row records are 16-byte aligned where
+//   the kernels read them with vector loads.
+//
+//   Q4_0  record 144 B: [d x8 : 16 B][codes x8 : 8 x 16 B]
+//   Q4_1  record 160 B: [(d,m) x8 : 32 B][codes x8 : 8 x 16 B]
+//   Q8_0  record 272 B: [d x8 : 16 B][codes x8 : 8 x 32 B]
+//   Q4_K  record 144 B: the block itself (d, dmin, scales[12], qs[128])
+//   Q5_K  record 176 B: the block itself
+//   Q3_K  plane A 128 x 96 B (hmask[32], qs[64]); plane B 128 x 14 B (scales[12], d)
+//   Q2_K  plane A 128 x 80 B (scales[16], qs[64]); plane B 128 x 4 B (dmin, d)
+//   Q6_K  plane A 128 x 192 B (ql, qh); plane B 128 x 16 B (scales); plane C 128 x 2 B (d)
+// ---------------------------------------------------------------------------
+struct Segment {
+    int src, len;
+    int64_t dst;
+};
+
+__host__ __device__ inline int block_segments(int type, int r, int j, Segment* s) {
+    const int R = TILE_ROWS;
+    switch (type) {
+        case T_Q4_0:
+            s[0] = {0, 2, (int64_t)r * 144 + 2 * j};
+            s[1] = {2, 16, (int64_t)r * 144 + 16 + 16 * j};
+            return 2;
+        case T_Q4_1:
+            s[0] = {0, 4, (int64_t)r * 160 + 4 * j};
+            s[1] = {4, 16, (int64_t)r * 160 + 32 + 16 * j};
+            return 2;
+        case T_Q8_0:
+            s[0] = {0, 2, (int64_t)r * 272 + 2 * j};
+            s[1] = {2, 32, (int64_t)r * 272 + 16 + 32 * j};
+            return 2;
+        case T_Q4_K:
+            s[0] = {0, 144, (int64_t)r * 144};
+            return 1;
+        case T_Q5_K:
+            s[0] = {0, 176, (int64_t)r * 176};
+            return 1;
+        case T_Q3_K:
+            s[0] = {0, 96, (int64_t)r * 96};
+            s[1] = {96, 14, (int64_t)R * 96 + r * 14};
+            return 2;
+        case T_Q2_K:
+            s[0] = {0, 80, (int64_t)r * 80};
+            s[1] = {80, 4, (int64_t)R * 80 + r * 4};
+            return 2;
+        case T_Q6_K:
+            s[0] = {0, 192, (int64_t)r * 192};
+            s[1] = {192, 16, (int64_t)R * 192 + r * 16};
+            s[2] = {208, 2, (int64_t)R * 208 + r * 2};
+            return 3;
+        default:
+            return 0;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Exact device decode.  Every multiply/subtract is an explicit round-to-nearest
+// fp32 intrinsic, in the reference's evaluation order, so nvcc cannot contract
+// them into FMAs and the decoded bits equal the reference's.
+// ---------------------------------------------------------------------------
+
+// IEEE half -> float keeping subnormals and NaN payloads (gguf_importer.cpp:202-237).
+__device__ __forceinline__ float half_bits_to_float(uint32_t h) {
+    uint32_t sign = (h & 0x8000u) << 16;
+    uint32_t e = (h >> 10) & 31u;
+    uint32_t f = h & 1023u;
+    if (e == 0) {
+        // f * 2^-24 is exact in fp32.
+        float mag = __fmul_rn((float)f, 5.9604644775390625e-08f);
+        return __uint_as_float(__float_as_uint(mag) | sign);
+    }
+    if (e == 31) return __uint_as_float(sign | 0x7F800000u | (f << 13));
+    return __uint_as_float(sign | ((e + 112u) << 23) | (f << 13));
+}
+
+__device__ __forceinline__ uint32_t rd16(const uint8_t* p) { return (uint32_t)p[0] | ((uint32_t)p[1] << 8); }
+
+// The shared 6-bit scale/min unpack of Q4_K/Q5_K (gguf_importer.cpp:856-861).
+__device__ __forceinline__ void kquant_scale_min(const uint8_t* sc, int g, int* s, int* m) {
+    if (g < 4) {
+        *s = sc[g] & 63;
+        *m = (sc[g] >> 6) | ((sc[g + 8] & 15) << 2);
+    } else {
+        *s = sc[g] & 63;
+        *m = (sc[g] >> 6) | ((sc[g + 4] >> 4) << 2);
+    }
+}
+
+// Decode 8 consecutive elements [e0, e0+8) (e0 % 8 == 0, e0 < CHUNK_K) of row r
+// of one tile-chunk into out[].  Values are bit-identical to the reference.
+__device__ inline void decode8(int type, const uint8_t* chunk, int r, int e0, float* out) {
+    const int R = TILE_ROWS;
+    switch (type) {
+        case T_Q4_0: {  // :679-695
+            const uint8_t* rec = chunk + (int64_t)r * 144;
+            int j = e0 >> 5, w = e0 & 31;
+            float d = half_bits_to_float(rd16(rec + 2 * j));
+            const uint8_t* q = rec + 16 + 16 * j;
+            for (int i = 0; i < 8; ++i) {
+                int e = w + i;
+                int c = e < 16 ? (q[e] & 15) : (q[e - 16] >> 4);
+                out[i] = __fmul_rn((float)(c - 8), d);
+            }
+            break;
+        }
+        case T_Q4_1: {  // :699-717
+            const uint8_t* rec = chunk + (int64_t)r * 160;
+            int j = e0 >> 5, w = e0 & 31;
+            float d = half_bits_to_float(rd16(rec + 4 * j));
+            float m = half_bits_to_float(rd16(rec + 4 * j + 2));
+            const uint8_t* q = rec + 32 + 16 * j;
+            for (int i = 0; i < 8; ++i) {
+                int e = w + i;
+                int c = e < 16 ? (q[e] & 15) : (q[e - 16] >> 4);
+                out[i] = __fadd_rn(__fmul_rn((float)c, d), m);
+            }
+            break;
+        }
+        case T_Q8_0: {  // :721-733
+            const uint8_t* rec = chunk + (int64_t)r * 272;
+            int j = e0 >> 5, w = e0 & 31;
+            float d = half_bits_to_float(rd16(rec + 2 * j));
+            const int8_t* q = (const int8_t*)(rec + 16 + 32 * j);
+            for (int i = 0; i < 8; ++i) out[i] = __fmul_rn((float)q[w + i], d);
+            break;
+        }
+        case T_Q2_K: {  // :756-786
+            const uint8_t* rec = chunk + (int64_t)r * 80;
+            const uint8_t* tail = chunk + (int64_t)R * 80 + r * 4;
+            float dmin = half_bits_to_float(rd16(tail));
+            float d = half_bits_to_float(rd16(tail + 2));
+            int g = e0 >> 4;
+            float s = __fmul_rn(d, (float)(rec[g] & 15));
+            float m = __fmul_rn(dmin, (float)(rec[g] >> 4));
+            for (int i = 0; i < 8; ++i) {
+                int e = e0 + i;
+                int q = (rec[16 + (e >> 2)] >> (2 * (e & 3))) & 3;
+                out[i] = __fsub_rn(__fmul_rn(s, (float)q), m);
+            }
+            break;
+        }
+        case T_Q3_K: {  // :791-833
+            const uint8_t* rec = chunk + (int64_t)r * 96;
+            const uint8_t* tail = chunk + (int64_t)R * 96 + r * 14;
+            float d = half_bits_to_float(rd16(tail + 12));
+            int g = e0 >> 4;
+            int i8 = g & 7;
+            int hi = tail[8 + i8 / 2] >> (4 * (i8 & 1));
+            int sc = g < 8 ? ((tail[i8] & 15) | ((hi & 3) << 4))
+                           : ((tail[i8] >> 4) | (((hi >> 2) & 3) << 4));
+            sc -= 32;
+            float ds = __fmul_rn(d, (float)sc);
+            for (int i = 0; i < 8; ++i) {
+                int e = e0 + i;
+                int q = ((rec[32 + (e >> 2)] >> (2 * (e & 3))) & 3) | (((rec[e >> 3] >> (e & 7)) & 1) << 2);
+                out[i] = __fmul_rn(ds, __fsub_rn((float)q, 4.0f));
+            }
+            break;
+        }
+        case T_Q4_K: {  // :838-873
+            const uint8_t* rec = chunk + (int64_t)r * 144;
+            float d = half_bits_to_float(rd16(rec));
+            float dmin = half_bits_to_float(rd16(rec + 2));
+            int s, m;
+            kquant_scale_min(rec + 4, e0 >> 5, &s, &m);
+            float ds = __fmul_rn(d, (float)s);
+            float dm = __fmul_rn(dmin, (float)m);
+            for (int i = 0; i < 8; ++i) {
+                int e = e0 + i;
+                int c = rec[16 + (e >> 1)];
+                int q = (e & 1) ? (c >> 4) : (c & 15);
+                out[i] = __fsub_rn(__fmul_rn(ds, (float)q), dm);
+            }
+            break;
+        }
+        case T_Q5_K: {  // :878-915
+            const uint8_t* rec = chunk + (int64_t)r * 176;
+            float d = half_bits_to_float(rd16(rec));
+            float dmin = half_bits_to_float(rd16(rec + 2));
+            int s, m;
+            kquant_scale_min(rec + 4, e0 >> 5, &s, &m);
+            float ds = __fmul_rn(d, (float)s);
+            float dm = __fmul_rn(dmin, (float)m);
+            for (int i = 0; i < 8; ++i) {
+                int e = e0 + i;
+                int c = rec[48 + (e >> 1)];
+                int q = ((e & 1) ? (c >> 4) : (c & 15)) | (((rec[16 + (e >> 3)] >> (e & 7)) & 1) << 4);
+                out[i] = __fsub_rn(__fmul_rn(ds, (float)q), dm);
+            }
+            break;
+        }
+        case T_Q6_K: {  // :924-954
+            const uint8_t* rec = chunk + (int64_t)r * 192;
+            const int8_t* scl = (const int8_t*)(chunk + (int64_t)R * 192 + r * 16);
+            float d = half_bits_to_float(rd16(chunk + (int64_t)R * 208 + r * 2));
+            float ds = __fmul_rn(d, (float)scl[e0 >> 4]);
+            for (int i = 0; i < 8; ++i) {
+                int e = e0 + i;
+                int lo = (e & 1) ? (rec[e >> 1] >> 4) : (rec[e >> 1] & 15);
+                int hi = (rec[128 + (e >> 2)] >> (2 * (e & 3))) & 3;
+                out[i] = __fmul_rn(ds, __fsub_rn((float)(lo | (hi << 4)), 32.0f));
+            }
+            break;
+        }
+        default:
+            for (int i = 0; i < 8; ++i) out[i] = 0.0f;
+    }
+}
+
+}  // namespace nxq

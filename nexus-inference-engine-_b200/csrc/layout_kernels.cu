@@ -1,0 +1,72 @@
+// Residency layout kernels: GGUF row-major blocks -> tiled HBM copy, and the
+// exact fp32 decode of a tiled copy (the device counterpart of
+// dequant_gguf_to_fp32, nexus/src/import/gguf_importer.cpp:958-1000).
+#include "nxq_internal.h"
+
+namespace nxq {
+
+// One thread per (row, block): copies the block's byte segments to their
+// tiled positions.  `src` holds `rows` rows of `src_row_blocks` blocks; blocks
+// [blk0, blk0 + K/QK) of each source row become row (row0 + i) of the weight.
+// (The offsets let a tensor-parallel rank take a column slice of each row.)
+__global__ void repack_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                              TiledShape s, int64_t row0, int64_t rows, int64_t blk0,
+                              int64_t src_row_blocks) {
+    const int64_t kb = s.K / s.g.qk;  // blocks per destination row
+    const int64_t total = rows * kb;
+    const int per_chunk = CHUNK_K / s.g.qk;
+    for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        int64_t i = idx / kb, b = idx % kb;
+        int64_t n = row0 + i;
+        const uint8_t* blk = src + (i * src_row_blocks + blk0 + b) * s.g.bb;
+        int64_t tile = n / TILE_ROWS, r = n % TILE_ROWS;
+        int64_t chunk = b / per_chunk, j = b % per_chunk;
+        uint8_t* base = dst + s.chunk_offset(tile, chunk);
+        Segment seg[3];
+        int ns = block_segments(s.type, (int)r, (int)j, seg);
+        for (int q = 0; q < ns; ++q)
+            for (int t = 0; t < seg[q].len; ++t) base[seg[q].dst + t] = blk[seg[q].src + t];
+    }
+}
+
+cudaError_t launch_repack(const uint8_t* src, uint8_t* dst, const TiledShape& s, int64_t row0,
+                          int64_t rows, int64_t blk0, int64_t src_row_blocks, cudaStream_t st) {
+    int64_t total = rows * (s.K / s.g.qk);
+    int64_t grid = (total + 255) / 256;
+    if (grid > 65535 * 8) grid = 65535 * 8;
+    if (grid < 1) grid = 1;
+    repack_kernel<<<(unsigned)grid, 256, 0, st>>>(src, dst, s, row0, rows, blk0, src_row_blocks);
+    note_launches(1);
+    return cudaGetLastError();
+}
+
+// One thread per 8 consecutive output elements; consecutive threads write
+// consecutive 32-byte runs of y[n][k].
+__global__ void dequant_kernel(const uint8_t* __restrict__ tiled, TiledShape s, float* __restrict__ y) {
+    const int64_t groups_per_row = s.K / 8;
+    const int64_t total = s.N * groups_per_row;
+    for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        int64_t n = idx / groups_per_row;
+        int64_t k = (idx % groups_per_row) * 8;
+        const uint8_t* chunk = tiled + s.chunk_offset(n / TILE_ROWS, k / CHUNK_K);
+        float v[8];
+        decode8(s.type, chunk, (int)(n % TILE_ROWS), (int)(k % CHUNK_K), v);
+        float4* o = reinterpret_cast<float4*>(y + n * s.K + k);
+        o[0] = make_float4(v[0], v[1], v[2], v[3]);
+        o[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
+}
+
+cudaError_t launch_dequant(const uint8_t* tiled, const TiledShape& s, float* y, cudaStream_t st) {
+    int64_t total = s.N * (s.K / 8);
+    int64_t grid = (total + 255) / 256;
+    if (grid > 65535 * 16) grid = 65535 * 16;
+    if (grid < 1) grid = 1;
+    dequant_kernel<<<(unsigned)grid, 256, 0, st>>>(tiled, s, y);
+    note_launches(1);
+    return cudaGetLastError();
+}
+
+}  // namespace nxq

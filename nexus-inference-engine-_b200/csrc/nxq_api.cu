@@ -1,0 +1,511 @@
+// The C ABI of libnxq.so (include/nxq.h): context, HBM weight residency,
+// dispatch to the kernels, and the synchronous host-buffer drop-in.
+//
+// Reference counterparts:
+//   ComputeDispatch::init_gpu / gemm_int4 / clear_buffer_cache
+//       nexus/src/compute/compute_dispatch.cpp:47, :142-176, :853-860
+//   MetalBackend::wrap_pointer / gemm_int4_gpu / buffer caches
+//       nexus/src/compute/metal/metal_backend.mm:814-834, :274-303
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <unordered_set>
+
+#include "nxq_internal.h"
+#include "qmm_tc.h"
+
+namespace nxq {
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+struct Context {
+    bool ready = false;
+    int device = -1;
+    int sm_count = 0;
+    int cc_major = 0, cc_minor = 0;
+    size_t smem_optin = 0;
+    cudaStream_t host_stream = nullptr;  // nxq_qmatmul_host and registration
+    // Device buffers of the host-buffer entry point (grown on demand).
+    void* hx = nullptr;
+    size_t hx_bytes = 0;
+    void* hy = nullptr;
+    size_t hy_bytes = 0;
+    DeviceStatus* status = nullptr;  // bounded-wait error word (device memory)
+    std::mutex mu;                   // registration, host entry point, teardown
+    std::unordered_set<Weight*> live;
+};
+
+Context g_ctx;
+std::mutex g_init_mu;
+
+int check_ready() {
+    if (!g_ctx.ready) return fail(NXQ_ERR_STATE, "nxq_init has not been called");
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != g_ctx.device) {
+        cudaError_t e = cudaSetDevice(g_ctx.device);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    }
+    return NXQ_OK;
+}
+
+int check_weight(nxq_weight_t h, Weight** out) {
+    Weight* w = reinterpret_cast<Weight*>(h);
+    if (!w) return fail(NXQ_ERR_ARG, "null weight handle");
+    std::lock_guard<std::mutex> lk(g_ctx.mu);
+    if (!g_ctx.live.count(w) || w->magic != kWeightMagic)
+        return fail(NXQ_ERR_ARG, "weight handle is not live (released or foreign)");
+    *out = w;
+    return NXQ_OK;
+}
+
+bool dtype_ok(int d) { return d == NXQ_F32 || d == NXQ_F16 || d == NXQ_BF16; }
+size_t dtype_size(int d) { return d == NXQ_F32 ? 4 : 2; }
+
+int grow(void** buf, size_t* have, size_t need) {
+    if (*have >= need) return NXQ_OK;
+    if (*buf) cudaFree(*buf);
+    *buf = nullptr;
+    *have = 0;
+    cudaError_t e = cudaMalloc(buf, need);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc (host-call buffers)");
+    *have = need;
+    return NXQ_OK;
+}
+
+// Reads the device status word after a synchronize; a nonzero code means a
+// bounded wait inside a kernel gave up.
+int check_device_status() {
+    DeviceStatus st{};
+    cudaError_t e = cudaMemcpy(&st, g_ctx.status, sizeof st, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "read device status");
+    if (st.code) {
+        cudaMemset(g_ctx.status, 0, sizeof(DeviceStatus));
+        return fail(NXQ_ERR_TIMEOUT, "device-side bounded wait expired (code %u at %u)", st.code,
+                    st.where);
+    }
+    return NXQ_OK;
+}
+
+// Registers N rows of K from GGUF blocks.  `src` is host (is_host) or device
+// memory; rows are `src_row_blocks` blocks long in the source and blocks
+// [blk0, blk0 + K/QK) of each are kept (a column slice for ROW sharding).
+int register_impl(const void* src, bool is_host, int type, int64_t N, int64_t K,
+                  int64_t src_row_blocks, int64_t blk0, cudaStream_t st, nxq_weight_t* out) {
+    TiledShape s;
+    if (!make_tiled_shape(type, N, K, &s)) {
+        Geometry g;
+        if (!geometry_of(type, &g)) return fail(NXQ_ERR_CODEC, "unsupported block type %d", type);
+        return fail(NXQ_ERR_SHAPE, "bad shape N=%lld K=%lld for block of %d elements",
+                    (long long)N, (long long)K, g.qk);
+    }
+    Weight* w = new (std::nothrow) Weight();
+    if (!w) return fail(NXQ_ERR_NOMEM, "host allocation failed");
+    w->magic = kWeightMagic;
+    w->device = g_ctx.device;
+    w->shape = s;
+    w->packed_bytes = (size_t)N * (size_t)(K / s.g.qk) * (size_t)s.g.bb;
+    w->dev_bytes = (size_t)s.total_bytes() + kTailPad;
+    cudaError_t e = cudaMalloc(&w->dev, w->dev_bytes);
+    if (e != cudaSuccess) {
+        delete w;
+        return cuda_fail(e, "cudaMalloc (weight)");
+    }
+    auto bail = [&](int status) {
+        cudaFree(w->dev);
+        delete w;
+        return status;
+    };
+    if ((e = cudaMemsetAsync(w->dev, 0, w->dev_bytes, st)) != cudaSuccess)
+        return bail(cuda_fail(e, "cudaMemsetAsync (weight)"));
+
+    const size_t slice_bytes = (size_t)(K / s.g.qk) * s.g.bb;
+    const size_t src_pitch = (size_t)src_row_blocks * s.g.bb;
+    if (!is_host) {
+        // Device source: repack straight from it.
+        e = launch_repack((const uint8_t*)src, w->dev, s, 0, N, blk0, src_row_blocks, st);
+        if (e != cudaSuccess) return bail(cuda_fail(e, "repack launch"));
+    } else {
+        // Host source: stage up to ~256 MB of rows at a time.
+        int64_t rows_per = (int64_t)((256u << 20) / slice_bytes);
+        if (rows_per < 1) rows_per = 1;
+        if (rows_per > N) rows_per = N;
+        uint8_t* stage = nullptr;
+        if ((e = cudaMalloc(&stage, (size_t)rows_per * slice_bytes)) != cudaSuccess)
+            return bail(cuda_fail(e, "cudaMalloc (staging)"));
+        for (int64_t r0 = 0; r0 < N && e == cudaSuccess; r0 += rows_per) {
+            int64_t nr = N - r0 < rows_per ? N - r0 : rows_per;
+            const uint8_t* hsrc = (const uint8_t*)src + (size_t)r0 * src_pitch + (size_t)blk0 * s.g.bb;
+            e = cudaMemcpy2DAsync(stage, slice_bytes, hsrc, src_pitch, slice_bytes, (size_t)nr,
+                                  cudaMemcpyHostToDevice, st);
+            if (e == cudaSuccess)
+                e = launch_repack(stage, w->dev, s, r0, nr, 0, K / s.g.qk, st);
+            // The staging buffer is reused: finish this pass before the next copy.
+            if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        }
+        cudaFree(stage);
+        if (e != cudaSuccess) return bail(cuda_fail(e, "weight upload/repack"));
+    }
+    if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return bail(cuda_fail(e, "weight registration"));
+    {
+        std::lock_guard<std::mutex> lk(g_ctx.mu);
+        g_ctx.live.insert(w);
+    }
+    *out = reinterpret_cast<nxq_weight_t>(w);
+    return NXQ_OK;
+}
+
+}  // namespace
+
+int fail(int status, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+    return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(NXQ_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+namespace {
+std::atomic<uint64_t> g_launches{0};
+}
+
+void note_launches(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+const char* type_name(int type) {
+    switch (type) {
+        case T_Q4_0: return "Q4_0";
+        case T_Q4_1: return "Q4_1";
+        case T_Q8_0: return "Q8_0";
+        case T_Q2_K: return "Q2_K";
+        case T_Q3_K: return "Q3_K";
+        case T_Q4_K: return "Q4_K";
+        case T_Q5_K: return "Q5_K";
+        case T_Q6_K: return "Q6_K";
+        default: return "?";
+    }
+}
+
+int context_sm_count() { return g_ctx.sm_count; }
+DeviceStatus* context_status() { return g_ctx.status; }
+
+// Runs y = x W^T on `st` through the best kernel for (type, M, dtypes).
+int qmatmul_dispatch(const Weight* w, const void* x, int x_dtype, void* y, int y_dtype, int64_t M,
+                     cudaStream_t st) {
+    const TiledShape& s = w->shape;
+    if (M == 0) return NXQ_OK;
+    if (tc_supported(s, M, x_dtype, y_dtype)) {
+        int rc = tc_qmatmul(w, x, x_dtype, y, y_dtype, M, st);
+        if (rc != NXQ_ERR_UNSUPPORTED) return rc;
+    }
+    int splits = simt_pick_splits(s, M, g_ctx.sm_count);
+    float* partials = nullptr;
+    cudaError_t e;
+    if (splits > 1) {
+        e = cudaMallocAsync((void**)&partials, (size_t)splits * M * s.N * sizeof(float), st);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync (split partials)");
+    }
+    e = launch_qmm_simt(w->dev, s, x, x_dtype, y, y_dtype, M, partials, splits, st);
+    if (partials) cudaFreeAsync(partials, st);
+    if (e != cudaSuccess) return cuda_fail(e, "qmm_simt launch");
+    return NXQ_OK;
+}
+
+}  // namespace nxq
+
+using namespace nxq;
+
+extern "C" {
+
+NXQ_API int nxq_abi_version(void) { return NXQ_ABI_VERSION; }
+
+NXQ_API int nxq_last_error(char* buf, size_t n) {
+    if (!buf || n == 0) return NXQ_ERR_ARG;
+    snprintf(buf, n, "%s", g_err);
+    return NXQ_OK;
+}
+
+NXQ_API int nxq_block_geometry(int type, int* block_elems, int* block_bytes) {
+    Geometry g;
+    if (!geometry_of(type, &g)) return fail(NXQ_ERR_CODEC, "unsupported block type %d", type);
+    if (block_elems) *block_elems = g.qk;
+    if (block_bytes) *block_bytes = g.bb;
+    return NXQ_OK;
+}
+
+NXQ_API int nxq_init(int device) {
+    std::lock_guard<std::mutex> lk(g_init_mu);
+    if (g_ctx.ready) {
+        if (device == g_ctx.device) return NXQ_OK;
+        return fail(NXQ_ERR_STATE, "nxq already initialised on device %d", g_ctx.device);
+    }
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || count == 0)
+        return fail(NXQ_ERR_UNSUPPORTED, "no CUDA device available (%s)",
+                    e == cudaSuccess ? "0 devices" : cudaGetErrorString(e));
+    if (device < 0 || device >= count) return fail(NXQ_ERR_ARG, "device %d out of range", device);
+    NXQ_CUDA(cudaSetDevice(device));
+    cudaDeviceProp p;
+    NXQ_CUDA(cudaGetDeviceProperties(&p, device));
+    if (p.major != 10)
+        return fail(NXQ_ERR_UNSUPPORTED, "device %d is sm_%d%d; libnxq is built for sm_100a only",
+                    device, p.major, p.minor);
+    g_ctx.device = device;
+    g_ctx.sm_count = p.multiProcessorCount;
+    g_ctx.cc_major = p.major;
+    g_ctx.cc_minor = p.minor;
+    g_ctx.smem_optin = p.sharedMemPerBlockOptin;
+    NXQ_CUDA(cudaStreamCreateWithFlags(&g_ctx.host_stream, cudaStreamNonBlocking));
+    NXQ_CUDA(cudaMalloc(&g_ctx.status, sizeof(DeviceStatus)));
+    NXQ_CUDA(cudaMemset(g_ctx.status, 0, sizeof(DeviceStatus)));
+    // Keep stream-ordered scratch in the pool between calls instead of
+    // returning it to the driver after every synchronize.
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
+        uint64_t keep = 1ull << 30;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    }
+    int rc = tc_init(device);
+    if (rc != NXQ_OK) return rc;
+    g_ctx.ready = true;
+    return NXQ_OK;
+}
+
+NXQ_API int nxq_shutdown(void) {
+    std::lock_guard<std::mutex> lk(g_init_mu);
+    if (!g_ctx.ready) return NXQ_OK;
+    cudaSetDevice(g_ctx.device);
+    cudaDeviceSynchronize();
+    {
+        std::lock_guard<std::mutex> lk2(g_ctx.mu);
+        for (Weight* w : g_ctx.live) {
+            w->magic = 0;
+            cudaFree(w->dev);
+            delete w;
+        }
+        g_ctx.live.clear();
+    }
+    if (g_ctx.hx) cudaFree(g_ctx.hx);
+    if (g_ctx.hy) cudaFree(g_ctx.hy);
+    g_ctx.hx = g_ctx.hy = nullptr;
+    g_ctx.hx_bytes = g_ctx.hy_bytes = 0;
+    if (g_ctx.status) cudaFree(g_ctx.status);
+    g_ctx.status = nullptr;
+    if (g_ctx.host_stream) cudaStreamDestroy(g_ctx.host_stream);
+    g_ctx.host_stream = nullptr;
+    g_ctx.ready = false;
+    g_ctx.device = -1;
+    return NXQ_OK;
+}
+
+NXQ_API int nxq_weight_register(const void* host_blocks, size_t bytes, int type, int64_t N,
+                                int64_t K, nxq_weight_t* out) {
+    if (!host_blocks || !out) return fail(NXQ_ERR_ARG, "null argument");
+    int rc = check_ready();
+    if (rc) return rc;
+    Geometry g;
+    if (!geometry_of(type, &g)) return fail(NXQ_ERR_CODEC, "unsupported block type %d", type);
+    if (N <= 0 || K <= 0 || K % g.qk)
+        return fail(NXQ_ERR_SHAPE, "bad shape N=%lld K=%lld (K must be a positive multiple of %d)",
+                    (long long)N, (long long)K, g.qk);
+    if (bytes != (size_t)N * (size_t)(K / g.qk) * (size_t)g.bb)
+        return fail(NXQ_ERR_SHAPE, "bytes=%zu but N*(K/%d)*%d = %zu", bytes, g.qk, g.bb,
+                    (size_t)N * (size_t)(K / g.qk) * (size_t)g.bb);
+    std::lock_guard<std::mutex> lk(g_init_mu);
+    return register_impl(host_blocks, true, type, N, K, K / g.qk, 0, g_ctx.host_stream, out);
+}
+
+NXQ_API int nxq_weight_register_device(const void* dev_blocks, size_t bytes, int type, int64_t N,
+                                       int64_t K, void* stream, nxq_weight_t* out) {
+    if (!dev_blocks || !out) return fail(NXQ_ERR_ARG, "null argument");
+    int rc = check_ready();
+    if (rc) return rc;
+    Geometry g;
+    if (!geometry_of(type, &g)) return fail(NXQ_ERR_CODEC, "unsupported block type %d", type);
+    if (N <= 0 || K <= 0 || K % g.qk)
+        return fail(NXQ_ERR_SHAPE, "bad shape N=%lld K=%lld", (long long)N, (long long)K);
+    if (bytes != (size_t)N * (size_t)(K / g.qk) * (size_t)g.bb)
+        return fail(NXQ_ERR_SHAPE, "bytes=%zu does not match N*(K/QK)*block_bytes", bytes);
+    std::lock_guard<std::mutex> lk(g_init_mu);
+    return register_impl(dev_blocks, false, type, N, K, K / g.qk, 0, (cudaStream_t)stream, out);
+}
+
+// Validates a TP shard request; fills the slice geometry.
+static int shard_geometry(size_t bytes, int type, int64_t N, int64_t K, int split, int rank,
+                          int world, Geometry* g, int64_t* n_loc, int64_t* k_loc) {
+    if (!geometry_of(type, g)) return fail(NXQ_ERR_CODEC, "unsupported block type %d", type);
+    if (world < 1 || rank < 0 || rank >= world) return fail(NXQ_ERR_ARG, "rank %d of %d", rank, world);
+    if (N <= 0 || K <= 0 || K % g->qk) return fail(NXQ_ERR_SHAPE, "bad shape");
+    if (bytes != (size_t)N * (size_t)(K / g->qk) * (size_t)g->bb)
+        return fail(NXQ_ERR_SHAPE, "bytes does not match N*(K/QK)*block_bytes");
+    if (split == NXQ_SPLIT_COL) {
+        if (N % world) return fail(NXQ_ERR_SHAPE, "N=%lld not divisible by %d", (long long)N, world);
+        *n_loc = N / world;
+        *k_loc = K;
+        return NXQ_OK;
+    }
+    if (split == NXQ_SPLIT_ROW) {
+        if (K % world || (K / world) % g->qk)
+            return fail(NXQ_ERR_SHAPE, "K=%lld / %d is not a multiple of the %d-element block",
+                        (long long)K, world, g->qk);
+        *n_loc = N;
+        *k_loc = K / world;
+        return NXQ_OK;
+    }
+    return fail(NXQ_ERR_ARG, "split must be NXQ_SPLIT_COL or NXQ_SPLIT_ROW");
+}
+
+NXQ_API int nxq_shard_extract(const void* host_blocks, size_t bytes, int type, int64_t N,
+                              int64_t K, int split, int rank, int world, void* out,
+                              size_t out_bytes) {
+    if (!host_blocks || !out) return fail(NXQ_ERR_ARG, "null argument");
+    Geometry g;
+    int64_t n_loc = 0, k_loc = 0;
+    int rc = shard_geometry(bytes, type, N, K, split, rank, world, &g, &n_loc, &k_loc);
+    if (rc) return rc;
+    const size_t row_bytes = (size_t)(K / g.qk) * g.bb;
+    const size_t slice = (size_t)(k_loc / g.qk) * g.bb;
+    if (out_bytes != (size_t)n_loc * slice)
+        return fail(NXQ_ERR_SHAPE, "out_bytes=%zu, shard needs %zu", out_bytes, (size_t)n_loc * slice);
+    const uint8_t* src = (const uint8_t*)host_blocks;
+    uint8_t* dst = (uint8_t*)out;
+    if (split == NXQ_SPLIT_COL) {
+        memcpy(dst, src + (size_t)rank * n_loc * row_bytes, (size_t)n_loc * row_bytes);
+    } else {
+        for (int64_t n = 0; n < N; ++n)
+            memcpy(dst + (size_t)n * slice, src + (size_t)n * row_bytes + (size_t)rank * slice, slice);
+    }
+    return NXQ_OK;
+}
+
+NXQ_API int nxq_weight_register_shard(const void* host_blocks, size_t bytes, int type, int64_t N,
+                                      int64_t K, int split, int rank, int world,
+                                      nxq_weight_t* out) {
+    if (!host_blocks || !out) return fail(NXQ_ERR_ARG, "null argument");
+    int rc = check_ready();
+    if (rc) return rc;
+    Geometry g;
+    int64_t n_loc = 0, k_loc = 0;
+    if ((rc = shard_geometry(bytes, type, N, K, split, rank, world, &g, &n_loc, &k_loc))) return rc;
+    const int64_t row_blocks = K / g.qk;
+    std::lock_guard<std::mutex> lk(g_init_mu);
+    if (split == NXQ_SPLIT_COL) {
+        const uint8_t* src = (const uint8_t*)host_blocks + (size_t)rank * n_loc * row_blocks * g.bb;
+        return register_impl(src, true, type, n_loc, K, row_blocks, 0, g_ctx.host_stream, out);
+    }
+    return register_impl(host_blocks, true, type, N, k_loc, row_blocks, rank * (k_loc / g.qk),
+                         g_ctx.host_stream, out);
+}
+
+NXQ_API int nxq_weight_release(nxq_weight_t h) {
+    Weight* w = nullptr;
+    int rc = check_weight(h, &w);
+    if (rc) return rc;
+    rc = check_ready();
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(g_ctx.mu);
+    g_ctx.live.erase(w);
+    w->magic = 0;
+    // Work queued on other streams may still read the weight.
+    cudaDeviceSynchronize();
+    cudaFree(w->dev);
+    delete w;
+    return NXQ_OK;
+}
+
+NXQ_API int nxq_weight_info(nxq_weight_t h, int* type, int64_t* N, int64_t* K, size_t* packed_bytes,
+                            size_t* device_bytes) {
+    Weight* w = nullptr;
+    int rc = check_weight(h, &w);
+    if (rc) return rc;
+    if (type) *type = w->shape.type;
+    if (N) *N = w->shape.N;
+    if (K) *K = w->shape.K;
+    if (packed_bytes) *packed_bytes = w->packed_bytes;
+    if (device_bytes) *device_bytes = w->dev_bytes;
+    return NXQ_OK;
+}
+
+NXQ_API int nxq_dequant(nxq_weight_t h, float* y_dev, void* stream) {
+    Weight* w = nullptr;
+    int rc = check_weight(h, &w);
+    if (rc) return rc;
+    if (!y_dev) return fail(NXQ_ERR_ARG, "null output");
+    if ((uintptr_t)y_dev % 16) return fail(NXQ_ERR_ARG, "output must be 16-byte aligned");
+    if ((rc = check_ready())) return rc;
+    cudaError_t e = launch_dequant(w->dev, w->shape, y_dev, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "dequant launch");
+    return NXQ_OK;
+}
+
+NXQ_API int nxq_qmatmul(nxq_weight_t h, const void* x_dev, int x_dtype, void* y_dev, int y_dtype,
+                        int64_t M, void* stream) {
+    Weight* w = nullptr;
+    int rc = check_weight(h, &w);
+    if (rc) return rc;
+    if (M < 0) return fail(NXQ_ERR_ARG, "M=%lld", (long long)M);
+    if (M > 0 && (!x_dev || !y_dev)) return fail(NXQ_ERR_ARG, "null activation or output");
+    if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return fail(NXQ_ERR_ARG, "bad dtype");
+    if ((rc = check_ready())) return rc;
+    return qmatmul_dispatch(w, x_dev, x_dtype, y_dev, y_dtype, M, (cudaStream_t)stream);
+}
+
+NXQ_API int nxq_qmatmul_host(nxq_weight_t h, const float* x_host, float* y_host, int64_t M) {
+    Weight* w = nullptr;
+    int rc = check_weight(h, &w);
+    if (rc) return rc;
+    if (M < 0) return fail(NXQ_ERR_ARG, "M=%lld", (long long)M);
+    if (M == 0) return NXQ_OK;
+    if (!x_host || !y_host) return fail(NXQ_ERR_ARG, "null activation or output");
+    if ((rc = check_ready())) return rc;
+    std::lock_guard<std::mutex> lk(g_init_mu);
+    const size_t xb = (size_t)M * w->shape.K * sizeof(float);
+    const size_t yb = (size_t)M * w->shape.N * sizeof(float);
+    if ((rc = grow(&g_ctx.hx, &g_ctx.hx_bytes, xb))) return rc;
+    if ((rc = grow(&g_ctx.hy, &g_ctx.hy_bytes, yb))) return rc;
+    cudaStream_t st = g_ctx.host_stream;
+    NXQ_CUDA(cudaMemcpyAsync(g_ctx.hx, x_host, xb, cudaMemcpyHostToDevice, st));
+    rc = qmatmul_dispatch(w, g_ctx.hx, NXQ_F32, g_ctx.hy, NXQ_F32, M, st);
+    if (rc) return rc;
+    NXQ_CUDA(cudaMemcpyAsync(y_host, g_ctx.hy, yb, cudaMemcpyDeviceToHost, st));
+    NXQ_CUDA(cudaStreamSynchronize(st));
+    return check_device_status();
+}
+
+NXQ_API int nxq_qmatmul_kernel_name(nxq_weight_t h, int64_t M, int x_dtype, int y_dtype, char* buf,
+                                    size_t n) {
+    Weight* w = nullptr;
+    int rc = check_weight(h, &w);
+    if (rc) return rc;
+    if (!buf || n == 0) return fail(NXQ_ERR_ARG, "null buffer");
+    if (M < 1 || !dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return fail(NXQ_ERR_ARG, "bad M or dtype");
+    if (tc_supported(w->shape, M, x_dtype, y_dtype)) {
+        tc_kernel_name(w->shape, M, buf, n);
+        return NXQ_OK;
+    }
+    snprintf(buf, n, "simt<%s,mb%d>", type_name(w->shape.type), simt_rows_per_pass(M));
+    return NXQ_OK;
+}
+
+NXQ_API int nxq_launch_count(uint64_t* out) {
+    if (!out) return fail(NXQ_ERR_ARG, "null argument");
+    *out = g_launches.load(std::memory_order_relaxed);
+    return NXQ_OK;
+}
+
+NXQ_API int nxq_stream_sync(void* stream) {
+    int rc = check_ready();
+    if (rc) return rc;
+    NXQ_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+    return check_device_status();
+}
+
+}  // extern "C"

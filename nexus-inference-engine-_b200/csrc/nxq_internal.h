@@ -1,0 +1,62 @@
+// Internal declarations shared by the C-ABI layer and the kernel files.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/nxq.h"
+#include "formats.cuh"
+
+namespace nxq {
+
+// A registered, HBM-resident weight (the nxq_weight_t handle).
+struct Weight {
+    uint32_t magic;       // kWeightMagic while live; guards stale handles
+    int device;
+    TiledShape shape;
+    uint8_t* dev = nullptr;   // tiled copy (shape.total_bytes() + kTailPad)
+    size_t dev_bytes = 0;
+    size_t packed_bytes = 0;  // N * K/QK * block_bytes (the algorithmic bytes)
+};
+constexpr uint32_t kWeightMagic = 0x4E58514Bu;  // "NXQK"
+constexpr size_t kTailPad = 256;                 // slack after the last tile-chunk
+
+// Records `msg` as the calling thread's last error and returns `status`.
+int fail(int status, const char* fmt, ...);
+// Maps a CUDA error to NXQ_ERR_CUDA with the call site in the message.
+int cuda_fail(cudaError_t e, const char* what);
+
+#define NXQ_CUDA(call)                                          \
+    do {                                                        \
+        cudaError_t e_ = (call);                                \
+        if (e_ != cudaSuccess) return ::nxq::cuda_fail(e_, #call); \
+    } while (0)
+
+// Device-side error word every bounded wait reports into (see tc kernels):
+// 0 = ok; nonzero = code of the wait that ran out.  Lives in the context.
+struct DeviceStatus {
+    unsigned int code;
+    unsigned int where;
+};
+
+// Process-wide count of kernels launched by the library (nxq_launch_count).
+void note_launches(unsigned n);
+
+// ---- kernel launchers (return cudaError_t of the launch) -------------------
+cudaError_t launch_repack(const uint8_t* src, uint8_t* dst, const TiledShape& s,
+                          int64_t row0, int64_t rows, int64_t blk0, int64_t src_row_blocks,
+                          cudaStream_t st);
+cudaError_t launch_dequant(const uint8_t* tiled, const TiledShape& s, float* y, cudaStream_t st);
+
+// CUDA-core fused dequant-GEMV/GEMM with exact fp32 decode; any M (chunked by 32).
+// `partials` must hold splits * M * N floats when splits > 1.
+cudaError_t launch_qmm_simt(const uint8_t* tiled, const TiledShape& s, const void* x, int x_dtype,
+                            void* y, int y_dtype, int64_t M, float* partials, int splits,
+                            cudaStream_t st);
+int simt_pick_splits(const TiledShape& s, int64_t M, int sm_count);
+int simt_rows_per_pass(int64_t M);
+const char* type_name(int type);
+
+}  // namespace nxq

@@ -1,0 +1,152 @@
+// Tensor parallelism over NCCL (NVLink 5 / NVSwitch): the north-star split of
+// one projection across the GPUs of a box.  The reference runs on one device
+// only and has no counterpart; the split rules are
+//   COL (QKV, gate, up):  rank r owns output rows [r*N/T, (r+1)*N/T); no exchange.
+//   ROW (O, down):        rank r owns reduction columns [r*K/T, (r+1)*K/T);
+//                         the fp32 partial outputs are summed by ncclAllReduce.
+//
+// NCCL is resolved at run time (dlopen of libnccl.so.2, preferring the copy
+// already loaded into the process, e.g. by torch.distributed), so libnxq.so
+// has no link-time NCCL dependency and the single-GPU entry points work
+// without it.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "qmm_tc.h"
+
+namespace nxq {
+int qmatmul_dispatch(const Weight* w, const void* x, int x_dtype, void* y, int y_dtype, int64_t M,
+                     cudaStream_t st);
+}
+
+using namespace nxq;
+
+namespace {
+
+struct NcclApi {
+    void* lib = nullptr;
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+NcclApi g_nccl;
+std::mutex g_tp_mu;
+ncclComm_t g_comm = nullptr;
+int g_rank = -1, g_world = 0;
+
+int load_nccl() {
+    if (g_nccl.lib) return NXQ_OK;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return fail(NXQ_ERR_NCCL, "cannot load libnccl.so.2: %s", dlerror());
+#define NXQ_SYM(field, name)                                                          \
+    g_nccl.field = reinterpret_cast<decltype(g_nccl.field)>(dlsym(h, name));          \
+    if (!g_nccl.field) return fail(NXQ_ERR_NCCL, "libnccl is missing %s", name);
+    NXQ_SYM(GetUniqueId, "ncclGetUniqueId")
+    NXQ_SYM(CommInitRank, "ncclCommInitRank")
+    NXQ_SYM(CommDestroy, "ncclCommDestroy")
+    NXQ_SYM(CommAbort, "ncclCommAbort")
+    NXQ_SYM(CommGetAsyncError, "ncclCommGetAsyncError")
+    NXQ_SYM(AllReduce, "ncclAllReduce")
+    NXQ_SYM(GetErrorString, "ncclGetErrorString")
+#undef NXQ_SYM
+    g_nccl.lib = h;
+    return NXQ_OK;
+}
+
+int nccl_fail(ncclResult_t r, const char* what) {
+    return fail(NXQ_ERR_NCCL, "%s: %s", what, g_nccl.GetErrorString ? g_nccl.GetErrorString(r) : "?");
+}
+
+int check_weight_ptr(nxq_weight_t h, const Weight** out) {
+    size_t bytes = 0;
+    int rc = nxq_weight_info(h, nullptr, nullptr, nullptr, nullptr, &bytes);
+    if (rc) return rc;
+    *out = reinterpret_cast<const Weight*>(h);
+    return NXQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+NXQ_API int nxq_tp_unique_id_size(void) { return (int)sizeof(ncclUniqueId); }
+
+NXQ_API int nxq_tp_unique_id(void* out, size_t n) {
+    if (!out || n < sizeof(ncclUniqueId)) return fail(NXQ_ERR_ARG, "buffer smaller than %zu", sizeof(ncclUniqueId));
+    int rc = load_nccl();
+    if (rc) return rc;
+    ncclUniqueId id;
+    ncclResult_t r = g_nccl.GetUniqueId(&id);
+    if (r != ncclSuccess) return nccl_fail(r, "ncclGetUniqueId");
+    memcpy(out, &id, sizeof id);
+    return NXQ_OK;
+}
+
+NXQ_API int nxq_tp_init(int rank, int world, const void* unique_id, size_t n) {
+    if (!unique_id || n < sizeof(ncclUniqueId)) return fail(NXQ_ERR_ARG, "bad unique id");
+    if (world < 1 || rank < 0 || rank >= world) return fail(NXQ_ERR_ARG, "rank %d of %d", rank, world);
+    std::lock_guard<std::mutex> lk(g_tp_mu);
+    if (g_comm) return fail(NXQ_ERR_STATE, "TP group already initialised");
+    int rc = load_nccl();
+    if (rc) return rc;
+    ncclUniqueId id;
+    memcpy(&id, unique_id, sizeof id);
+    ncclResult_t r = g_nccl.CommInitRank(&g_comm, world, id, rank);
+    if (r != ncclSuccess) {
+        g_comm = nullptr;
+        return nccl_fail(r, "ncclCommInitRank");
+    }
+    g_rank = rank;
+    g_world = world;
+    return NXQ_OK;
+}
+
+NXQ_API int nxq_tp_shutdown(void) {
+    std::lock_guard<std::mutex> lk(g_tp_mu);
+    if (!g_comm) return NXQ_OK;
+    ncclResult_t async_err = ncclSuccess;
+    g_nccl.CommGetAsyncError(g_comm, &async_err);
+    // A communicator with a pending error cannot be destroyed cleanly.
+    ncclResult_t r = async_err == ncclSuccess ? g_nccl.CommDestroy(g_comm) : g_nccl.CommAbort(g_comm);
+    g_comm = nullptr;
+    g_rank = -1;
+    g_world = 0;
+    if (r != ncclSuccess) return nccl_fail(r, "ncclCommDestroy");
+    return NXQ_OK;
+}
+
+NXQ_API int nxq_tp_allreduce_f32(float* buf_dev, int64_t count, void* stream) {
+    if (!buf_dev || count < 0) return fail(NXQ_ERR_ARG, "bad buffer");
+    if (!g_comm) return fail(NXQ_ERR_STATE, "nxq_tp_init has not been called");
+    ncclResult_t r = g_nccl.AllReduce(buf_dev, buf_dev, (size_t)count, ncclFloat32, ncclSum, g_comm,
+                                      (cudaStream_t)stream);
+    if (r != ncclSuccess) return nccl_fail(r, "ncclAllReduce");
+    return NXQ_OK;
+}
+
+NXQ_API int nxq_tp_qmatmul(nxq_weight_t shard, const void* x_dev, int x_dtype, void* y_dev,
+                           int y_dtype, int64_t M, int split, void* stream) {
+    const Weight* w = nullptr;
+    int rc = check_weight_ptr(shard, &w);
+    if (rc) return rc;
+    if (split != NXQ_SPLIT_COL && split != NXQ_SPLIT_ROW) return fail(NXQ_ERR_ARG, "bad split");
+    if (!g_comm) return fail(NXQ_ERR_STATE, "nxq_tp_init has not been called");
+    if (split == NXQ_SPLIT_ROW && y_dtype != NXQ_F32)
+        return fail(NXQ_ERR_ARG, "ROW split produces fp32 partial sums; y_dtype must be NXQ_F32");
+    rc = nxq_qmatmul(shard, x_dev, x_dtype, y_dev, y_dtype, M, stream);
+    if (rc || split == NXQ_SPLIT_COL) return rc;
+    return nxq_tp_allreduce_f32((float*)y_dev, M * w->shape.N, stream);
+}
+
+}  // extern "C"

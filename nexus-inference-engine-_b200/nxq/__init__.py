@@ -1,0 +1,285 @@
+"""ctypes binding of libnxq.so, the C ABI declared in include/nxq.h.
+
+This is the Python face of the drop-in boundary for NEXUS's quantized-matmul
+operator (``ComputeDispatch::gemm_int4``, nexus/src/compute/compute_dispatch.h:59-61):
+weights are registered once and stay resident in HBM (``Weight``), activations
+and outputs are torch CUDA tensors (``qmatmul``) or host numpy arrays
+(``qmatmul_host``, the synchronous drop-in).  Every call goes through the CUDA
+library; there is no CPU path, and importing fails loudly if the library is
+missing.
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+from typing import Optional
+
+import numpy as np
+
+__all__ = [
+    "NxqError", "lib", "init", "shutdown", "Weight", "qmatmul", "qmatmul_host", "stream_sync",
+    "kernel_name", "launch_count",
+    "TYPES", "GEOMETRY", "F32", "F16", "BF16", "SPLIT_COL", "SPLIT_ROW", "declared_symbols",
+    "tp_unique_id", "tp_init", "tp_shutdown", "tp_qmatmul", "tp_allreduce_f32",
+]
+
+LIB_PATH = Path(__file__).with_name("libnxq.so")
+HEADER = Path(__file__).resolve().parents[2] / "include" / "nxq.h"
+
+# GGUF type ids (nexus/src/import/gguf_importer.h:28-57) and block geometry
+# (elements per block, bytes per block; gguf_importer.cpp:679-954).
+TYPES = {"Q4_0": 2, "Q4_1": 3, "Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14}
+GEOMETRY = {2: (32, 18), 3: (32, 20), 8: (32, 34), 10: (256, 84), 11: (256, 110), 12: (256, 144),
+            13: (256, 176), 14: (256, 210)}
+F32, F16, BF16 = 0, 1, 2
+SPLIT_COL, SPLIT_ROW = 0, 1
+
+STATUS = {0: "OK", -1: "ERR_ARG", -2: "ERR_CODEC", -3: "ERR_SHAPE", -4: "ERR_CUDA",
+          -5: "ERR_TIMEOUT", -6: "ERR_NOMEM", -7: "ERR_STATE", -8: "ERR_NCCL", -9: "ERR_UNSUPPORTED"}
+
+
+class NxqError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"nxq {STATUS.get(code, code)}: {message}")
+        self.code = code
+        self.name = STATUS.get(code, str(code))
+
+
+_lib: Optional[ctypes.CDLL] = None
+
+_c = ctypes
+_SIGS = {
+    "nxq_init": [_c.c_int],
+    "nxq_shutdown": [],
+    "nxq_last_error": [_c.c_char_p, _c.c_size_t],
+    "nxq_abi_version": [],
+    "nxq_block_geometry": [_c.c_int, _c.POINTER(_c.c_int), _c.POINTER(_c.c_int)],
+    "nxq_weight_register": [_c.c_void_p, _c.c_size_t, _c.c_int, _c.c_int64, _c.c_int64,
+                            _c.POINTER(_c.c_void_p)],
+    "nxq_weight_register_device": [_c.c_void_p, _c.c_size_t, _c.c_int, _c.c_int64, _c.c_int64,
+                                   _c.c_void_p, _c.POINTER(_c.c_void_p)],
+    "nxq_weight_register_shard": [_c.c_void_p, _c.c_size_t, _c.c_int, _c.c_int64, _c.c_int64,
+                                  _c.c_int, _c.c_int, _c.c_int, _c.POINTER(_c.c_void_p)],
+    "nxq_shard_extract": [_c.c_void_p, _c.c_size_t, _c.c_int, _c.c_int64, _c.c_int64, _c.c_int,
+                          _c.c_int, _c.c_int, _c.c_void_p, _c.c_size_t],
+    "nxq_weight_release": [_c.c_void_p],
+    "nxq_weight_info": [_c.c_void_p, _c.POINTER(_c.c_int), _c.POINTER(_c.c_int64),
+                        _c.POINTER(_c.c_int64), _c.POINTER(_c.c_size_t), _c.POINTER(_c.c_size_t)],
+    "nxq_dequant": [_c.c_void_p, _c.c_void_p, _c.c_void_p],
+    "nxq_qmatmul": [_c.c_void_p, _c.c_void_p, _c.c_int, _c.c_void_p, _c.c_int, _c.c_int64,
+                    _c.c_void_p],
+    "nxq_qmatmul_host": [_c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int64],
+    "nxq_stream_sync": [_c.c_void_p],
+    "nxq_qmatmul_kernel_name": [_c.c_void_p, _c.c_int64, _c.c_int, _c.c_int, _c.c_char_p, _c.c_size_t],
+    "nxq_launch_count": [_c.POINTER(_c.c_uint64)],
+    "nxq_tp_unique_id_size": [],
+    "nxq_tp_unique_id": [_c.c_void_p, _c.c_size_t],
+    "nxq_tp_init": [_c.c_int, _c.c_int, _c.c_void_p, _c.c_size_t],
+    "nxq_tp_shutdown": [],
+    "nxq_tp_qmatmul": [_c.c_void_p, _c.c_void_p, _c.c_int, _c.c_void_p, _c.c_int, _c.c_int64,
+                       _c.c_int, _c.c_void_p],
+    "nxq_tp_allreduce_f32": [_c.c_void_p, _c.c_int64, _c.c_void_p],
+}
+
+
+def lib() -> ctypes.CDLL:
+    """Load libnxq.so (built by nexus-inference-engine-_b200/build.py)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(f"{LIB_PATH} is missing: run `python nexus-inference-engine-_b200/build.py`")
+        L = ctypes.CDLL(str(LIB_PATH))
+        missing = [s for s in declared_symbols() if s not in _SIGS]
+        if missing:
+            raise ImportError(f"binding lacks signatures for {missing}")
+        for name, args in _SIGS.items():
+            f = getattr(L, name)
+            f.argtypes = args
+            f.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def declared_symbols() -> list[str]:
+    """Entry points declared in include/nxq.h (NXQ_API functions)."""
+    text = HEADER.read_text()
+    return re.findall(r"NXQ_API\s+int\s+(nxq_\w+)\s*\(", text)
+
+
+def last_error() -> str:
+    buf = ctypes.create_string_buffer(512)
+    lib().nxq_last_error(buf, 512)
+    return buf.value.decode(errors="replace")
+
+
+def _check(rc: int) -> None:
+    if rc != 0:
+        raise NxqError(rc, last_error())
+
+
+def init(device: int = 0) -> None:
+    _check(lib().nxq_init(device))
+
+
+def shutdown() -> None:
+    _check(lib().nxq_shutdown())
+
+
+def _stream_ptr(stream) -> ctypes.c_void_p:
+    if stream is None:
+        import torch
+
+        return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    if isinstance(stream, int):
+        return ctypes.c_void_p(stream)
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+def _dtype_code(t) -> int:
+    import torch
+
+    return {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}[t]
+
+
+class Weight:
+    """HBM-resident packed weight [N][K] of GGUF blocks of `type`."""
+
+    def __init__(self, handle: int, type_id: int, N: int, K: int):
+        self._h = ctypes.c_void_p(handle)
+        self.type = type_id
+        self.N = N
+        self.K = K
+
+    @staticmethod
+    def _type_id(type_) -> int:
+        return TYPES[type_] if isinstance(type_, str) else int(type_)
+
+    @classmethod
+    def register(cls, blocks, type_, N: int, K: int) -> "Weight":
+        t = cls._type_id(type_)
+        buf = np.ascontiguousarray(np.frombuffer(memoryview(blocks).cast("B"), dtype=np.uint8))
+        h = ctypes.c_void_p()
+        _check(lib().nxq_weight_register(buf.ctypes.data, buf.nbytes, t, N, K, ctypes.byref(h)))
+        return cls(h.value, t, N, K)
+
+    @classmethod
+    def register_device(cls, blocks_tensor, type_, N: int, K: int, stream=None) -> "Weight":
+        t = cls._type_id(type_)
+        h = ctypes.c_void_p()
+        nbytes = blocks_tensor.numel() * blocks_tensor.element_size()
+        _check(lib().nxq_weight_register_device(blocks_tensor.data_ptr(), nbytes, t, N, K,
+                                                _stream_ptr(stream), ctypes.byref(h)))
+        return cls(h.value, t, N, K)
+
+    @classmethod
+    def register_shard(cls, blocks, type_, N: int, K: int, split: int, rank: int, world: int) -> "Weight":
+        t = cls._type_id(type_)
+        buf = np.ascontiguousarray(np.frombuffer(memoryview(blocks).cast("B"), dtype=np.uint8))
+        h = ctypes.c_void_p()
+        _check(lib().nxq_weight_register_shard(buf.ctypes.data, buf.nbytes, t, N, K, split, rank,
+                                               world, ctypes.byref(h)))
+        n_loc = N // world if split == SPLIT_COL else N
+        k_loc = K // world if split == SPLIT_ROW else K
+        return cls(h.value, t, n_loc, k_loc)
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        if self._h is None or not self._h.value:
+            raise NxqError(-1, "weight already released")
+        return self._h
+
+    def info(self) -> dict:
+        t, n, k = ctypes.c_int(), ctypes.c_int64(), ctypes.c_int64()
+        pb, db = ctypes.c_size_t(), ctypes.c_size_t()
+        _check(lib().nxq_weight_info(self.handle, ctypes.byref(t), ctypes.byref(n), ctypes.byref(k),
+                                     ctypes.byref(pb), ctypes.byref(db)))
+        return {"type": t.value, "N": n.value, "K": k.value, "packed_bytes": pb.value,
+                "device_bytes": db.value}
+
+    @property
+    def packed_bytes(self) -> int:
+        return self.info()["packed_bytes"]
+
+    def dequant(self, out=None, stream=None):
+        import torch
+
+        if out is None:
+            out = torch.empty((self.N, self.K), dtype=torch.float32, device="cuda")
+        _check(lib().nxq_dequant(self.handle, out.data_ptr(), _stream_ptr(stream)))
+        return out
+
+    def release(self) -> None:
+        if self._h is not None and self._h.value:
+            _check(lib().nxq_weight_release(self._h))
+        self._h = None
+
+
+def qmatmul(w: Weight, x, out=None, out_dtype=None, stream=None):
+    """y[M][N] = x[M][K] W^T on the current (or given) stream; x is a CUDA tensor."""
+    import torch
+
+    assert x.is_cuda and x.is_contiguous() and x.shape[-1] == w.K
+    M = x.numel() // w.K
+    if out is None:
+        out = torch.empty((M, w.N), dtype=out_dtype or torch.float32, device=x.device)
+    _check(lib().nxq_qmatmul(w.handle, x.data_ptr(), _dtype_code(x.dtype), out.data_ptr(),
+                             _dtype_code(out.dtype), M, _stream_ptr(stream)))
+    return out
+
+
+def qmatmul_host(w: Weight, x: np.ndarray, out: Optional[np.ndarray] = None) -> np.ndarray:
+    """Synchronous drop-in for ComputeDispatch::gemm_int4: fp32 host arrays in and out."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M = x.size // w.K
+    if out is None:
+        out = np.empty((M, w.N), dtype=np.float32)
+    _check(lib().nxq_qmatmul_host(w.handle, x.ctypes.data, out.ctypes.data, M))
+    return out
+
+
+def stream_sync(stream=None) -> None:
+    _check(lib().nxq_stream_sync(_stream_ptr(stream)))
+
+
+def kernel_name(w: Weight, M: int, x_dtype: int = F16, y_dtype: int = F32) -> str:
+    """The kernel nxq_qmatmul launches for this weight, M and dtypes."""
+    buf = ctypes.create_string_buffer(128)
+    _check(lib().nxq_qmatmul_kernel_name(w.handle, M, x_dtype, y_dtype, buf, 128))
+    return buf.value.decode()
+
+
+def launch_count() -> int:
+    v = ctypes.c_uint64()
+    _check(lib().nxq_launch_count(ctypes.byref(v)))
+    return v.value
+
+
+# ---- tensor parallelism ------------------------------------------------------
+
+def tp_unique_id() -> bytes:
+    n = lib().nxq_tp_unique_id_size()
+    buf = ctypes.create_string_buffer(n)
+    _check(lib().nxq_tp_unique_id(buf, n))
+    return buf.raw
+
+
+def tp_init(rank: int, world: int, uid: bytes) -> None:
+    buf = ctypes.create_string_buffer(uid, len(uid))
+    _check(lib().nxq_tp_init(rank, world, buf, len(uid)))
+
+
+def tp_shutdown() -> None:
+    _check(lib().nxq_tp_shutdown())
+
+
+def tp_qmatmul(shard: Weight, x, out, split: int, stream=None):
+    M = x.numel() // shard.K
+    _check(lib().nxq_tp_qmatmul(shard.handle, x.data_ptr(), _dtype_code(x.dtype), out.data_ptr(),
+                                _dtype_code(out.dtype), M, split, _stream_ptr(stream)))
+    return out
+
+
+def tp_allreduce_f32(buf, stream=None):
+    _check(lib().nxq_tp_allreduce_f32(buf.data_ptr(), buf.numel(), _stream_ptr(stream)))
+    return buf

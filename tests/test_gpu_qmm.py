@@ -1,0 +1,156 @@
+"""GPU: the dequant-fused matmul through the C ABI against the reference CPU
+path (oracle: the reference's decoders + fp32 dot products).
+
+Tolerance: relative L2 error <= 1e-3 with fp32 accumulation (the bar the
+north star sets).  Outputs rounded to bf16 are compared with the oracle output
+rounded to bf16 under the same bar, since bf16 rounding of the output alone is
+about 1.7e-3 against fp32."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import ALL_TYPES, MAIN_TYPES, NAMES, golden
+from oracle import loader
+from nxq import synth
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def _run(nxq, w, x_np, x_dtype, y_dtype):
+    torch = _torch()
+    x = torch.from_numpy(x_np).to(x_dtype).cuda()
+    y = nxq.qmatmul(w, x, out_dtype=y_dtype)
+    torch.cuda.synchronize()
+    nxq.stream_sync()
+    return y.float().cpu().numpy()
+
+
+@pytest.mark.parametrize("t", ALL_TYPES, ids=lambda t: NAMES[t])
+def test_qmm_golden_matrix(gpu, t):
+    torch = _torch()
+    g = golden(t)
+    N, K = int(g["mat_N"]), int(g["mat_K"])
+    w = gpu.Weight.register(g["mat_blocks"], t, N, K)
+    try:
+        y = _run(gpu, w, g["mat_x"], torch.float16, torch.float32)
+        assert synth.rel_l2(y, g["mat_y"]) < TOL
+        y = gpu.qmatmul_host(w, g["mat_x"])
+        assert synth.rel_l2(y, g["mat_y"]) < TOL
+    finally:
+        w.release()
+
+
+@pytest.mark.parametrize("t", ALL_TYPES, ids=lambda t: NAMES[t])
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 7, 8, 16, 31, 32])
+def test_qmm_batch_sizes(gpu, t, M):
+    torch = _torch()
+    N, K = 384, 2048
+    blocks = synth.make_blocks(t, N, K, seed=100 + M)
+    x = synth.make_activations(M, K, seed=200 + M, dtype=np.float16).astype(np.float32)
+    want = loader.qmatmul(t, blocks, N, K, x)
+    w = gpu.Weight.register(blocks, t, N, K)
+    try:
+        assert synth.rel_l2(_run(gpu, w, x, torch.float16, torch.float32), want) < TOL
+    finally:
+        w.release()
+
+
+@pytest.mark.parametrize("t", MAIN_TYPES, ids=lambda t: NAMES[t])
+@pytest.mark.parametrize("N,K", [(1, 256), (130, 512), (1000, 768), (257, 4096)])
+def test_qmm_ragged_shapes(gpu, t, N, K):
+    torch = _torch()
+    if K % synth.GEOMETRY[t][0]:
+        pytest.skip("K not a multiple of the block")
+    blocks = synth.make_blocks(t, N, K, seed=N + K)
+    for M in (1, 5):
+        x = synth.make_activations(M, K, seed=M, dtype=np.float16).astype(np.float32)
+        want = loader.qmatmul(t, blocks, N, K, x)
+        w = gpu.Weight.register(blocks, t, N, K)
+        try:
+            assert synth.rel_l2(_run(gpu, w, x, torch.float16, torch.float32), want) < TOL
+        finally:
+            w.release()
+
+
+@pytest.mark.parametrize("x_dt,y_dt", [("f32", "f32"), ("bf16", "f32"), ("f16", "f16"),
+                                       ("f16", "bf16"), ("bf16", "bf16")])
+def test_qmm_dtypes(gpu, x_dt, y_dt):
+    torch = _torch()
+    dt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
+    t, N, K, M = 12, 512, 2048, 8
+    blocks = synth.make_blocks(t, N, K, seed=3)
+    x32 = synth.make_activations(M, K, seed=4, dtype=np.float32)
+    # The oracle sees exactly the activation values the GPU sees.
+    x_in = torch.from_numpy(x32).to(dt[x_dt]).float().numpy()
+    want = loader.qmatmul(t, blocks, N, K, x_in)
+    w = gpu.Weight.register(blocks, t, N, K)
+    try:
+        got = _run(gpu, w, x_in, dt[x_dt], dt[y_dt])
+    finally:
+        w.release()
+    want = torch.from_numpy(want).to(dt[y_dt]).float().numpy()
+    assert synth.rel_l2(got, want) < TOL
+
+
+@pytest.mark.parametrize("t,N,K,M", [
+    (2, 4096, 4096, 1),      # config 1 (Q4_0 GEMV)
+    (12, 14336, 4096, 1),    # config 2 gate/up
+    (12, 4096, 14336, 32),   # config 2 down
+    (8, 1024, 4096, 1),      # config 3 k/v
+    (11, 1024, 16384, 8),    # config 5 k/v
+])
+def test_qmm_benchmark_shapes(gpu, t, N, K, M):
+    torch = _torch()
+    blocks = synth.make_blocks(t, N, K, seed=17)
+    x = synth.make_activations(M, K, seed=18, dtype=np.float16).astype(np.float32)
+    want = loader.qmatmul(t, blocks, N, K, x)
+    w = gpu.Weight.register(blocks, t, N, K)
+    try:
+        assert synth.rel_l2(_run(gpu, w, x, torch.float16, torch.float32), want) < TOL
+    finally:
+        w.release()
+
+
+def test_qmm_prefill_sampled_rows(gpu):
+    """Config 4 at full size (M=2048, K=4096, N=14336, bf16 in): every output
+    is checked against the oracle on a sample of tokens and all N columns."""
+    torch = _torch()
+    t, N, K, M = 12, 14336, 4096, 2048
+    blocks = synth.make_blocks(t, N, K, seed=41)
+    x = torch.from_numpy(synth.make_activations(M, K, seed=42, dtype=np.float32)).to(torch.bfloat16)
+    w = gpu.Weight.register(blocks, t, N, K)
+    try:
+        y = gpu.qmatmul(w, x.cuda(), out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        y = y.cpu().numpy()
+    finally:
+        w.release()
+    rows = np.array([0, 1, 127, 128, 1000, 2047])
+    want = loader.qmatmul(t, blocks, N, K, x[rows].float().numpy())
+    assert synth.rel_l2(y[rows], want) < TOL
+
+
+def test_qmm_errors(gpu):
+    torch = _torch()
+    nxq = gpu
+    blocks = synth.make_blocks(12, 128, 256, seed=1)
+    w = nxq.Weight.register(blocks, 12, 128, 256)
+    x = torch.zeros(2, 256, device="cuda", dtype=torch.float16)
+    y = torch.zeros(2, 128, device="cuda")
+    L = nxq.lib()
+    s = nxq._stream_ptr(None)
+    assert L.nxq_qmatmul(w.handle, x.data_ptr(), 7, y.data_ptr(), 0, 2, s) == -1
+    assert L.nxq_qmatmul(w.handle, x.data_ptr(), 1, y.data_ptr(), 0, -1, s) == -1
+    assert L.nxq_qmatmul(w.handle, None, 1, y.data_ptr(), 0, 2, s) == -1
+    assert L.nxq_qmatmul(w.handle, x.data_ptr(), 1, y.data_ptr(), 0, 0, s) == 0  # M=0 is a no-op
+    w.release()
+    assert L.nxq_qmatmul(w._h or None, x.data_ptr(), 1, y.data_ptr(), 0, 2, s) == -1
