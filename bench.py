@@ -290,62 +290,82 @@ def run_gpu_arm(args, rank, world, local):
     step_bytes = sum(call_bytes(M, K, N) for _, K, N, M in calls)
     names = {(name, M): nxq.kernel_name(weights[name][0], M, nxq.F16, nxq.F32) for name, K, N, M in calls}
     counter = [0]
+    stream = torch.cuda.Stream(device=dev)
 
-    def step(events=None):
-        for i, (name, K, N, M) in enumerate(calls):
-            w = weights[name][counter[0] % reps]
-            if events is not None:
-                events[i][0].record()
-            nxq.qmatmul(w, xs[M][K], out=ys[M][N])
-            if events is not None:
-                events[i][1].record()
-            if name == "down":
-                pass
-        counter[0] += 1
+    def step_calls(rep):
+        for name, K, N, M in calls:
+            nxq.qmatmul(weights[name][rep], xs[M][K], out=ys[M][N], stream=stream)
 
-    for _ in range(args.warmup):
-        step()
+    # Warm up on the capture stream (sizes its scratch), then capture one graph
+    # per weight replica: replaying graph r runs the 15 calls on replica r.
+    with torch.cuda.stream(stream):
+        for r in range(args.warmup):
+            step_calls(r % reps)
+    stream.synchronize()
+    nxq.stream_sync(stream)
+    step_graphs = []
+    for r in range(reps):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step_calls(r)
+        step_graphs.append(g)
+    for r in range(args.warmup):
+        step_graphs[r % reps].replay()
     torch.cuda.synchronize()
-    nxq.stream_sync()
 
-    # --- timed region --------------------------------------------------------
-    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in calls] for _ in range(args.steps)]
+    # --- timed region: K step-graph replays ------------------------------------
     clocks = ClockSampler(local)
     time.sleep(0.3)
     barrier(world)
     torch.cuda.synchronize()
-    l0 = nxq.launch_count()
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
-    t_start.record()
-    for s in range(args.steps):
-        step(ev[s])
-    t_end.record()
+    with torch.cuda.stream(stream):
+        t_start.record(stream)
+        for s_i in range(args.steps):
+            step_graphs[s_i % reps].replay()
+        t_end.record(stream)
     torch.cuda.synchronize()
-    launches = nxq.launch_count() - l0
+    # Graph replays bypass the library's host-side launch counter: every
+    # captured call is one kernel node of ours.
+    launches = len(calls) * args.steps
     barrier(world)
     clk = clocks.stop()
-    nxq.stream_sync()
+    nxq.stream_sync(stream)
     ms = t_start.elapsed_time(t_end)
     ms_max = max_over_ranks(ms, world)
     value = step_bytes * args.steps * world / (ms_max / 1e3) / 1e9
 
-    # per-call and per-kernel accounting
+    # --- per-case device time: a graph of `reps` back-to-back launches of one
+    # (projection, M), each on a different replica ------------------------------
     per_kernel = {}
     per_case = {}
-    for s in range(args.steps):
-        for i, (name, K, N, M) in enumerate(calls):
-            d = ev[s][i][0].elapsed_time(ev[s][i][1])
-            kname = names[(name, M)]
-            k = per_kernel.setdefault(kname, {"ms": 0.0, "bytes": 0, "launches": 0, "shapes": set()})
-            k["ms"] += d
-            k["bytes"] += call_bytes(M, K, N)
-            k["launches"] += 1
-            k["shapes"].add(f"K{K}xN{N}xM{M}")
-            c = per_case.setdefault(f"{name}_M{M}", {"ms": 0.0, "bytes": 0})
-            c["ms"] += d
-            c["bytes"] += call_bytes(M, K, N)
+    for name, K, N, M in calls:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for r in range(reps):
+                nxq.qmatmul(weights[name][r], xs[M][K], out=ys[M][N], stream=stream)
+        g.replay()
+        a_ev, b_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            a_ev.record(stream)
+            for _ in range(3):
+                g.replay()
+            b_ev.record(stream)
+        torch.cuda.synchronize()
+        n_l = 3 * reps
+        d = a_ev.elapsed_time(b_ev)
+        kname = names[(name, M)]
+        k = per_kernel.setdefault(kname, {"ms": 0.0, "bytes": 0, "launches": 0, "shapes": set()})
+        k["ms"] += d
+        k["bytes"] += call_bytes(M, K, N) * n_l
+        k["launches"] += n_l
+        k["shapes"].add(f"K{K}xN{N}xM{M}")
+        c = per_case.setdefault(f"{name}_M{M}", {"ms": 0.0, "bytes": 0})
+        c["ms"] += d
+        c["bytes"] += call_bytes(M, K, N) * n_l
+        del g
+    nxq.stream_sync(stream)
     total_k = sum(k["ms"] for k in per_kernel.values())
     dom_name, dom = max(per_kernel.items(), key=lambda kv: kv[1]["ms"])
     achieved = dom["bytes"] / (dom["ms"] / 1e3) / 1e9
@@ -380,6 +400,7 @@ def run_gpu_arm(args, rank, world, local):
 
         for _ in range(2):
             host_step()
+        nxq.stream_sync()
         barrier(world)
         t0 = time.perf_counter()
         for _ in range(e2e_steps):
@@ -390,6 +411,7 @@ def run_gpu_arm(args, rank, world, local):
                "api": "nxq_qmatmul_host (fp32 host x/y, weights resident)", "steps": e2e_steps,
                "ms_per_step": el / e2e_steps * 1e3}
 
+    del step_graphs
     for name in weights:
         for w in weights[name]:
             w.release()
@@ -408,17 +430,25 @@ def run_gpu_arm(args, rank, world, local):
                 torch.bfloat16).to(dev)
             y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
             prefill["kernel"] = nxq.kernel_name(w, M, nxq.BF16, nxq.BF16)
-            for _ in range(3):
-                nxq.qmatmul(w, x, out=y)
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    nxq.qmatmul(w, x, out=y, stream=stream)
+            stream.synchronize()
+            iters = 4
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for _ in range(iters):
+                    nxq.qmatmul(w, x, out=y, stream=stream)
+            g.replay()
             torch.cuda.synchronize()
-            iters = 5 if M <= 2048 else 3
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             barrier(world)
-            a.record()
-            for _ in range(iters):
-                nxq.qmatmul(w, x, out=y)
-            b.record()
+            with torch.cuda.stream(stream):
+                a.record(stream)
+                g.replay()
+                b.record(stream)
             torch.cuda.synchronize()
+            del g
             t = max_over_ranks(a.elapsed_time(b) / iters, world)
             tf = 2.0 * M * N * K / (t / 1e3) / 1e12
             prefill["cases"][f"M{M}"] = {"ms": t, "TFLOP/s": tf,

@@ -570,6 +570,11 @@ int scratch_for(cudaStream_t st, size_t ws_floats, size_t n_counters, size_t xh_
     }
     const bool grow = sc->ws_floats < ws_floats || sc->n_counters < n_counters || sc->xh_elems < xh_elems;
     if (grow) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
+            return fail(NXQ_ERR_STATE,
+                        "scratch for this stream must grow, which cannot happen during graph capture: "
+                        "run the largest call once on this stream before capturing");
         // The old buffers may still be in use by work queued on this stream.
         cudaError_t e = cudaStreamSynchronize(st);
         if (e != cudaSuccess) return cuda_fail(e, "scratch grow sync");
