@@ -492,15 +492,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                 epi_bar();
                 if (*last_flag) {
                     __threadfence();
+                    // Sum the contributors in CTA order; the NT loads of one
+                    // contributor are independent, so they are all in flight.
+                    float a[NT];
+#pragma unroll
+                    for (int m = 0; m < NT; ++m) a[m] = 0.0f;
+                    for (int64_t c2 = cf; c2 <= cl; ++c2) {
+                        const int s2 = (unit_begin(c2, U, G) / chunks == t) ? 0 : 1;
+                        const float* src = p.ws + ((size_t)c2 * 2 + s2) * (NT * TILE_ROWS) + r;
+#pragma unroll
+                        for (int m = 0; m < NT; ++m)
+                            if (m < M) a[m] += __ldcg(src + m * TILE_ROWS);
+                    }
                     if (n < N) {
-                        for (int m = 0; m < NT && m < M; ++m) {
-                            float a = 0.0f;
-                            for (int64_t c2 = cf; c2 <= cl; ++c2) {
-                                const int s2 = (unit_begin(c2, U, G) / chunks == t) ? 0 : 1;
-                                a += __ldcg(p.ws + ((size_t)c2 * 2 + s2) * (NT * TILE_ROWS) + m * TILE_ROWS + r);
-                            }
-                            store_y(p.y, p.y_dtype, m * N + n, a);
-                        }
+#pragma unroll
+                        for (int m = 0; m < NT; ++m)
+                            if (m < M) store_y(p.y, p.y_dtype, m * N + n, a[m]);
                     }
                     if (et == 0) p.counters[t] = 0u;
                 }

