@@ -154,6 +154,21 @@ NXQ_API int nxq_dequant(nxq_weight_t w, float* y_dev, void* stream);
 NXQ_API int nxq_qmatmul(nxq_weight_t w, const void* x_dev, int x_dtype, void* y_dev,
                         int y_dtype, int64_t M, void* stream);
 
+/* Allocation-free form of nxq_qmatmul, for callers that must not allocate GPU
+ * memory during the call: allocator or memory-pool callbacks, latency-critical
+ * loops that cannot afford cudaMalloc's implicit synchronization, and hosts
+ * that reserve all GPU memory up front.  It has no counterpart in the
+ * reference.  It always runs the exact-decode CUDA-core kernel and keeps that
+ * kernel's split-K partial sums in one fixed 8 MiB device array that every
+ * GPU loading the library holds until exit; M * N may not exceed 2^21
+ * (NXQ_ERR_SHAPE otherwise).  The first call on a device looks up the array's
+ * device address, so make that first call before any stream capture.  All
+ * calls share the array: calls that may overlap on the GPU (on different
+ * streams) race, and the caller must order them.  Same arguments, dtypes and
+ * results (within the matmul tolerance) as nxq_qmatmul. */
+NXQ_API int nxq_qmatmul_noalloc(nxq_weight_t w, const void* x_dev, int x_dtype, void* y_dev,
+                                int y_dtype, int64_t M, void* stream);
+
 /* Host-buffer form, synchronous: the drop-in for ComputeDispatch::gemm_int4
  * (compute_dispatch.h:59-61, .cpp:142-176) - fp32 activations [M][K] in, fp32
  * output [M][N] out, weights resident.  The reference ignores M

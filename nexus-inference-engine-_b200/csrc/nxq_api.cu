@@ -458,6 +458,20 @@ NXQ_API int nxq_qmatmul(nxq_weight_t h, const void* x_dev, int x_dtype, void* y_
     return qmatmul_dispatch(w, x_dev, x_dtype, y_dev, y_dtype, M, (cudaStream_t)stream);
 }
 
+NXQ_API int nxq_qmatmul_noalloc(nxq_weight_t h, const void* x_dev, int x_dtype, void* y_dev, int y_dtype,
+                                int64_t M, void* stream) {
+    Weight* w = nullptr;
+    int rc = check_weight(h, &w);
+    if (rc) return rc;
+    if (M < 0) return fail(NXQ_ERR_ARG, "M=%lld", (long long)M);
+    if (M == 0) return NXQ_OK;
+    if (!x_dev || !y_dev) return fail(NXQ_ERR_ARG, "null activation or output");
+    if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return fail(NXQ_ERR_ARG, "bad dtype");
+    if ((rc = check_ready())) return rc;
+    return launch_qmm_simt_noalloc(w->dev, w->shape, x_dev, x_dtype, y_dev, y_dtype, M, g_ctx.sm_count,
+                                   (cudaStream_t)stream);
+}
+
 NXQ_API int nxq_qmatmul_host(nxq_weight_t h, const float* x_host, float* y_host, int64_t M) {
     Weight* w = nullptr;
     int rc = check_weight(h, &w);

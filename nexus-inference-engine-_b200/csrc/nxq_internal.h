@@ -56,6 +56,11 @@ cudaError_t launch_qmm_simt(const uint8_t* tiled, const TiledShape& s, const voi
                             void* y, int y_dtype, int64_t M, float* partials, int splits,
                             cudaStream_t st);
 int simt_pick_splits(const TiledShape& s, int64_t M, int sm_count);
+// The CUDA-core kernel with its split-K partials in a fixed device array
+// (no allocation); M * N must not exceed kNoAllocScratchFloats.
+constexpr int64_t kNoAllocScratchFloats = 2 * 1024 * 1024;  // 8 MiB of fp32
+int launch_qmm_simt_noalloc(const uint8_t* tiled, const TiledShape& s, const void* x, int x_dtype, void* y,
+                            int y_dtype, int64_t M, int sm_count, cudaStream_t st);
 int simt_rows_per_pass(int64_t M);
 const char* type_name(int type);
 

@@ -10,6 +10,8 @@
 
 #include <cuda_bf16.h>
 
+#include <mutex>
+
 namespace nxq {
 
 namespace {
@@ -138,6 +140,60 @@ cudaError_t launch_qmm_simt(const uint8_t* tiled, const TiledShape& s, const voi
     reduce_splits_kernel<<<(unsigned)g, 256, 0, st>>>(partials, splits, count, y, y_dtype);
     note_launches(1);
     return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant (nxq_qmatmul_noalloc).
+//
+// Some callers cannot allocate GPU memory while they run: code inside a
+// custom allocator or memory-pool callback, real-time loops that forbid
+// cudaMalloc's implicit device synchronization, and hosts whose GPU memory
+// is fully reserved up front.  For them the split-K partial sums of the
+// kernel above live in this fixed array instead of a per-call buffer.  Every
+// GPU that loads the library holds it (kNoAllocScratchFloats floats, 8 MiB)
+// until the process exits.  All calls share it, so calls that can overlap on
+// the GPU (different streams) race and must be serialized by the caller.
+// Nothing in it has to start at zero: every split writes all of its M x N
+// partials before the reduction reads them.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) float g_noalloc_partials[kNoAllocScratchFloats];
+
+namespace {
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[64] = {};  // device address of g_noalloc_partials, per device
+}  // namespace
+
+int launch_qmm_simt_noalloc(const uint8_t* tiled, const TiledShape& s, const void* x, int x_dtype, void* y,
+                            int y_dtype, int64_t M, int sm_count, cudaStream_t st) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return fail(NXQ_ERR_ARG, "device index %d out of range", dev);
+    const int64_t outputs = M * s.N;
+    if (outputs > (int64_t)kNoAllocScratchFloats)
+        return fail(NXQ_ERR_SHAPE,
+                    "nxq_qmatmul_noalloc: M*N = %lld exceeds its fixed scratch of %lld fp32 values",
+                    (long long)outputs, (long long)kNoAllocScratchFloats);
+    float* ptr = nullptr;
+    {
+        // First call on this device: resolve the array's device address (the
+        // host-side symbol is only a stand-in and must not reach a kernel).
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (!g_noalloc_ptr[dev]) {
+            void* p = nullptr;
+            e = cudaGetSymbolAddress(&p, g_noalloc_partials);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress (no-alloc scratch)");
+            g_noalloc_ptr[dev] = static_cast<float*>(p);
+        }
+        ptr = g_noalloc_ptr[dev];
+    }
+    int splits = simt_pick_splits(s, M, sm_count);
+    const int64_t fit = (int64_t)kNoAllocScratchFloats / (outputs > 0 ? outputs : 1);
+    if (splits > fit) splits = (int)fit;
+    if (splits < 1) splits = 1;
+    e = launch_qmm_simt(tiled, s, x, x_dtype, y, y_dtype, M, ptr, splits, st);
+    if (e != cudaSuccess) return cuda_fail(e, "qmm_simt (no-alloc) launch");
+    return NXQ_OK;
 }
 
 }  // namespace nxq

@@ -70,6 +70,8 @@ _SIGS = {
     "nxq_qmatmul": [_c.c_void_p, _c.c_void_p, _c.c_int, _c.c_void_p, _c.c_int, _c.c_int64,
                     _c.c_void_p],
     "nxq_qmatmul_host": [_c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int64],
+    "nxq_qmatmul_noalloc": [_c.c_void_p, _c.c_void_p, _c.c_int, _c.c_void_p, _c.c_int, _c.c_int64,
+                            _c.c_void_p],
     "nxq_stream_sync": [_c.c_void_p],
     "nxq_qmatmul_kernel_name": [_c.c_void_p, _c.c_int64, _c.c_int, _c.c_int, _c.c_char_p, _c.c_size_t],
     "nxq_launch_count": [_c.POINTER(_c.c_uint64)],
