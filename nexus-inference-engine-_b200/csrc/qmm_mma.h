@@ -1,0 +1,17 @@
+// Register-fragment (mma.sync) dequant-fused GEMV for decode batches M <= 32.
+#pragma once
+#include "nxq_internal.h"
+
+namespace nxq {
+
+int context_sm_count();
+
+// Kernel attributes; reads NXQ_DECODE_KERNEL ("tc" or "simt" select another
+// decode kernel, for comparisons).
+int mma_init(int device);
+bool mma_supported(const TiledShape& s, int64_t M);
+void mma_kernel_name(const TiledShape& s, int64_t M, char* buf, size_t n);
+// y = x W^T; NXQ_ERR_UNSUPPORTED to decline.
+int mma_qmatmul(const Weight* w, const void* x, int x_dtype, void* y, int y_dtype, int64_t M, cudaStream_t st);
+
+}  // namespace nxq

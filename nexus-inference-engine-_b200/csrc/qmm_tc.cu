@@ -42,6 +42,7 @@
 
 #include "qmm_tc.h"
 #include "sm100_ptx.cuh"
+#include "stream_scratch.h"
 
 namespace nxq {
 
@@ -526,20 +527,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-// Activation conversion to f16 (for bf16/fp32 or unaligned inputs).
-__global__ void to_half_kernel(const void* __restrict__ x, int dt, __half* __restrict__ out, int64_t n) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        float v;
-        if (dt == NXQ_F32)
-            v = reinterpret_cast<const float*>(x)[i];
-        else if (dt == NXQ_BF16)
-            v = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[i]);
-        else
-            v = __half2float(reinterpret_cast<const __half*>(x)[i]);
-        out[i] = __float2half_rn(v);
-    }
-}
-
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
@@ -550,71 +537,6 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
 EncodeTiledFn g_encode = nullptr;
 bool g_tc_enabled = true;
 size_t g_smem_limit = 0;
-
-// Scratch owned per stream: calls on one stream are ordered, so they can share
-// it; calls on different streams get different scratch.
-struct StreamScratch {
-    cudaStream_t st = nullptr;
-    float* ws = nullptr;
-    size_t ws_floats = 0;
-    unsigned* counters = nullptr;
-    size_t n_counters = 0;
-    __half* xh = nullptr;
-    size_t xh_elems = 0;
-};
-std::mutex g_scratch_mu;
-std::vector<StreamScratch> g_scratch;
-
-int scratch_for(cudaStream_t st, size_t ws_floats, size_t n_counters, size_t xh_elems, StreamScratch** out) {
-    std::lock_guard<std::mutex> lk(g_scratch_mu);
-    StreamScratch* sc = nullptr;
-    for (auto& e : g_scratch)
-        if (e.st == st) sc = &e;
-    if (!sc) {
-        g_scratch.push_back(StreamScratch{});
-        sc = &g_scratch.back();
-        sc->st = st;
-    }
-    const bool grow = sc->ws_floats < ws_floats || sc->n_counters < n_counters || sc->xh_elems < xh_elems;
-    if (grow) {
-        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-        if (cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
-            return fail(NXQ_ERR_STATE,
-                        "scratch for this stream must grow, which cannot happen during graph capture: "
-                        "run the largest call once on this stream before capturing");
-        // The old buffers may still be in use by work queued on this stream.
-        cudaError_t e = cudaStreamSynchronize(st);
-        if (e != cudaSuccess) return cuda_fail(e, "scratch grow sync");
-        if (sc->ws_floats < ws_floats) {
-            cudaFree(sc->ws);
-            sc->ws = nullptr;
-            sc->ws_floats = 0;
-            if ((e = cudaMalloc(&sc->ws, ws_floats * sizeof(float))) != cudaSuccess)
-                return cuda_fail(e, "cudaMalloc (split-K workspace)");
-            sc->ws_floats = ws_floats;
-        }
-        if (sc->n_counters < n_counters) {
-            cudaFree(sc->counters);
-            sc->counters = nullptr;
-            sc->n_counters = 0;
-            if ((e = cudaMalloc(&sc->counters, n_counters * sizeof(unsigned))) != cudaSuccess)
-                return cuda_fail(e, "cudaMalloc (tile counters)");
-            if ((e = cudaMemset(sc->counters, 0, n_counters * sizeof(unsigned))) != cudaSuccess)
-                return cuda_fail(e, "cudaMemset (tile counters)");
-            sc->n_counters = n_counters;
-        }
-        if (sc->xh_elems < xh_elems) {
-            cudaFree(sc->xh);
-            sc->xh = nullptr;
-            sc->xh_elems = 0;
-            if ((e = cudaMalloc(&sc->xh, xh_elems * sizeof(__half))) != cudaSuccess)
-                return cuda_fail(e, "cudaMalloc (f16 activations)");
-            sc->xh_elems = xh_elems;
-        }
-    }
-    *out = sc;
-    return NXQ_OK;
-}
 
 template <int TYPE>
 constexpr int stage_bytes() {
@@ -669,8 +591,8 @@ bool type_has_tc(int type) { return type == T_Q4_K || type == T_Q4_0 || type == 
 }  // namespace
 
 int tc_init(int device) {
-    const char* env = getenv("NXQ_DISABLE_TC");
-    g_tc_enabled = !(env && env[0] == '1');
+    const char* env = getenv("NXQ_DECODE_KERNEL");
+    g_tc_enabled = !(env && env[0] == 's');  // "simt" selects the CUDA-core kernel
     cudaDeviceProp prop;
     cudaError_t e = cudaGetDeviceProperties(&prop, device);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
@@ -717,12 +639,7 @@ int tc_qmatmul(const Weight* w, const void* x, int x_dtype, void* y, int y_dtype
     if (rc) return rc;
     const void* xh = x;
     if (!direct) {
-        int64_t n = M * s.K;
-        int g = (int)((n + 255) / 256);
-        if (g > 4096) g = 4096;
-        to_half_kernel<<<g, 256, 0, st>>>(x, x_dtype, sc->xh, n);
-        note_launches(1);
-        cudaError_t e = cudaGetLastError();
+        cudaError_t e = launch_to_half(x, x_dtype, sc->xh, M * s.K, st);
         if (e != cudaSuccess) return cuda_fail(e, "to_half launch");
         xh = sc->xh;
     }

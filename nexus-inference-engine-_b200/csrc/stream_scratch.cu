@@ -1,0 +1,93 @@
+// Per-stream scratch shared by the matmul kernels (stream_scratch.h).
+#include "stream_scratch.h"
+
+#include <cuda_bf16.h>
+
+#include <list>
+#include <mutex>
+
+namespace nxq {
+
+namespace {
+
+__global__ void to_half_kernel(const void* __restrict__ x, int dt, __half* __restrict__ out, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        float v;
+        if (dt == NXQ_F32)
+            v = reinterpret_cast<const float*>(x)[i];
+        else if (dt == NXQ_BF16)
+            v = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[i]);
+        else
+            v = __half2float(reinterpret_cast<const __half*>(x)[i]);
+        out[i] = __float2half_rn(v);
+    }
+}
+
+std::mutex g_scratch_mu;
+// Entries are never moved, so pointers handed out stay valid.
+std::list<StreamScratch> g_scratch;
+
+}  // namespace
+
+int scratch_for(cudaStream_t st, size_t ws_floats, size_t n_counters, size_t xh_elems, StreamScratch** out) {
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    StreamScratch* sc = nullptr;
+    for (auto& e : g_scratch)
+        if (e.st == st) sc = &e;
+    if (!sc) {
+        g_scratch.push_back(StreamScratch{});
+        sc = &g_scratch.back();
+        sc->st = st;
+    }
+    const bool grow = sc->ws_floats < ws_floats || sc->n_counters < n_counters || sc->xh_elems < xh_elems;
+    if (grow) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
+            return fail(NXQ_ERR_STATE,
+                        "scratch for this stream must grow, which cannot happen during graph capture: "
+                        "run the largest call once on this stream before capturing");
+        // The old buffers may still be in use by work queued on this stream.
+        cudaError_t e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) return cuda_fail(e, "scratch grow sync");
+        if (sc->ws_floats < ws_floats) {
+            cudaFree(sc->ws);
+            sc->ws = nullptr;
+            sc->ws_floats = 0;
+            if ((e = cudaMalloc(&sc->ws, ws_floats * sizeof(float))) != cudaSuccess)
+                return cuda_fail(e, "cudaMalloc (split-K workspace)");
+            sc->ws_floats = ws_floats;
+        }
+        if (sc->n_counters < n_counters) {
+            cudaFree(sc->counters);
+            sc->counters = nullptr;
+            sc->n_counters = 0;
+            if ((e = cudaMalloc(&sc->counters, n_counters * sizeof(unsigned))) != cudaSuccess)
+                return cuda_fail(e, "cudaMalloc (tile counters)");
+            if ((e = cudaMemset(sc->counters, 0, n_counters * sizeof(unsigned))) != cudaSuccess)
+                return cuda_fail(e, "cudaMemset (tile counters)");
+            sc->n_counters = n_counters;
+        }
+        if (sc->xh_elems < xh_elems) {
+            cudaFree(sc->xh);
+            sc->xh = nullptr;
+            sc->xh_elems = 0;
+            if ((e = cudaMalloc(&sc->xh, xh_elems * sizeof(__half))) != cudaSuccess)
+                return cuda_fail(e, "cudaMalloc (f16 activations)");
+            sc->xh_elems = xh_elems;
+        }
+    }
+    *out = sc;
+    return NXQ_OK;
+}
+
+
+cudaError_t launch_to_half(const void* x, int dtype, __half* out, int64_t n, cudaStream_t st) {
+    int64_t g = (n + 255) / 256;
+    if (g > 4096) g = 4096;
+    if (g < 1) g = 1;
+    to_half_kernel<<<(unsigned)g, 256, 0, st>>>(x, dtype, out, n);
+    note_launches(1);
+    return cudaGetLastError();
+}
+
+}  // namespace nxq

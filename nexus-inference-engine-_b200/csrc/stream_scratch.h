@@ -1,0 +1,31 @@
+// Per-stream scratch shared by the matmul kernels: split-K workspace, tile
+// counters (zero between calls; the kernels reset what they use) and an f16
+// copy of the activations for inputs that are not f16.  Calls on one stream
+// are ordered, so they can share one set; calls on different streams get
+// different sets.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "nxq_internal.h"
+
+namespace nxq {
+
+struct StreamScratch {
+    cudaStream_t st = nullptr;
+    float* ws = nullptr;
+    size_t ws_floats = 0;
+    unsigned* counters = nullptr;
+    size_t n_counters = 0;
+    __half* xh = nullptr;
+    size_t xh_elems = 0;
+};
+
+// Scratch of `st`, grown to at least the given sizes.  Growing synchronizes the
+// stream and is refused while the stream is being captured into a graph.
+int scratch_for(cudaStream_t st, size_t ws_floats, size_t n_counters, size_t xh_elems, StreamScratch** out);
+
+// out[i] = (half)x[i] for an f32/bf16/f16 array of n elements.
+cudaError_t launch_to_half(const void* x, int dtype, __half* out, int64_t n, cudaStream_t st);
+
+}  // namespace nxq

@@ -178,15 +178,17 @@ def test_qmm_errors(gpu):
 
 
 @pytest.mark.parametrize("t", MAIN_TYPES, ids=lambda t: NAMES[t])
-def test_tensor_core_path_is_selected(gpu, t):
-    """The block types of the benchmark configs run on the tcgen05 kernel for
-    decode batches; larger M and the other types run the exact CUDA-core path."""
+def test_decode_kernel_is_selected(gpu, t):
+    """The block types of the benchmark configs run decode batches of up to 8
+    tokens on the register-fragment mma.sync kernel and 9..32 tokens on the
+    tcgen05 kernel; larger M and the other types run the exact CUDA-core path."""
     blocks = synth.make_blocks(t, 256, 1024, seed=1)
     w = gpu.Weight.register(blocks, t, 256, 1024)
     try:
-        for M in (1, 16):
-            assert gpu.kernel_name(w, M).startswith("tc_gemv<") and "n16" in gpu.kernel_name(w, M)
-        assert gpu.kernel_name(w, 32).endswith("n32>")
+        for M in (1, 4, 8):
+            assert gpu.kernel_name(w, M) == f"mma_gemv<{NAMES[t]},m8>"
+        for M, nt in ((9, 16), (16, 16), (17, 32), (32, 32)):
+            assert gpu.kernel_name(w, M) == f"tc_gemv<{NAMES[t]},n{nt}>"
     finally:
         w.release()
 
