@@ -1,0 +1,142 @@
+// f16 dequantization of one 32-element group of one weight row, as 16 packed
+// f16 pairs (element 2c in the low half of word c, 2c+1 in the high half) -
+// the layout of a K-major MMA operand row in TMEM.  Used by the tcgen05
+// kernels; `stage` is a tile-chunk staged in shared memory (formats.cuh).
+//
+// Each weight is formed as one f16 rounding of its exact value, computed from
+// f16 scale terms: Q4_K fl16(q*fl16(d*sc) + fl16(-dmin*m)); Q4_0 fl16((q-8)*d);
+// Q8_0 fl16(q*d); Q3_K fl16((q-4)*fl16(d*sc)).  Codes enter through the
+// magic-number trick: a nibble placed in the mantissa of 1024 (or of 64 for a
+// nibble 4 bits higher) is an exact f16 integer once the magic is subtracted.
+#pragma once
+#include <cuda_fp16.h>
+
+#include "formats.cuh"
+
+namespace nxq {
+namespace dq {
+
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+template <int TYPE>
+struct Group;
+
+// Q4_K (gguf_importer.cpp:838-873): record = (d, dmin, scales[12], qs[128]);
+// group G = sub-block G = code bytes 16G..16G+15.
+template <>
+struct Group<T_Q4_K> {
+    static constexpr int kStage = TILE_ROWS * 144;
+    template <int G>
+    __device__ __forceinline__ static void decode(const uint8_t* stage, int r, uint32_t (&o)[16]) {
+        const uint8_t* rec = stage + r * 144;
+        const uint4 hd = *reinterpret_cast<const uint4*>(rec);
+        const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFFu)));
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
+        const uint32_t sb = ((G < 4 ? hd.y : hd.z) >> (8 * (G & 3))) & 0xFFu;
+        const uint32_t eb = (hd.w >> (8 * (G & 3))) & 0xFFu;
+        const int S = (int)(sb & 63u);
+        const int Mn = (int)((sb >> 6) | ((G < 4 ? (eb & 15u) : (eb >> 4)) << 2));
+        const __half2 s2 = __float2half2_rn(d * (float)S);
+        const __half2 o2 = __float2half2_rn(-(dmin * (float)Mn));
+        const __half2 magic = u2h(0x54006400u);  // (1024, 64)
+        const uint4 q = *reinterpret_cast<const uint4*>(rec + 16 + 16 * G);
+        const uint32_t wds[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const uint32_t t = __byte_perm(wds[wi], 0u, 0x4040u | (b << 8) | b);
+                o[wi * 4 + b] = h2u(__hfma2(__hsub2(u2h((t & 0x00F0000Fu) | 0x54006400u), magic), s2, o2));
+            }
+    }
+};
+
+// Q4_0 (gguf_importer.cpp:679-695): record = [d x8][codes x8 of 16 B]; group G
+// = block G: elements 0..15 are the low nibbles of its code bytes, 16..31 the
+// high nibbles.
+template <>
+struct Group<T_Q4_0> {
+    static constexpr int kStage = TILE_ROWS * 144;
+    template <int G>
+    __device__ __forceinline__ static void decode(const uint8_t* stage, int r, uint32_t (&o)[16]) {
+        const uint8_t* rec = stage + r * 144;
+        const uint32_t dbits = *reinterpret_cast<const uint16_t*>(rec + 2 * G);
+        const __half2 s2 = u2h(dbits | (dbits << 16));
+        const __half2 o2 = __hmul2(s2, u2h(0xC800C800u));  // -8 d, exact
+        const __half2 mlo = u2h(0x64006400u), mhi = u2h(0x54005400u);
+        const uint4 q = *reinterpret_cast<const uint4*>(rec + 16 + 16 * G);
+        const uint32_t wds[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+            const uint32_t t0 = __byte_perm(wds[wi], 0u, 0x4140u);
+            const uint32_t t1 = __byte_perm(wds[wi], 0u, 0x4342u);
+            o[2 * wi] = h2u(__hfma2(__hsub2(u2h((t0 & 0x000F000Fu) | 0x64006400u), mlo), s2, o2));
+            o[2 * wi + 1] = h2u(__hfma2(__hsub2(u2h((t1 & 0x000F000Fu) | 0x64006400u), mlo), s2, o2));
+            o[8 + 2 * wi] = h2u(__hfma2(__hsub2(u2h((t0 & 0x00F000F0u) | 0x54005400u), mhi), s2, o2));
+            o[8 + 2 * wi + 1] = h2u(__hfma2(__hsub2(u2h((t1 & 0x00F000F0u) | 0x54005400u), mhi), s2, o2));
+        }
+    }
+};
+
+// Q8_0 (gguf_importer.cpp:721-733): record = [d x8][codes x8 of 32 B].
+template <>
+struct Group<T_Q8_0> {
+    static constexpr int kStage = TILE_ROWS * 272;
+    template <int G>
+    __device__ __forceinline__ static void decode(const uint8_t* stage, int r, uint32_t (&o)[16]) {
+        const uint8_t* rec = stage + r * 272;
+        const uint32_t dbits = *reinterpret_cast<const uint16_t*>(rec + 2 * G);
+        const __half2 s2 = u2h(dbits | (dbits << 16));
+        const __half2 bias = u2h(0x64806480u);  // 1152: signed byte b is 1152 + b after the xor
+        const uint4* qv = reinterpret_cast<const uint4*>(rec + 16 + 32 * G);
+        const uint4 q0 = qv[0], q1 = qv[1];
+        const uint32_t wds[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+        for (int wi = 0; wi < 8; ++wi) {
+            const uint32_t t0 = __byte_perm(wds[wi], 0u, 0x4140u) ^ 0x64806480u;
+            const uint32_t t1 = __byte_perm(wds[wi], 0u, 0x4342u) ^ 0x64806480u;
+            o[2 * wi] = h2u(__hmul2(__hsub2(u2h(t0), bias), s2));
+            o[2 * wi + 1] = h2u(__hmul2(__hsub2(u2h(t1), bias), s2));
+        }
+    }
+};
+
+// Q3_K (gguf_importer.cpp:791-833): plane A = [hmask 32][qs 64] at r*96,
+// plane B = [scales 12][d] at 128*96 + r*14; group G = elements 32G..32G+31,
+// scale groups 2G and 2G+1.
+template <>
+struct Group<T_Q3_K> {
+    static constexpr int kStage = TILE_ROWS * 110;
+    template <int G>
+    __device__ __forceinline__ static void decode(const uint8_t* stage, int r, uint32_t (&o)[16]) {
+        const uint8_t* rec = stage + r * 96;
+        const uint8_t* tl = stage + TILE_ROWS * 96 + r * 14;
+        const float d = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(tl + 12)));
+        __half2 s2[2];
+#pragma unroll
+        for (int gg = 0; gg < 2; ++gg) {
+            const int g = 2 * G + gg;
+            const int i8 = g & 7;
+            const uint32_t lo = tl[i8];
+            const uint32_t hi = tl[8 + i8 / 2] >> (4 * (i8 & 1));
+            const int S = g < 8 ? (int)((lo & 15u) | ((hi & 3u) << 4)) : (int)((lo >> 4) | (((hi >> 2) & 3u) << 4));
+            s2[gg] = __float2half2_rn(d * (float)(S - 32));
+        }
+        const uint32_t hm = *reinterpret_cast<const uint32_t*>(rec + 4 * G);
+        const uint2 qq = *reinterpret_cast<const uint2*>(rec + 32 + 8 * G);
+        const __half2 bias = u2h(0x64046404u);  // 1028: removes the magic and the -4 offset
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+            const uint32_t qw = c < 8 ? qq.x : qq.y;
+            const uint32_t lo = (qw >> (4 * (c & 7))) & 0xFu;  // two 2-bit fields
+            const uint32_t hb = (hm >> (2 * c)) & 3u;           // their two high bits
+            const uint32_t qa = (lo & 3u) | ((hb & 1u) << 2);
+            const uint32_t qb = ((lo >> 2) & 3u) | ((hb >> 1) << 2);
+            o[c] = h2u(__hmul2(__hsub2(u2h(qa | (qb << 16) | 0x64006400u), bias), s2[c >> 3]));
+        }
+    }
+};
+
+}  // namespace dq
+}  // namespace nxq

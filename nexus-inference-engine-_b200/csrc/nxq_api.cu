@@ -15,6 +15,7 @@
 #include <unordered_set>
 
 #include "nxq_internal.h"
+#include "qmm_gemm.h"
 #include "qmm_mma.h"
 #include "qmm_tc.h"
 
@@ -206,6 +207,10 @@ int qmatmul_dispatch(const Weight* w, const void* x, int x_dtype, void* y, int y
         int rc = mma_qmatmul(w, x, x_dtype, y, y_dtype, M, st);
         if (rc != NXQ_ERR_UNSUPPORTED) return rc;
     }
+    if (gemm_supported(s, M)) {
+        int rc = gemm_qmatmul(w, x, x_dtype, y, y_dtype, M, st);
+        if (rc != NXQ_ERR_UNSUPPORTED) return rc;
+    }
     if (tc_supported(s, M, x_dtype, y_dtype)) {
         int rc = tc_qmatmul(w, x, x_dtype, y, y_dtype, M, st);
         if (rc != NXQ_ERR_UNSUPPORTED) return rc;
@@ -281,6 +286,7 @@ NXQ_API int nxq_init(int device) {
     int rc = tc_init(device);
     if (rc != NXQ_OK) return rc;
     if ((rc = mma_init(device)) != NXQ_OK) return rc;
+    if ((rc = gemm_init(device)) != NXQ_OK) return rc;
     g_ctx.ready = true;
     return NXQ_OK;
 }
@@ -509,6 +515,10 @@ NXQ_API int nxq_qmatmul_kernel_name(nxq_weight_t h, int64_t M, int x_dtype, int 
     if (M < 1 || !dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return fail(NXQ_ERR_ARG, "bad M or dtype");
     if (mma_supported(w->shape, M)) {
         mma_kernel_name(w->shape, M, buf, n);
+        return NXQ_OK;
+    }
+    if (gemm_supported(w->shape, M)) {
+        gemm_kernel_name(w->shape, M, buf, n);
         return NXQ_OK;
     }
     if (tc_supported(w->shape, M, x_dtype, y_dtype)) {

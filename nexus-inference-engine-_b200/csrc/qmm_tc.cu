@@ -41,6 +41,7 @@
 #include <vector>
 
 #include "qmm_tc.h"
+#include "dq_f16.cuh"
 #include "sm100_ptx.cuh"
 #include "stream_scratch.h"
 
@@ -65,181 +66,22 @@ constexpr int kMaxNT = 32;
 // `rec` points at the row's record in the shared-memory stage.
 // ---------------------------------------------------------------------------
 
-__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
-
-// Q4_K: record = block (d, dmin, scales[12], qs[128]); gguf_importer.cpp:838-873.
-template <int H>
-__device__ __forceinline__ void dq_q4k(const uint8_t* stage, int r, uint32_t taddr) {
-    const uint8_t* rec = stage + r * 144;
-    const uint4 hd = *reinterpret_cast<const uint4*>(rec);
-    const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFFu)));
-    const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
-    const uint4* qv = reinterpret_cast<const uint4*>(rec + 16 + 64 * H);
-    const __half2 magic = u2h(0x54006400u);  // (1024, 64)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int g = 4 * H + j;
-        uint32_t sb, eb;
-        int S, Mn;
-        if (g < 4) {
-            sb = (hd.y >> (8 * g)) & 0xFFu;
-            eb = (hd.w >> (8 * g)) & 0xFFu;
-            S = sb & 63;
-            Mn = (int)((sb >> 6) | ((eb & 15u) << 2));
-        } else {
-            sb = (hd.z >> (8 * (g - 4))) & 0xFFu;
-            eb = (hd.w >> (8 * (g - 4))) & 0xFFu;
-            S = sb & 63;
-            Mn = (int)((sb >> 6) | ((eb >> 4) << 2));
-        }
-        const __half2 s2 = __float2half2_rn(d * (float)S);
-        const __half2 o2 = __float2half2_rn(-(dmin * (float)Mn));
-        const uint4 q = qv[j];
-        const uint32_t wds[4] = {q.x, q.y, q.z, q.w};
-        uint32_t o[16];
-#pragma unroll
-        for (int wi = 0; wi < 4; ++wi) {
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const uint32_t t = __byte_perm(wds[wi], 0u, 0x4040u | (b << 8) | b);
-                __half2 h = u2h((t & 0x00F0000Fu) | 0x54006400u);
-                h = __hfma2(__hsub2(h, magic), s2, o2);
-                o[wi * 4 + b] = h2u(h);
-            }
-        }
-        ptx::tmem_st16(taddr + 16 * j, o);
-    }
-}
-
-// Q4_0: record = [d x8][codes x8 (16 B)]; gguf_importer.cpp:679-695.
-template <int H>
-__device__ __forceinline__ void dq_q40(const uint8_t* stage, int r, uint32_t taddr) {
-    const uint8_t* rec = stage + r * 144;
-    const uint4 dv = *reinterpret_cast<const uint4*>(rec);
-    const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
-    const uint4* qv = reinterpret_cast<const uint4*>(rec + 16 + 64 * H);
-    const __half2 mlo = u2h(0x64006400u), mhi = u2h(0x54005400u);
-    const __half2 neg8 = u2h(0xC800C800u);  // (-8, -8)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int blk = 4 * H + j;
-        const uint32_t dbits = (blk & 1) ? (dw[blk >> 1] >> 16) : (dw[blk >> 1] & 0xFFFFu);
-        const __half2 s2 = u2h(dbits | (dbits << 16));
-        const __half2 o2 = __hmul2(s2, neg8);  // exact
-        const uint4 q = qv[j];
-        const uint32_t wds[4] = {q.x, q.y, q.z, q.w};
-        uint32_t o[16];
-#pragma unroll
-        for (int wi = 0; wi < 4; ++wi) {
-            const uint32_t t0 = __byte_perm(wds[wi], 0u, 0x4140u);
-            const uint32_t t1 = __byte_perm(wds[wi], 0u, 0x4342u);
-            o[2 * wi] = h2u(__hfma2(__hsub2(u2h((t0 & 0x000F000Fu) | 0x64006400u), mlo), s2, o2));
-            o[2 * wi + 1] = h2u(__hfma2(__hsub2(u2h((t1 & 0x000F000Fu) | 0x64006400u), mlo), s2, o2));
-            o[8 + 2 * wi] = h2u(__hfma2(__hsub2(u2h((t0 & 0x00F000F0u) | 0x54005400u), mhi), s2, o2));
-            o[8 + 2 * wi + 1] = h2u(__hfma2(__hsub2(u2h((t1 & 0x00F000F0u) | 0x54005400u), mhi), s2, o2));
-        }
-        ptx::tmem_st16(taddr + 16 * j, o);
-    }
-}
-
-// Q8_0: record = [d x8][codes x8 (32 B)]; gguf_importer.cpp:721-733.
-template <int H>
-__device__ __forceinline__ void dq_q80(const uint8_t* stage, int r, uint32_t taddr) {
-    const uint8_t* rec = stage + r * 272;
-    const uint4 dv = *reinterpret_cast<const uint4*>(rec);
-    const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
-    const __half2 bias = u2h(0x64806480u);  // (1152, 1152)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int blk = 4 * H + j;
-        const uint32_t dbits = (blk & 1) ? (dw[blk >> 1] >> 16) : (dw[blk >> 1] & 0xFFFFu);
-        const __half2 s2 = u2h(dbits | (dbits << 16));
-        const uint4* qv = reinterpret_cast<const uint4*>(rec + 16 + 32 * blk);
-        const uint4 q0 = qv[0], q1 = qv[1];
-        const uint32_t wds[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-        uint32_t o[16];
-#pragma unroll
-        for (int wi = 0; wi < 8; ++wi) {
-            const uint32_t t0 = __byte_perm(wds[wi], 0u, 0x4140u);
-            const uint32_t t1 = __byte_perm(wds[wi], 0u, 0x4342u);
-            o[2 * wi] = h2u(__hmul2(__hsub2(u2h((t0 ^ 0x00800080u) | 0x64006400u), bias), s2));
-            o[2 * wi + 1] = h2u(__hmul2(__hsub2(u2h((t1 ^ 0x00800080u) | 0x64006400u), bias), s2));
-        }
-        ptx::tmem_st16(taddr + 16 * j, o);
-    }
-}
-
-// Q3_K: plane A = [hmask 32][qs 64] at r*96, plane B = [scales 12][d] at
-// 128*96 + r*14; gguf_importer.cpp:791-833.
-template <int H>
-__device__ __forceinline__ void dq_q3k(const uint8_t* stage, int r, uint32_t taddr) {
-    const uint8_t* rec = stage + r * 96;
-    const uint16_t* tl = reinterpret_cast<const uint16_t*>(stage + TILE_ROWS * 96 + r * 14);
-    uint32_t sc[12];
-#pragma unroll
-    for (int i = 0; i < 6; ++i) {
-        const uint32_t v = tl[i];
-        sc[2 * i] = v & 0xFFu;
-        sc[2 * i + 1] = v >> 8;
-    }
-    const float d = __half2float(__ushort_as_half(tl[6]));
-    const __half2 bias = u2h(0x64046404u);  // (1028, 1028): removes the magic and the -4 offset
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int e0 = 128 * H + 32 * j;
-        const uint32_t hm = *reinterpret_cast<const uint32_t*>(rec + e0 / 8);
-        const uint2 qq = *reinterpret_cast<const uint2*>(rec + 32 + e0 / 4);
-        __half2 s2[2];
-#pragma unroll
-        for (int gg = 0; gg < 2; ++gg) {
-            const int g = e0 / 16 + gg;
-            const int i8 = g & 7;
-            const uint32_t hi = sc[8 + i8 / 2] >> (4 * (i8 & 1));
-            int S = g < 8 ? (int)((sc[i8] & 15u) | ((hi & 3u) << 4)) : (int)((sc[i8] >> 4) | (((hi >> 2) & 3u) << 4));
-            s2[gg] = __float2half2_rn(d * (float)(S - 32));
-        }
-        uint32_t o[16];
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-            const uint32_t qw = c < 8 ? qq.x : qq.y;
-            const int sh = 4 * (c & 7);
-            const uint32_t lo = (qw >> sh) & 0xFu;                 // two 2-bit fields
-            const uint32_t hb = (hm >> (2 * c)) & 3u;                // two high bits
-            const uint32_t qa = (lo & 3u) | ((hb & 1u) << 2);
-            const uint32_t qb = ((lo >> 2) & 3u) | ((hb >> 1) << 2);
-            const __half2 v = __hsub2(u2h(qa | (qb << 16) | 0x64006400u), bias);
-            o[c] = h2u(__hmul2(v, s2[c >> 3]));
-        }
-        ptx::tmem_st16(taddr + 16 * j, o);
-    }
-}
-
+// Fmt<TYPE>::dq<H>: half H of a row's chunk (groups 4H..4H+3) into 64 TMEM columns.
 template <int TYPE>
-struct Fmt;
-template <>
-struct Fmt<T_Q4_K> {
-    static constexpr int kStageBytes = TILE_ROWS * 144;
+struct Fmt {
+    static constexpr int kStageBytes = dq::Group<TYPE>::kStage;
     template <int H>
-    __device__ static void dq(const uint8_t* s, int r, uint32_t t) { dq_q4k<H>(s, r, t); }
-};
-template <>
-struct Fmt<T_Q4_0> {
-    static constexpr int kStageBytes = TILE_ROWS * 144;
-    template <int H>
-    __device__ static void dq(const uint8_t* s, int r, uint32_t t) { dq_q40<H>(s, r, t); }
-};
-template <>
-struct Fmt<T_Q8_0> {
-    static constexpr int kStageBytes = TILE_ROWS * 272;
-    template <int H>
-    __device__ static void dq(const uint8_t* s, int r, uint32_t t) { dq_q80<H>(s, r, t); }
-};
-template <>
-struct Fmt<T_Q3_K> {
-    static constexpr int kStageBytes = TILE_ROWS * 110;
-    template <int H>
-    __device__ static void dq(const uint8_t* s, int r, uint32_t t) { dq_q3k<H>(s, r, t); }
+    __device__ static void dq(const uint8_t* s, int r, uint32_t t) {
+        uint32_t o[16];
+        dq::Group<TYPE>::template decode<4 * H + 0>(s, r, o);
+        ptx::tmem_st16(t + 0, o);
+        dq::Group<TYPE>::template decode<4 * H + 1>(s, r, o);
+        ptx::tmem_st16(t + 16, o);
+        dq::Group<TYPE>::template decode<4 * H + 2>(s, r, o);
+        ptx::tmem_st16(t + 32, o);
+        dq::Group<TYPE>::template decode<4 * H + 3>(s, r, o);
+        ptx::tmem_st16(t + 48, o);
+    }
 };
 
 // ---------------------------------------------------------------------------

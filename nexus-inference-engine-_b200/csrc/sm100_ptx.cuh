@@ -54,7 +54,7 @@ struct WaitCtl {
     DeviceStatus* status;     // device status word (global)
 };
 
-__device__ __noinline__ void raise_timeout(const WaitCtl& c, unsigned where) {
+static __device__ __noinline__ void raise_timeout(const WaitCtl& c, unsigned where) {
     *c.abort = 1;
     if (atomicCAS(&c.status->code, 0u, 1u) == 0u) c.status->where = where;
     __threadfence();

@@ -228,3 +228,25 @@ def test_launch_counter_counts_our_kernels(gpu):
     torch.cuda.synchronize()
     assert gpu.launch_count() - c0 == 5
     w.release()
+
+
+@pytest.mark.parametrize("t", MAIN_TYPES, ids=lambda t: NAMES[t])
+@pytest.mark.parametrize("M,N,K", [(33, 384, 2048), (300, 256, 1024), (512, 1000, 768), (1024, 640, 4096)])
+def test_prefill_gemm_shapes(gpu, t, M, N, K):
+    """The tcgen05 prefill GEMM on ragged token counts, row counts and (for
+    32-element blocks) reduction lengths, bf16 activations."""
+    torch = _torch()
+    if K % synth.GEOMETRY[t][0]:
+        pytest.skip("K not a multiple of the block")
+    blocks = synth.make_blocks(t, N, K, seed=M + N + K)
+    x = torch.from_numpy(synth.make_activations(M, K, seed=M, dtype=np.float32)).to(torch.bfloat16)
+    w = gpu.Weight.register(blocks, t, N, K)
+    try:
+        assert gpu.kernel_name(w, M, gpu.BF16, gpu.F32).startswith("tc_gemm<")
+        y = gpu.qmatmul(w, x.cuda(), out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        gpu.stream_sync()
+        want = loader.qmatmul(t, blocks, N, K, x.float().numpy())
+        assert synth.rel_l2(y.cpu().numpy(), want) < TOL
+    finally:
+        w.release()
