@@ -11,13 +11,15 @@
 //   warp 0       producer: the packed tile-chunk (256 k) by one 1-D bulk copy
 //                per chunk, and the 256 x 64 f16 activation box by TMA
 //                (128-byte swizzle, no multicast)
-//   warps 2-9    two dequant warpgroups: thread r decodes row r's 32-element
-//                group (2 per k-step, one per warpgroup) to f16 and writes it
-//                to TMEM with tcgen05.st - the MMA's A operand
+//   warps 2-17   four dequant warpgroups: thread r decodes row r's 32-element
+//                group to f16 and writes it to TMEM with tcgen05.st - the
+//                MMA's A operand; a k-step's two groups go to two warpgroups,
+//                alternate k-steps to the other two
 //   warp 1       one thread issues 4 x tcgen05.mma.kind::f16 M=128 N=256 K=16
 //                (A from TMEM, B from shared memory) into a 256-column fp32
 //                accumulator in TMEM
-//   warps 10-13  epilogue: tcgen05.ld of the accumulator, conversion, store
+//   warps 18-25  epilogue: tcgen05.ld of the accumulator (two warps per lane
+//                quadrant, half the token columns each), conversion, store
 // Every wait is bounded (sm100_ptx.cuh).
 //
 // Numerics as the decode kernels: weights rounded once to f16, activations
@@ -38,8 +40,10 @@ namespace nxq {
 
 namespace {
 
-constexpr int kThreads = 448;
-constexpr int kWarpProducer = 0, kWarpMma = 1, kWarpDeq0 = 2, kWarpEpi0 = 10;
+constexpr int kDeqGroups = 4;  // dequant warpgroups
+constexpr int kEpiWarps = 8;   // two per TMEM lane quadrant
+constexpr int kWarpProducer = 0, kWarpMma = 1, kWarpDeq0 = 2, kWarpEpi0 = 2 + 4 * kDeqGroups;
+constexpr int kThreads = 32 * (kWarpEpi0 + kEpiWarps);
 constexpr int kNT = 256;              // tokens per work tile (MMA N)
 constexpr int kKS = 64;               // reduction elements per k-step (one swizzle atom)
 constexpr int kStepsPerChunk = CHUNK_K / kKS;
@@ -117,14 +121,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p
         }
         for (int i = 0; i < kWStages; ++i) {
             ptx::mbar_init(&w_full[i], 1);
-            ptx::mbar_init(&w_empty[i], 8);
+            ptx::mbar_init(&w_empty[i], 4 * kDeqGroups);
         }
         for (int i = 0; i < kAStages; ++i) {
             ptx::mbar_init(&a_full[i], 8);
             ptx::mbar_init(&a_empty[i], 1);
         }
         ptx::mbar_init(d_full, 1);
-        ptx::mbar_init(d_empty, 4);
+        ptx::mbar_init(d_empty, kEpiWarps);
         ptx::mbar_init(drain, 1);
         *abort_flag = 0;
         ptx::fence_mbar_init();
@@ -206,7 +210,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p
             }
         }
     } else if (warp < kWarpEpi0) {
-        const int h = (warp - kWarpDeq0) >> 2, quad = warp & 3, r = quad * 32 + lane;
+        // Warpgroup wg takes k-steps of parity wg/2, group 2*step + wg%2.
+        const int wg = (warp - kWarpDeq0) >> 2, quad = warp & 3, r = quad * 32 + lane;
+        const int h = wg & 1, par = wg >> 1;
         uint32_t qw = 0, qa = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < p.tiles && ok; tile += G) {
@@ -216,6 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p
                 const uint8_t* stage = ws + sw * WB;
 #pragma unroll
                 for (int st = 0; st < kStepsPerChunk; ++st, ++qa) {
+                    if ((st & 1) != par) continue;
                     const int sa = qa % kAStages;
                     if (qa >= kAStages && !(ok = warp_wait(&a_empty[sa], ((qa / kAStages) & 1) ^ 1u, ctl, 17))) break;
                     ptx::tc_fence_after();
@@ -234,7 +241,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p
             }
         }
     } else {
-        const int quad = warp & 3, r = quad * 32 + lane;
+        const int ew = warp - kWarpEpi0, quad = warp & 3, r = quad * 32 + lane;
+        const int half = ew >> 2;  // which 128 token columns
         const int64_t M = p.M, N = p.s.N;
         uint32_t nt = 0;
         for (int tile = blockIdx.x; tile < p.tiles; tile += G, ++nt) {
@@ -242,16 +250,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p
             ptx::tc_fence_after();
             const int wt = tile / p.m_tiles, mt = tile - wt * p.m_tiles;
             const int64_t n = (int64_t)wt * TILE_ROWS + r;
-            const int64_t m0 = (int64_t)mt * kNT;
+            const int64_t m0 = (int64_t)mt * kNT + half * (kNT / 2);
 #pragma unroll 1
-            for (int cb = 0; cb < kNT / 16; ++cb) {
-                uint32_t v[16];
-                ptx::tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + kColD + 16 * cb, v);
+            for (int cb = 0; cb < kNT / 2 / 32; ++cb) {
+                uint32_t v[32];
+                const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + kColD + half * (kNT / 2) + 32 * cb;
+                ptx::tmem_ld16(ta, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+                ptx::tmem_ld16(ta + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
                 ptx::tmem_wait_ld();
                 if (n < N) {
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int64_t m = m0 + 16 * cb + j;
+                    for (int j = 0; j < 32; ++j) {
+                        const int64_t m = m0 + 32 * cb + j;
                         if (m < M) store_y(p.y, p.y_dtype, m * N + n, __uint_as_float(v[j]));
                     }
                 }
