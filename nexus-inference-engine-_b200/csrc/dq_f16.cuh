@@ -22,6 +22,17 @@ __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__
 template <int TYPE>
 struct Group;
 
+// Four f16 pairs of a code word in the tiled 4-bit order (formats.cuh,
+// q4_code_pos): elements (8w, 8w+1) .. (8w+6, 8w+7) as fl16(q * s + o).
+__device__ __forceinline__ void q4_word_pairs(uint32_t w, __half2 s2, __half2 o2, uint32_t* o) {
+    const __half2 m_lo = u2h(0x64006400u), m_hi = u2h(0x54005400u);  // 1024, 64
+    const uint32_t w8 = w >> 8;
+    o[0] = h2u(__hfma2(__hsub2(u2h((w & 0x000F000Fu) | 0x64006400u), m_lo), s2, o2));
+    o[1] = h2u(__hfma2(__hsub2(u2h((w & 0x00F000F0u) | 0x54005400u), m_hi), s2, o2));
+    o[2] = h2u(__hfma2(__hsub2(u2h((w8 & 0x000F000Fu) | 0x64006400u), m_lo), s2, o2));
+    o[3] = h2u(__hfma2(__hsub2(u2h((w8 & 0x00F000F0u) | 0x54005400u), m_hi), s2, o2));
+}
+
 // Q4_K (gguf_importer.cpp:838-873): record = (d, dmin, scales[12], qs[128]);
 // group G = sub-block G = code bytes 16G..16G+15.
 template <>
@@ -39,22 +50,16 @@ struct Group<T_Q4_K> {
         const int Mn = (int)((sb >> 6) | ((G < 4 ? (eb & 15u) : (eb >> 4)) << 2));
         const __half2 s2 = __float2half2_rn(d * (float)S);
         const __half2 o2 = __float2half2_rn(-(dmin * (float)Mn));
-        const __half2 magic = u2h(0x54006400u);  // (1024, 64)
         const uint4 q = *reinterpret_cast<const uint4*>(rec + 16 + 16 * G);
-        const uint32_t wds[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int wi = 0; wi < 4; ++wi)
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const uint32_t t = __byte_perm(wds[wi], 0u, 0x4040u | (b << 8) | b);
-                o[wi * 4 + b] = h2u(__hfma2(__hsub2(u2h((t & 0x00F0000Fu) | 0x54006400u), magic), s2, o2));
-            }
+        q4_word_pairs(q.x, s2, o2, &o[0]);
+        q4_word_pairs(q.y, s2, o2, &o[4]);
+        q4_word_pairs(q.z, s2, o2, &o[8]);
+        q4_word_pairs(q.w, s2, o2, &o[12]);
     }
 };
 
 // Q4_0 (gguf_importer.cpp:679-695): record = [d x8][codes x8 of 16 B]; group G
-// = block G: elements 0..15 are the low nibbles of its code bytes, 16..31 the
-// high nibbles.
+// = block G.
 template <>
 struct Group<T_Q4_0> {
     static constexpr int kStage = TILE_ROWS * 144;
@@ -64,18 +69,11 @@ struct Group<T_Q4_0> {
         const uint32_t dbits = *reinterpret_cast<const uint16_t*>(rec + 2 * G);
         const __half2 s2 = u2h(dbits | (dbits << 16));
         const __half2 o2 = __hmul2(s2, u2h(0xC800C800u));  // -8 d, exact
-        const __half2 mlo = u2h(0x64006400u), mhi = u2h(0x54005400u);
         const uint4 q = *reinterpret_cast<const uint4*>(rec + 16 + 16 * G);
-        const uint32_t wds[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int wi = 0; wi < 4; ++wi) {
-            const uint32_t t0 = __byte_perm(wds[wi], 0u, 0x4140u);
-            const uint32_t t1 = __byte_perm(wds[wi], 0u, 0x4342u);
-            o[2 * wi] = h2u(__hfma2(__hsub2(u2h((t0 & 0x000F000Fu) | 0x64006400u), mlo), s2, o2));
-            o[2 * wi + 1] = h2u(__hfma2(__hsub2(u2h((t1 & 0x000F000Fu) | 0x64006400u), mlo), s2, o2));
-            o[8 + 2 * wi] = h2u(__hfma2(__hsub2(u2h((t0 & 0x00F000F0u) | 0x54005400u), mhi), s2, o2));
-            o[8 + 2 * wi + 1] = h2u(__hfma2(__hsub2(u2h((t1 & 0x00F000F0u) | 0x54005400u), mhi), s2, o2));
-        }
+        q4_word_pairs(q.x, s2, o2, &o[0]);
+        q4_word_pairs(q.y, s2, o2, &o[4]);
+        q4_word_pairs(q.z, s2, o2, &o[8]);
+        q4_word_pairs(q.w, s2, o2, &o[12]);
     }
 };
 

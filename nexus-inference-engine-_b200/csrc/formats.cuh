@@ -15,8 +15,11 @@
 // Inside a tile-chunk each format keeps a row's bytes in "planes" so a thread
 // that owns row r reads 16-byte aligned words (see place_block() below).
 // Rows beyond N and blocks beyond K are zero bytes, which every format decodes
-// to zero.  No byte is transformed: decoding the tiled copy gives exactly the
-// values of decoding the GGUF bytes.
+// to zero.  Decoding the tiled copy gives exactly the values of decoding the
+// GGUF bytes.  Scales and most codes are copied byte for byte; the one
+// transformation is the order of the 4-bit codes of Q4_0 and Q4_K inside each
+// 32-element group (see q4_code_pos()), chosen so that one AND/OR of a 32-bit
+// code word yields two consecutive elements as an f16 pair.
 #pragma once
 #include <cstdint>
 #include <cuda_fp16.h>
@@ -90,10 +93,11 @@ inline bool make_tiled_shape(int type, int64_t N, int64_t K, TiledShape* s) {
 //   segments; planes are laid out so per-row records are 16-byte aligned where
 //   the kernels read them with vector loads.
 //
-//   Q4_0  record 144 B: [d x8 : 16 B][codes x8 : 8 x 16 B]
+//   Q4_0  record 144 B: [d x8 : 16 B][codes x8 : 8 x 16 B, tiled code order]
 //   Q4_1  record 160 B: [(d,m) x8 : 32 B][codes x8 : 8 x 16 B]
 //   Q8_0  record 272 B: [d x8 : 16 B][codes x8 : 8 x 32 B]
-//   Q4_K  record 144 B: the block itself (d, dmin, scales[12], qs[128])
+//   Q4_K  record 144 B: the block itself (d, dmin, scales[12], qs[128]), qs in
+//         tiled code order
 //   Q5_K  record 176 B: the block itself
 //   Q3_K  plane A 128 x 96 B (hmask[32], qs[64]); plane B 128 x 14 B (scales[12], d)
 //   Q2_K  plane A 128 x 80 B (scales[16], qs[64]); plane B 128 x 4 B (dmin, d)
@@ -144,6 +148,46 @@ __host__ __device__ inline int block_segments(int type, int r, int j, Segment* s
 }
 
 // ---------------------------------------------------------------------------
+// 4-bit code order of Q4_0 / Q4_K in the tiled copy.  A 32-element group (a
+// Q4_0 block; a Q4_K sub-block) keeps its 16 code bytes, as four 32-bit
+// little-endian words; element e of the group sits in word e/8 at bit
+// 16*(e&1) + 4*((e&7)>>1).  So word w holds elements 8w..8w+7 with the pairs
+// (8w, 8w+1), (8w+2, 8w+3) in bits {0-3, 16-19} and {4-7, 20-23}, and the next
+// two pairs in the same places of w >> 8.
+// Where the GGUF block holds element e of a group:
+//   Q4_0  byte e % 16, high nibble iff e >= 16   (gguf_importer.cpp:687-690)
+//   Q4_K  byte e / 2,  high nibble iff e is odd  (gguf_importer.cpp:864-868)
+// ---------------------------------------------------------------------------
+__host__ __device__ inline void q4_code_pos(int e, int* byte, int* shift) {
+    const int i = e & 7;
+    *byte = 4 * (e >> 3) + 2 * (i & 1) + (i >> 2);
+    *shift = 4 * ((i >> 1) & 1);
+}
+
+__host__ __device__ inline int q4_gguf_code(int type, const uint8_t* g, int e) {
+    if (type == T_Q4_0) return e < 16 ? (g[e] & 15) : (g[e - 16] >> 4);
+    return (e & 1) ? (g[e >> 1] >> 4) : (g[e >> 1] & 15);
+}
+
+// Writes the 16 code bytes of one 32-element group in the tiled order.
+__host__ __device__ inline void q4_reorder_group(int type, const uint8_t* gguf, uint8_t* out) {
+    uint8_t b[16];
+    for (int i = 0; i < 16; ++i) b[i] = 0;
+    for (int e = 0; e < 32; ++e) {
+        int byte, shift;
+        q4_code_pos(e, &byte, &shift);
+        b[byte] = (uint8_t)(b[byte] | (q4_gguf_code(type, gguf, e) << shift));
+    }
+    for (int i = 0; i < 16; ++i) out[i] = b[i];
+}
+
+__device__ __forceinline__ int q4_tiled_code(const uint8_t* g, int e) {
+    int byte, shift;
+    q4_code_pos(e, &byte, &shift);
+    return (g[byte] >> shift) & 15;
+}
+
+// ---------------------------------------------------------------------------
 // Exact device decode.  Every multiply/subtract is an explicit round-to-nearest
 // fp32 intrinsic, in the reference's evaluation order, so nvcc cannot contract
 // them into FMAs and the decoded bits equal the reference's.
@@ -186,11 +230,7 @@ __device__ inline void decode8(int type, const uint8_t* chunk, int r, int e0, fl
             int j = e0 >> 5, w = e0 & 31;
             float d = half_bits_to_float(rd16(rec + 2 * j));
             const uint8_t* q = rec + 16 + 16 * j;
-            for (int i = 0; i < 8; ++i) {
-                int e = w + i;
-                int c = e < 16 ? (q[e] & 15) : (q[e - 16] >> 4);
-                out[i] = __fmul_rn((float)(c - 8), d);
-            }
+            for (int i = 0; i < 8; ++i) out[i] = __fmul_rn((float)(q4_tiled_code(q, w + i) - 8), d);
             break;
         }
         case T_Q4_1: {  // :699-717
@@ -255,12 +295,9 @@ __device__ inline void decode8(int type, const uint8_t* chunk, int r, int e0, fl
             kquant_scale_min(rec + 4, e0 >> 5, &s, &m);
             float ds = __fmul_rn(d, (float)s);
             float dm = __fmul_rn(dmin, (float)m);
-            for (int i = 0; i < 8; ++i) {
-                int e = e0 + i;
-                int c = rec[16 + (e >> 1)];
-                int q = (e & 1) ? (c >> 4) : (c & 15);
-                out[i] = __fsub_rn(__fmul_rn(ds, (float)q), dm);
-            }
+            const uint8_t* q = rec + 16 + 16 * (e0 >> 5);
+            for (int i = 0; i < 8; ++i)
+                out[i] = __fsub_rn(__fmul_rn(ds, (float)q4_tiled_code(q, (e0 & 31) + i)), dm);
             break;
         }
         case T_Q5_K: {  // :878-915

@@ -27,6 +27,12 @@ __global__ void repack_kernel(const uint8_t* __restrict__ src, uint8_t* __restri
         int ns = block_segments(s.type, (int)r, (int)j, seg);
         for (int q = 0; q < ns; ++q)
             for (int t = 0; t < seg[q].len; ++t) base[seg[q].dst + t] = blk[seg[q].src + t];
+        // 4-bit codes go in the tiled order (formats.cuh, q4_code_pos).
+        if (s.type == T_Q4_0) {
+            q4_reorder_group(T_Q4_0, blk + 2, base + seg[1].dst);
+        } else if (s.type == T_Q4_K) {
+            for (int g = 0; g < 8; ++g) q4_reorder_group(T_Q4_K, blk + 16 + 16 * g, base + seg[0].dst + 16 + 16 * g);
+        }
     }
 }
 

@@ -8,28 +8,35 @@
 // Why mma.sync and not tcgen05 here: a tcgen05.mma with M=128, K=16 costs
 // ~60 cycles for any N <= 128 (measured on this B200), so feeding dequantized
 // weights as its 128-row operand caps a GEMV at ~34 weights/cycle/SM.  The
-// warp-level mma.sync.m16n8k16 is issued by all four schedulers with operands
-// straight from registers (measured 2 cycles/instruction/SM); with the
-// weights as its 8-column B operand that is 64 weights/cycle/SM at M <= 16,
-// leaving the packed-weight stream from HBM as the bound.  The prefill GEMM,
-// where N is large, uses tcgen05.
+// warp-level mma.sync.m16n8k16 takes its operands straight from the registers
+// the dequantization writes, at 2 cycles/instruction/SM (measured), and the
+// kernel is bound by the instructions that unpack the codes.  So the design
+// minimises instructions per weight:
+//   - weights are the mma's 16-row A operand (256 weights per mma; the tokens
+//     are its 8 columns, 1..4 n8 tiles for M <= 8/16/32, all reusing the same
+//     dequantized fragments);
+//   - the tiled 4-bit code order (formats.cuh, q4_code_pos) makes each pair
+//     of consecutive elements one AND/OR of a code word, then one f16
+//     subtract of the magic number and one f16 FMA with the scale and offset;
+//   - the activations are staged in their natural order, 8 elements per
+//     16-byte piece, in lane order so the fragment loads are conflict-free.
 //
 // Decomposition (shared with the tcgen05 kernels): the weight is stored tiled
 // (formats.cuh), a unit is one tile-chunk (128 rows x 256 k, contiguous in
-// HBM), and a persistent grid of one CTA per SM takes contiguous unit ranges
-// (stream-K).  A tile split between CTAs is summed by the last of them to
-// finish (per-tile counter, fp32 partials in a workspace, CTA order), so the
-// result is deterministic; each CTA processes its split tiles first, so those
-// fixups overlap the rest of its work instead of trailing it.
+// HBM), and a persistent grid of one or two CTAs per SM takes contiguous unit
+// ranges (stream-K).  A tile split between CTAs is summed by the last of them
+// to finish (per-tile counter, fp32 partials in a workspace, CTA order), so
+// the result is deterministic; each CTA processes its split tiles first, so
+// those fixups overlap the rest of its work instead of trailing it.
 //
-// Per CTA, 16 warps; warp w owns weight rows 8w..8w+7 of the tile (the n8
-// tile of its mma).  In lane (g, t) (g = lane/4, t = lane%4), the mma's
+// Per CTA, 8 warps; warp w owns weight rows 16w..16w+15 of the tile.  Lane
+// (g, t) (g = lane/4, t = lane%4) holds rows 16w+g and 16w+8+g, and the mma's
 // k-slots {2t, 2t+1, 2t+8, 2t+9} of k-step j map to chunk elements
-// 64t + 4j + {0,1,2,3}, for x and W alike, so every lane reads one row (g) and
-// one private 64-element slice of it: exactly two 32-element sub-blocks, whose
-// scales it alone needs.  Units are staged with cp.async into an S-deep
-// shared-memory ring: the packed tile-chunk byte for byte, and x as 8-byte
-// pieces in a bank-conflict-free fragment order.
+// 64t + 4j + {0, 1, 2, 3}, for x and W alike: every lane decodes one private
+// 64-element slice of two rows, exactly the sub-blocks whose scales it alone
+// needs.  Units are staged with cp.async into an S-deep shared-memory ring:
+// the packed tile-chunk byte for byte, and x as 16-byte pieces
+// x[token][64t + 8m .. 64t + 8m + 7] at piece index (n8 tile, m, lane).
 //
 // Numerics: each weight is formed in f16 as fl16(q * fl16(d*sc) + fl16(-dmin*m))
 // (Q4_K; the other types analogously), products are exact and accumulate in
@@ -40,7 +47,9 @@
 #include <cstdio>
 #include <cstdlib>
 
+#include "dq_f16.cuh"
 #include "qmm_mma.h"
+#include "sm100_ptx.cuh"
 #include "stream_scratch.h"
 
 namespace nxq {
@@ -51,21 +60,18 @@ constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxMT = 32;
 
+using dq::h2u;
+using dq::u2h;
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// C[16 rows][8 tokens] += A[16 rows][16 k] * B[16 k][8 tokens]; f16 in, fp32 accumulate.
 __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
     asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
@@ -74,67 +80,23 @@ __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
-__device__ __forceinline__ uint32_t sel4(uint32_t i, const uint4& v) {
-    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
-}
 __device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
     return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
-// Byte b of a 32-bit word as the f16 pair (1024 + lo nibble, 64 + hi nibble).
-__device__ __forceinline__ __half2 nib_pair(uint32_t w, int b) {
-    const uint32_t t = __byte_perm(w, 0u, 0x4040u | (b << 8) | b);
-    return u2h((t & 0x00F0000Fu) | 0x54006400u);
-}
 
 // ---------------------------------------------------------------------------
-// Per-format lane decoders.  load() reads the lane's slice of row `row` of a
-// staged tile-chunk; frag(j) returns the two B registers of k-step j (weights
-// at chunk elements 64t + 4j + {0,1} and {2,3}) as f16 pairs.
+// Per-format lane decoders.  load() reads the lane's 64-element slice (chunk
+// elements 64t .. 64t+63) of row `row` of a staged tile-chunk and its scales;
+// pairs(m, p) returns elements 8m .. 8m+7 of the slice as four f16 pairs
+// (2i, 2i+1), i = 0..3.
 // ---------------------------------------------------------------------------
 template <int TYPE>
 struct Lane;
 
 // Q4_K (gguf_importer.cpp:838-873): record = block (d, dmin, scales[12], qs[128]);
-// the lane's elements are sub-blocks 2t, 2t+1 = code bytes 32t .. 32t+31.
+// the slice is sub-blocks 2t, 2t+1 = code bytes 32t .. 32t+31.
 template <>
 struct Lane<T_Q4_K> {
-    static constexpr int kStage = TILE_ROWS * 144;
-    uint4 hd, q0, q1;
-    __half2 s2[2], o2[2];
-    __device__ __forceinline__ void load(const uint8_t* st, int row, int t) {
-        const uint8_t* rec = st + row * 144;
-        hd = *reinterpret_cast<const uint4*>(rec);
-        q0 = *reinterpret_cast<const uint4*>(rec + 16 + 32 * t);
-        q1 = *reinterpret_cast<const uint4*>(rec + 32 + 32 * t);
-        const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFFu)));
-        const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
-#pragma unroll
-        for (int sub = 0; sub < 2; ++sub) {
-            const int g = 2 * t + sub;
-            const uint32_t sb = ((g < 4 ? hd.y : hd.z) >> (8 * (g & 3))) & 0xFFu;
-            const uint32_t eb = (hd.w >> (8 * (g & 3))) & 0xFFu;
-            const int S = (int)(sb & 63u);
-            const int Mn = (int)((sb >> 6) | ((g < 4 ? (eb & 15u) : (eb >> 4)) << 2));
-            s2[sub] = __float2half2_rn(d * (float)S);
-            o2[sub] = __float2half2_rn(-(dmin * (float)Mn));
-        }
-    }
-    __device__ __forceinline__ void frag(int j, uint32_t& b0, uint32_t& b1) const {
-        const uint32_t w = word_of(j < 8 ? q0 : q1, (j >> 1) & 3);
-        const int b = 2 * (j & 1);
-        const __half2 magic = u2h(0x54006400u);
-        const int sub = j >> 3;
-        b0 = h2u(__hfma2(__hsub2(nib_pair(w, b), magic), s2[sub], o2[sub]));
-        b1 = h2u(__hfma2(__hsub2(nib_pair(w, b + 1), magic), s2[sub], o2[sub]));
-    }
-};
-
-// Q4_0 (gguf_importer.cpp:679-695): record = [d x8][codes x8 of 16 B]; the
-// lane's elements are blocks 2t, 2t+1.
-template <>
-struct Lane<T_Q4_0> {
     static constexpr int kStage = TILE_ROWS * 144;
     uint4 q0, q1;
     __half2 s2[2], o2[2];
@@ -143,33 +105,51 @@ struct Lane<T_Q4_0> {
         const uint4 hd = *reinterpret_cast<const uint4*>(rec);
         q0 = *reinterpret_cast<const uint4*>(rec + 16 + 32 * t);
         q1 = *reinterpret_cast<const uint4*>(rec + 32 + 32 * t);
-        const uint32_t dw = sel4((uint32_t)t, hd);
-        const __half2 neg8 = u2h(0xC800C800u);
+        const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFFu)));
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
+        // Sub-blocks 2t, 2t+1: scale bytes 2t, 2t+1 and nibbles of bytes 8 + 2(t&1) + {0,1}.
+        const uint32_t sbw = ((t < 2 ? hd.y : hd.z) >> (16 * (t & 1))) & 0xFFFFu;
+        const uint32_t ebw = ((hd.w >> (16 * (t & 1))) >> (4 * (t >> 1))) & 0x0F0Fu;
 #pragma unroll
         for (int sub = 0; sub < 2; ++sub) {
-            const uint32_t bits = sub ? (dw >> 16) : (dw & 0xFFFFu);
-            s2[sub] = u2h(bits | (bits << 16));
-            o2[sub] = __hmul2(s2[sub], neg8);  // exact
+            const uint32_t sb = (sbw >> (8 * sub)) & 0xFFu;
+            const uint32_t eb = (ebw >> (8 * sub)) & 0xFu;
+            const int S = (int)(sb & 63u);
+            const int Mn = (int)((sb >> 6) | (eb << 2));
+            s2[sub] = __float2half2_rn(d * (float)S);
+            o2[sub] = __float2half2_rn(-(dmin * (float)Mn));
         }
     }
-    __device__ __forceinline__ void frag(int j, uint32_t& b0, uint32_t& b1) const {
-        const int sub = j >> 3, jj = j & 7;
-        const uint32_t w = word_of(sub ? q1 : q0, jj & 3);
-        const uint32_t t0 = __byte_perm(w, 0u, 0x4140u), t1 = __byte_perm(w, 0u, 0x4342u);
-        __half2 v0, v1;
-        if (jj < 4) {  // elements 0..15 of the block: low nibbles
-            v0 = __hsub2(u2h((t0 & 0x000F000Fu) | 0x64006400u), u2h(0x64006400u));
-            v1 = __hsub2(u2h((t1 & 0x000F000Fu) | 0x64006400u), u2h(0x64006400u));
-        } else {  // elements 16..31: high nibbles
-            v0 = __hsub2(u2h((t0 & 0x00F000F0u) | 0x54005400u), u2h(0x54005400u));
-            v1 = __hsub2(u2h((t1 & 0x00F000F0u) | 0x54005400u), u2h(0x54005400u));
-        }
-        b0 = h2u(__hfma2(v0, s2[sub], o2[sub]));
-        b1 = h2u(__hfma2(v1, s2[sub], o2[sub]));
+    __device__ __forceinline__ void pairs(int m, uint32_t (&p)[4]) const {
+        dq::q4_word_pairs(word_of(m < 4 ? q0 : q1, m & 3), s2[m >> 2], o2[m >> 2], p);
     }
 };
 
-// Q8_0 (gguf_importer.cpp:721-733): record = [d x8][codes x8 of 32 B].
+// Q4_0 (gguf_importer.cpp:679-695): record = [d x8][codes x8 of 16 B]; the
+// slice is blocks 2t, 2t+1.
+template <>
+struct Lane<T_Q4_0> {
+    static constexpr int kStage = TILE_ROWS * 144;
+    uint4 q0, q1;
+    __half2 s2[2], o2[2];
+    __device__ __forceinline__ void load(const uint8_t* st, int row, int t) {
+        const uint8_t* rec = st + row * 144;
+        const uint32_t dw = *reinterpret_cast<const uint32_t*>(rec + 4 * t);
+        q0 = *reinterpret_cast<const uint4*>(rec + 16 + 32 * t);
+        q1 = *reinterpret_cast<const uint4*>(rec + 32 + 32 * t);
+        const __half2 neg8 = u2h(0xC800C800u);
+        s2[0] = u2h((dw & 0xFFFFu) | (dw << 16));
+        s2[1] = u2h((dw >> 16) | (dw & 0xFFFF0000u));
+        o2[0] = __hmul2(s2[0], neg8);  // exact
+        o2[1] = __hmul2(s2[1], neg8);
+    }
+    __device__ __forceinline__ void pairs(int m, uint32_t (&p)[4]) const {
+        dq::q4_word_pairs(word_of(m < 4 ? q0 : q1, m & 3), s2[m >> 2], o2[m >> 2], p);
+    }
+};
+
+// Q8_0 (gguf_importer.cpp:721-733): record = [d x8][codes x8 of 32 B]; the
+// slice is blocks 2t, 2t+1 = code bytes 64t .. 64t+63.
 template <>
 struct Lane<T_Q8_0> {
     static constexpr int kStage = TILE_ROWS * 272;
@@ -177,29 +157,29 @@ struct Lane<T_Q8_0> {
     __half2 s2[2];
     __device__ __forceinline__ void load(const uint8_t* st, int row, int t) {
         const uint8_t* rec = st + row * 272;
-        const uint4 hd = *reinterpret_cast<const uint4*>(rec);
+        const uint32_t dw = *reinterpret_cast<const uint32_t*>(rec + 4 * t);
         const uint4* cv = reinterpret_cast<const uint4*>(rec + 16 + 64 * t);
 #pragma unroll
         for (int i = 0; i < 4; ++i) c[i] = cv[i];
-        const uint32_t dw = sel4((uint32_t)t, hd);
         s2[0] = u2h((dw & 0xFFFFu) | (dw << 16));
         s2[1] = u2h((dw >> 16) | (dw & 0xFFFF0000u));
     }
-    __device__ __forceinline__ void frag(int j, uint32_t& b0, uint32_t& b1) const {
-        const int sub = j >> 3, jj = j & 7;
-        const uint32_t w = word_of(c[2 * sub + (jj >> 2)], jj & 3);
+    __device__ __forceinline__ void pairs(int m, uint32_t (&p)[4]) const {
         // Signed byte b -> f16 1152 + b via (b ^ 0x80) in the mantissa of 1024.
         const __half2 bias = u2h(0x64806480u);
-        const uint32_t t0 = __byte_perm(w, 0u, 0x4140u) ^ 0x64806480u;
-        const uint32_t t1 = __byte_perm(w, 0u, 0x4342u) ^ 0x64806480u;
-        b0 = h2u(__hmul2(__hsub2(u2h(t0), bias), s2[sub]));
-        b1 = h2u(__hmul2(__hsub2(u2h(t1), bias), s2[sub]));
+        const uint32_t w0 = word_of(c[m >> 1], 2 * (m & 1)), w1 = word_of(c[m >> 1], 2 * (m & 1) + 1);
+        const __half2 s = s2[m >> 2];
+        p[0] = h2u(__hmul2(__hsub2(u2h(__byte_perm(w0, 0u, 0x4140u) ^ 0x64806480u), bias), s));
+        p[1] = h2u(__hmul2(__hsub2(u2h(__byte_perm(w0, 0u, 0x4342u) ^ 0x64806480u), bias), s));
+        p[2] = h2u(__hmul2(__hsub2(u2h(__byte_perm(w1, 0u, 0x4140u) ^ 0x64806480u), bias), s));
+        p[3] = h2u(__hmul2(__hsub2(u2h(__byte_perm(w1, 0u, 0x4342u) ^ 0x64806480u), bias), s));
     }
 };
 
 // Q3_K (gguf_importer.cpp:791-833): plane A = [hmask 32][qs 64] at row*96,
-// plane B = [scales 12][d] at 128*96 + row*14.  The lane's elements 64t..64t+63
-// are qs bytes 16t.. and hmask bytes 8t.., in four 16-element scale groups.
+// plane B = [scales 12][d] at 128*96 + row*14.  The slice's elements are qs
+// bytes 16t.. (2 bits each, element e at bits 2(e&3) of byte e/4) and hmask
+// bytes 8t.. (bit e), in four 16-element scale groups.
 template <>
 struct Lane<T_Q3_K> {
     static constexpr int kStage = TILE_ROWS * 110;
@@ -225,28 +205,58 @@ struct Lane<T_Q3_K> {
             s2[gg] = __float2half2_rn(d * (float)(S - 32));
         }
     }
-    __device__ __forceinline__ void frag(int j, uint32_t& b0, uint32_t& b1) const {
-        const uint32_t Q = (word_of(qs, j >> 2) >> (8 * (j & 3))) & 0xFFu;
-        const uint32_t H = (((j >> 3) ? hm.y : hm.x) >> (8 * ((j >> 1) & 3) + 4 * (j & 1))) & 0xFu;
-        const uint32_t q0 = (Q & 3u) | ((H & 1u) << 2), q1 = ((Q >> 2) & 3u) | (((H >> 1) & 1u) << 2);
-        const uint32_t q2 = ((Q >> 4) & 3u) | (((H >> 2) & 1u) << 2), q3 = (Q >> 6) | (((H >> 3) & 1u) << 2);
-        const __half2 bias = u2h(0x64046404u);  // 1028: removes the magic and the -4 offset
-        const __half2 s = s2[j >> 2];
-        b0 = h2u(__hmul2(__hsub2(u2h(q0 | (q1 << 16) | 0x64006400u), bias), s));
-        b1 = h2u(__hmul2(__hsub2(u2h(q2 | (q3 << 16) | 0x64006400u), bias), s));
+    // Elements 8m+4h .. 8m+4h+3: code byte Q (fields at bits 0-1, 2-3, 4-5,
+    // 6-7) and high bits H (bits 0..3).  The 3-bit value u = lo + 4*hb of
+    // each element goes into an f16 mantissa whose unit sits at the field's
+    // bit: (e0, e1) -> (1024 + u0, 256 + u1), (e2, e3) -> (64 + u2, 16 + u3);
+    // subtracting (magic + 4) leaves u - 4 exactly.
+    __device__ __forceinline__ void quad(uint32_t qw, int byte, uint32_t h4, __half2 s, uint32_t* p) const {
+        const uint32_t tq = __byte_perm(qw, 0u, 0x4040u | (byte << 8) | byte);  // Q in bytes 0 and 2
+        const uint32_t v01 = ((tq & 0x000C0003u) | 0x5C006400u) | ((h4 * 0x00080004u) & 0x00100004u);
+        const uint32_t v23 = ((tq & 0x00C00030u) | 0x4C005400u) | ((h4 * 0x00200010u) & 0x01000040u);
+        p[0] = h2u(__hmul2(__hsub2(u2h(v01), u2h(0x5C106404u)), s));  // (1028, 260)
+        p[1] = h2u(__hmul2(__hsub2(u2h(v23), u2h(0x4D005440u)), s));  // (68, 20)
+    }
+    __device__ __forceinline__ void pairs(int m, uint32_t (&p)[4]) const {
+        const uint32_t qw = word_of(qs, m >> 1);
+        const uint32_t hw = (m < 4 ? hm.x : hm.y) >> (8 * (m & 3));
+        const __half2 s = s2[m >> 1];
+        quad(qw, 2 * (m & 1), hw & 0xFu, s, &p[0]);
+        quad(qw, 2 * (m & 1) + 1, (hw >> 4) & 0xFu, s, &p[2]);
     }
 };
 
+// Cluster-wide barrier over all threads of all CTAs of the cluster.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void named_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+constexpr int kGroups = 2;                      // consumer warpgroups of 8 warps
+constexpr int kConsumers = kGroups * kThreads;  // 512
+constexpr int kAll = kConsumers + 32;           // + the producer warp
+constexpr int kMaxCluster = 8;
+
 template <int TYPE, int MT>
 struct Cfg {
+    static constexpr int NT = MT / 8;                   // n8 token tiles
     static constexpr int WB = Lane<TYPE>::kStage;
-    static constexpr int XB = (MT < 16 ? 16 : MT) * 512;  // token slots x 256 f16
-    // Two CTAs per SM when a 3-deep ring fits in half the shared memory.
-    static constexpr int S2 = (112 * 1024) / (WB + XB);
-    static constexpr int CPS = S2 >= 3 ? 2 : 1;
-    static constexpr int S0 = CPS == 2 ? S2 : (220 * 1024) / (WB + XB);
-    static constexpr int S = S0 > 6 ? 6 : S0;
-    static constexpr size_t smem = (size_t)S * (WB + XB);
+    static constexpr int XB = NT * 8 * 32 * 16;         // pieces (n8 tile, m, lane) of 16 B
+    static constexpr int PB = NT * 8 * TILE_ROWS * 4;   // one tile's fp32 partial, [row][token]
+    static constexpr int CMAX = NT >= 4 ? (WB > 20000 ? 2 : 4) : kMaxCluster;
+    static constexpr int RECV = (CMAX - 1) * PB;        // cluster leader: the other ranks' partials
+    static constexpr int COMB = 2 * PB;                 // group 1 -> group 0 hand-over, two tiles deep
+    static constexpr int S0 = (227 * 1024 - 2048 - RECV - COMB) / (WB + XB);
+    static constexpr int S = S0 > 8 ? 8 : S0;
+    static constexpr size_t smem = (size_t)S * (WB + XB) + COMB + RECV;
     static_assert(S >= 3, "pipeline too shallow");
 };
 
@@ -257,17 +267,10 @@ struct MmaParams {
     int64_t M;
     void* y;
     int y_dtype;
-    float* ws;
-    unsigned* counters;
-    int64_t units;
-    int grid;
+    int C;         // CTAs per cluster: the reduction is split C ways inside a cluster
+    int clusters;  // cluster q takes tiles q, q + clusters, ...
+    DeviceStatus* status;
 };
-
-__device__ __forceinline__ int range_begin(int c, int U, int G) { return (int)((int64_t)c * U / G); }
-// The CTA whose range holds unit u.
-__device__ __forceinline__ int owner_of(int u, int U, int G) {
-    return (int)((((int64_t)u + 1) * G + U - 1) / U) - 1;
-}
 
 __device__ __forceinline__ void store_y(void* y, int dt, int64_t i, float v) {
     if (dt == NXQ_F32)
@@ -278,245 +281,296 @@ __device__ __forceinline__ void store_y(void* y, int dt, int64_t i, float v) {
         reinterpret_cast<__nv_bfloat16*>(y)[i] = __float2bfloat16_rn(v);
 }
 
-// The CTA's unit range [u0, u1) as up to four segments, each inside one tile
-// or made of whole tiles: split tiles first, whole tiles after.
-struct Segs {
-    int start[4], len[4];
-    bool whole[4];
-    int n;
-    __device__ void add(int s, int l, bool w) {
-        if (l > 0) {
-            start[n] = s;
-            len[n] = l;
-            whole[n] = w;
-            ++n;
-        }
-    }
-};
+// x piece (16 B) by cp.async; src_bytes = 0 fills the piece with zeros.
+__device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+// Arrives (once, counted in the barrier's expected count) on `bar` when all
+// cp.async this thread issued so far have landed.
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 
-// A walk over the segments, one unit at a time, without divisions except on
-// entering a segment.
-struct Cursor {
-    int seg, left, t, kc;
-    bool whole;
-    __device__ void enter(const Segs& sg, int k, int chunks) {
-        seg = k;
-        if (k >= sg.n) {
-            left = 0;
-            return;
-        }
-        left = sg.len[k];
-        t = sg.start[k] / chunks;
-        kc = sg.start[k] - t * chunks;
-        whole = sg.whole[k];
-    }
-    __device__ void next(const Segs& sg, int chunks) {
-        if (--left > 0) {
-            if (++kc == chunks) {
-                kc = 0;
-                ++t;
-            }
-        } else {
-            enter(sg, seg + 1, chunks);
-        }
-    }
-    // Last unit of a tile's segment: the tile's result is complete here.
-    __device__ bool tile_end(int chunks) const { return left == 1 || kc == chunks - 1; }
-};
-
+// One CTA per SM: warps 0-15 are two consumer groups that take the CTA's units
+// alternately (group = unit parity), warp 16 is the producer.  CTA rank r of
+// cluster q takes chunks [r K/C, (r+1) K/C) of every tile of the cluster, so
+// with C = 1 a CTA owns whole tiles and writes y directly; with C > 1 the
+// cluster owns one tile and ranks 1..C-1 push their partial sums into rank
+// 0's shared memory (one bulk copy each, completing on an mbarrier there),
+// which adds them in rank order: no global-memory round trip and a result
+// that does not depend on timing.
 template <int TYPE, int MT>
-__global__ void __launch_bounds__(kThreads, Cfg<TYPE, MT>::CPS) mma_gemv_kernel(const MmaParams p) {
-    using C = Cfg<TYPE, MT>;
-    constexpr int S = C::S, WB = C::WB, XB = C::XB;
-    extern __shared__ __align__(16) uint8_t smem[];
-    uint8_t* wst = smem;                   // S x WB
-    uint8_t* xst = smem + (size_t)S * WB;  // S x XB
-    __shared__ int s_last;
+__global__ void __launch_bounds__(kAll, 1) mma_gemv_kernel(const MmaParams p) {
+    using Cf = Cfg<TYPE, MT>;
+    constexpr int S = Cf::S, WB = Cf::WB, XB = Cf::XB, NT = Cf::NT, PB = Cf::PB;
+    constexpr int RS = NT * 8;  // floats per row in a partial
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t* wst = smem;                                       // S x WB
+    uint8_t* xst = smem + (size_t)S * WB;                      // S x XB
+    float* comb = reinterpret_cast<float*>(xst + (size_t)S * XB);           // 2 x PB
+    float* recv = reinterpret_cast<float*>(xst + (size_t)S * XB + Cf::COMB);  // (CMAX-1) x PB
+    __shared__ uint64_t full[S];   // unit landed: tile-chunk bytes + 32 producer cp.async arrivals + 1
+    __shared__ uint64_t empty[S];  // the 8 warps of the consuming group are done with the stage
+    __shared__ uint64_t recv_full;  // cluster leader: the C-1 partials have landed
+    __shared__ int s_abort;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, tq = lane & 3;
-    const int U = (int)p.units, G = p.grid, chunks = (int)p.s.chunks;
+    const int C = p.C, rank = (int)(blockIdx.x % (unsigned)C), q = (int)(blockIdx.x / (unsigned)C);
+    const int T = (int)p.s.tiles, Kc = (int)p.s.chunks;
+    const int kc0 = rank * Kc / C, kr = (rank + 1) * Kc / C - kc0;
+    const int ntiles = q < T ? (T - 1 - q) / p.clusters + 1 : 0;
+    const int n = ntiles * kr;
     const int64_t K = p.s.K, N = p.s.N;
     const int M = (int)p.M;
-    const int u0 = range_begin(blockIdx.x, U, G), u1 = range_begin(blockIdx.x + 1, U, G);
-    const int n = u1 - u0;
-
-    Segs sg;
-    sg.n = 0;
-    {
-        const int tf = u0 / chunks, tl = (u1 - 1) / chunks;
-        if (tf == tl) {
-            sg.add(u0, n, u0 == tf * chunks && u1 == (tf + 1) * chunks);
-        } else {
-            const bool wa = u0 == tf * chunks, wb = u1 == (tl + 1) * chunks;
-            const int a_end = (tf + 1) * chunks, b_beg = tl * chunks;
-            if (!wb) sg.add(b_beg, u1 - b_beg, false);
-            sg.add(u0, a_end - u0, wa);
-            sg.add(a_end, b_beg - a_end, true);
-            if (wb) sg.add(b_beg, u1 - b_beg, true);
-        }
-    }
-
-    // Loader: stages the unit under `lc` into stage `stg`.  x is stored as the
-    // mma's A fragments: 16-byte slot (tile16, t4, j, g) holds, for chunk
-    // elements k = 64*t4 + 4*j, the words {x[g][k,k+1], x[g+8][k,k+1],
-    // x[g][k+2,k+3], x[g+8][k+2,k+3]} (g = token % 8 within a 16-token tile),
-    // at slot index (tile16*64 + t4*16 + j)*8 + (g ^ 2*t4) so each 8-lane phase
-    // of the 16-byte fragment loads hits distinct banks.
-    Cursor lc;
-    lc.enter(sg, 0, chunks);
-    auto load_unit = [&](int stg) {
-        const uint8_t* src = p.w + p.s.chunk_offset(lc.t, lc.kc) + 16 * tid;
-        uint8_t* dst = wst + stg * WB + 16 * tid;
-        constexpr int kPieces = WB / 16, kFull = kPieces / kThreads;
-#pragma unroll
-        for (int r = 0; r < kFull; ++r) cp_async16(dst + 16 * kThreads * r, src + 16 * kThreads * r);
-        if (kPieces % kThreads && tid < kPieces % kThreads)
-            cp_async16(dst + 16 * kThreads * kFull, src + 16 * kThreads * kFull);
-        uint32_t* xd = reinterpret_cast<uint32_t*>(xst + stg * XB);
-        const int k0 = lc.kc * CHUNK_K;
-        for (int q = tid; q < M * 128; q += kThreads) {
-            // q -> (token, t4, j, half): one 4-byte pair x[tok][k + 2*half .. +1]
-            const int tok = q >> 7, r = q & 127, t4 = r >> 5, j = (r >> 1) & 15, half = r & 1;
-            const int k = k0 + 64 * t4 + 4 * j + 2 * half;
-            const int gg = tok & 7, up = (tok >> 3) & 1;
-            uint32_t* d = xd + ((((tok >> 4) * 64 + t4 * 16 + j) * 8 + (gg ^ (2 * t4))) << 2) + 2 * half + up;
-            if (k < K)
-                cp_async4(d, p.x + (int64_t)tok * K + k);
-            else
-                *d = 0u;
-        }
-        lc.next(sg, chunks);
-    };
 
     // Token slots at or beyond M are never loaded; zero them once so the
     // fragment loads need no predicate.
-    for (int q = tid; q < S * XB / 16; q += kThreads) reinterpret_cast<uint4*>(xst)[q] = make_uint4(0u, 0u, 0u, 0u);
-    __syncthreads();
-
-    // acc[n8 tile][token tile][c0..c3]; the warp's n8 tiles are rows
-    // 16*warp + g and 16*warp + 8 + g.
-    constexpr int TT = MT < 16 ? 1 : MT / 16;  // 16-token tiles
-    float acc[2][TT][4];
-#pragma unroll
-    for (int st = 0; st < S - 1; ++st) {
-        if (st < n) load_unit(st);
-        cp_commit();
+    for (int i = tid; i < S * XB / 16; i += kAll) reinterpret_cast<uint4*>(xst)[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (tid == 0) {
+        for (int st = 0; st < S; ++st) {
+            ptx::mbar_init(&full[st], 33);
+            ptx::mbar_init(&empty[st], kWarps);
+        }
+        ptx::mbar_init(&recv_full, 1);
+        if (C > 1 && rank == 0)
+            asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&recv_full)),
+                         "r"((uint32_t)((C - 1) * PB))
+                         : "memory");
+        s_abort = 0;
+        ptx::fence_mbar_init();
     }
-    Cursor cc;
-    cc.enter(sg, 0, chunks);
-    bool fresh = true;
-    for (int i = 0; i < n; ++i) {
-        cp_wait<S - 2>();
+    if (C > 1)
+        cluster_sync();  // barriers initialised before any rank pushes to the leader
+    else
         __syncthreads();
-        if (i + S - 1 < n) load_unit((i + S - 1) % S);
-        cp_commit();
+    const ptx::WaitCtl ctl{&s_abort, p.status};
+    // Programmatic dependent launch: the next kernel of the stream may be
+    // scheduled as soon as every CTA of this grid has started; this grid reads
+    // x and writes y only after griddepcontrol.wait (the previous kernel has
+    // completed and its memory is visible).  The weights are immutable once
+    // registered, so the producer requests the first tile-chunks before it.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-        if (fresh) {
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                for (int tt = 0; tt < TT; ++tt)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) acc[nt][tt][e] = 0.0f;
-            fresh = false;
-        }
-
-        // ---- compute on stage i % S ----
-        const int stg = i % S;
-        Lane<TYPE> LA, LB;
-        LA.load(wst + stg * WB, 16 * warp + g, tq);
-        LB.load(wst + stg * WB, 16 * warp + 8 + g, tq);
-        const uint4* xs = reinterpret_cast<const uint4*>(xst + stg * XB) + tq * 128 + (g ^ (2 * tq));
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            uint32_t a0, a1, b0, b1;
-            LA.frag(j, a0, a1);
-            LB.frag(j, b0, b1);
-#pragma unroll
-            for (int tt = 0; tt < TT; ++tt) {
-                const uint4 xa = xs[tt * 512 + j * 8];
-                mma16816(acc[0][tt], xa.x, xa.y, xa.z, xa.w, a0, a1);
-                mma16816(acc[1][tt], xa.x, xa.y, xa.z, xa.w, b0, b1);
+    int w_issued = 0;  // producer lane 0: tile-chunk copies issued
+    if (warp == 2 * kWarps) {
+        // ---- producer: lane 0 issues the tile-chunk bulk copies, all 32
+        // lanes the x pieces: piece (token, t4, m) holds the 8 elements
+        // x[token][k0 + 64 t4 + 8m ..] at index ((token / 8) * 8 + m) * 32 +
+        // 4 (token % 8) + t4.
+        auto w_src = [&](int u) {
+            const int ti = u / kr;
+            return p.w + p.s.chunk_offset(q + (int64_t)ti * p.clusters, kc0 + (u - ti * kr));
+        };
+        const int pre = n < S ? n : S;
+        if (lane == 0)
+            for (int u = 0; u < pre; ++u, ++w_issued) {
+                ptx::mbar_arrive_expect_tx(&full[u], WB);
+                ptx::bulk_g2s(wst + u * WB, w_src(u), WB, &full[u]);
             }
-        }
-
-        // ---- end of this tile's segment: write or hand over the result ----
-        const bool seg_end = cc.tile_end(chunks);
-        const int t = cc.t;
-        const bool whole = cc.whole;
-        cc.next(sg, chunks);
-        if (!seg_end) continue;
-        fresh = true;
-        if (whole) {
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                for (int tt = 0; tt < TT; ++tt)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int tok = 16 * tt + g + (e >> 1) * 8;
-                        const int64_t row = (int64_t)t * TILE_ROWS + 16 * warp + 8 * nt + 2 * tq + (e & 1);
-                        if (tok < M && row < N) store_y(p.y, p.y_dtype, tok * N + row, acc[nt][tt][e]);
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        for (int u = 0; u < n; ++u) {
+            const int stg = u % S;
+            if (u >= S) {
+                int ok = 0;
+                if (lane == 0) {
+                    ok = ptx::mbar_wait(&empty[stg], (uint32_t)(u / S - 1) & 1u, ctl, 32) ? 1 : 0;
+                    if (ok) {
+                        ptx::mbar_arrive_expect_tx(&full[stg], WB);
+                        ptx::bulk_g2s(wst + stg * WB, w_src(u), WB, &full[stg]);
+                        ++w_issued;
                     }
-        } else {
-            const int c = blockIdx.x;
-            const int slot = u0 >= t * chunks ? 0 : 1;  // 0: tile t is where this CTA's range starts
-            float* mine = p.ws + ((size_t)c * 2 + slot) * (kMaxMT * TILE_ROWS);
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                for (int tt = 0; tt < TT; ++tt)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int tok = 16 * tt + g + (e >> 1) * 8;
-                        if (tok < M) mine[tok * TILE_ROWS + 16 * warp + 8 * nt + 2 * tq + (e & 1)] = acc[nt][tt][e];
-                    }
-            __threadfence();
-            __syncthreads();
-            const int cf = owner_of(t * chunks, U, G);
-            const int cl = owner_of((t + 1) * chunks - 1, U, G);
-            if (tid == 0) {
-                const unsigned old = atomicAdd(&p.counters[t], 1u);
-                s_last = (old == (unsigned)(cl - cf)) ? 1 : 0;
-            }
-            __syncthreads();
-            if (s_last) {
-                __threadfence();
-                // Contributors after the first start inside tile t (slot 0); the
-                // first uses slot 0 only if its range starts exactly at the tile.
-                const int first_slot = range_begin(cf, U, G) >= t * chunks ? 0 : 1;
-                for (int q = tid; q < M * TILE_ROWS; q += kThreads) {
-                    const int tok = q >> 7, rr = q & (TILE_ROWS - 1);
-                    float a = 0.0f;
-                    for (int c2 = cf; c2 <= cl; ++c2) {
-                        const int s2 = c2 == cf ? first_slot : 0;
-                        a += __ldcg(p.ws + ((size_t)c2 * 2 + s2) * (kMaxMT * TILE_ROWS) + tok * TILE_ROWS + rr);
-                    }
-                    const int64_t row = (int64_t)t * TILE_ROWS + rr;
-                    if (row < N) store_y(p.y, p.y_dtype, tok * N + row, a);
                 }
-                if (tid == 0) p.counters[t] = 0u;
+                if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) break;
+            }
+            uint4* xd = reinterpret_cast<uint4*>(xst + stg * XB);
+            const int ti = u / kr;
+            const int64_t k0 = (int64_t)(kc0 + u - ti * kr) * CHUNK_K;
+            for (int i = lane; i < M * 32; i += 32) {
+                const int tok = i >> 5, t4 = (i >> 3) & 3, m = i & 7;
+                const int64_t k = k0 + 64 * t4 + 8 * m;
+                cp_async16_zfill(xd + ((tok >> 3) * 8 + m) * 32 + 4 * (tok & 7) + t4,
+                                 p.x + (int64_t)tok * K + (k < K ? k : 0), k < K ? 16u : 0u);
+            }
+            cp_async_arrive(&full[stg]);
+        }
+    } else {
+        // ---- consumers: group gi takes the units of parity gi of each tile ----
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        const int gi = warp >> 3, wg = warp & 7;
+        bool dead = false;
+        for (int ti = 0; ti < ntiles; ++ti) {
+            // acc[n8 token tile][c0..c3]: c0/c1 = row 16wg+g, tokens 8nt+2t,
+            // 8nt+2t+1; c2/c3 = row 16wg+8+g.
+            float acc[NT][4];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[nt][e] = 0.0f;
+            for (int c = gi; c < kr; c += kGroups) {
+                const int u = ti * kr + c, stg = u % S;
+                if (!dead && !ptx::mbar_wait(&full[stg], (uint32_t)(u / S) & 1u, ctl, 31)) dead = true;
+                if (!dead) {
+                    Lane<TYPE> LA, LB;
+                    LA.load(wst + stg * WB, 16 * wg + g, tq);
+                    LB.load(wst + stg * WB, 16 * wg + 8 + g, tq);
+                    const uint4* xs = reinterpret_cast<const uint4*>(xst + stg * XB) + lane;
+#pragma unroll
+                    for (int m = 0; m < 8; ++m) {
+                        uint32_t pa[4], pb[4];
+                        LA.pairs(m, pa);
+                        LB.pairs(m, pb);
+#pragma unroll
+                        for (int nt = 0; nt < NT; ++nt) {
+                            const uint4 xv = xs[(nt * 8 + m) * 32];
+                            mma16816(acc[nt], pa[0], pb[0], pa[1], pb[1], xv.x, xv.y);
+                            mma16816(acc[nt], pa[2], pb[2], pa[3], pb[3], xv.z, xv.w);
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive(&empty[stg]);
+            }
+            // ---- tile end: group 1 hands its partial to group 0 ----
+            float* cb = comb + (ti & 1) * (PB / 4);
+            const int r0 = 16 * wg + g;
+            if (gi == 1) {
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    *reinterpret_cast<float2*>(cb + r0 * RS + 8 * nt + 2 * tq) = make_float2(acc[nt][0], acc[nt][1]);
+                    *reinterpret_cast<float2*>(cb + (r0 + 8) * RS + 8 * nt + 2 * tq) = make_float2(acc[nt][2], acc[nt][3]);
+                }
+            }
+            named_sync(1, kConsumers);
+            if (gi == 1) continue;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const float2 a = *reinterpret_cast<const float2*>(cb + r0 * RS + 8 * nt + 2 * tq);
+                const float2 b = *reinterpret_cast<const float2*>(cb + (r0 + 8) * RS + 8 * nt + 2 * tq);
+                acc[nt][0] += a.x;
+                acc[nt][1] += a.y;
+                acc[nt][2] += b.x;
+                acc[nt][3] += b.y;
+            }
+            const int64_t tile = q + (int64_t)ti * p.clusters;
+            if (C == 1) {
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int tok = 8 * nt + 2 * tq + (e & 1);
+                        const int64_t row = tile * TILE_ROWS + r0 + 8 * (e >> 1);
+                        if (tok < M && row < N) store_y(p.y, p.y_dtype, tok * N + row, acc[nt][e]);
+                    }
+            } else if (rank > 0) {
+                // Push this rank's partial to the leader: stage memory is free
+                // now (every unit has been consumed), so it holds the copy source.
+                float* send = reinterpret_cast<float*>(smem);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    *reinterpret_cast<float2*>(send + r0 * RS + 8 * nt + 2 * tq) = make_float2(acc[nt][0], acc[nt][1]);
+                    *reinterpret_cast<float2*>(send + (r0 + 8) * RS + 8 * nt + 2 * tq) = make_float2(acc[nt][2], acc[nt][3]);
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                named_sync(2, kThreads);
+                if (tid == 0 && !s_abort) {
+                    const uint32_t dst = cluster_addr(recv + (size_t)(rank - 1) * (PB / 4), 0);
+                    const uint32_t bar = cluster_addr(&recv_full, 0);
+                    asm volatile(
+                        "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                            dst),
+                        "r"(smem_u32(send)), "r"((uint32_t)PB), "r"(bar)
+                        : "memory");
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                }
+            } else {
+                // Leader: add the other ranks' partials in rank order.
+                if (tid == 0) ptx::mbar_arrive(&recv_full);
+                // Waits even after an abort (bounded), so that no rank's copy
+                // lands in shared memory that has gone away.
+                bool ok = ptx::mbar_try_wait(&recv_full, 0);
+                const long long t0 = clock64();
+                while (!ok && clock64() - t0 < ptx::kWaitCycles) ok = ptx::mbar_try_wait(&recv_full, 0);
+                if (!ok && lane == 0) ptx::raise_timeout(ctl, 33);
+                if (ok && !s_abort) {
+                    for (int rr = 1; rr < C; ++rr) {
+                        const float* src = recv + (size_t)(rr - 1) * (PB / 4);
+#pragma unroll
+                        for (int nt = 0; nt < NT; ++nt) {
+                            const float2 a = *reinterpret_cast<const float2*>(src + r0 * RS + 8 * nt + 2 * tq);
+                            const float2 b = *reinterpret_cast<const float2*>(src + (r0 + 8) * RS + 8 * nt + 2 * tq);
+                            acc[nt][0] += a.x;
+                            acc[nt][1] += a.y;
+                            acc[nt][2] += b.x;
+                            acc[nt][3] += b.y;
+                        }
+                    }
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int tok = 8 * nt + 2 * tq + (e & 1);
+                            const int64_t row = tile * TILE_ROWS + r0 + 8 * (e >> 1);
+                            if (tok < M && row < N) store_y(p.y, p.y_dtype, tok * N + row, acc[nt][e]);
+                        }
+                }
             }
         }
     }
-    cp_wait<0>();
+
+    __syncthreads();
+    if (s_abort) {
+        // Let the copies still in flight land (bounded) before the CTA's shared
+        // memory goes away: only the last S tile-chunks issued can be pending.
+        cp_wait<0>();
+        if (tid == 2 * kThreads) {
+            for (int u = w_issued > S ? w_issued - S : 0; u < w_issued; ++u) {
+                const long long t0 = clock64();
+                while (!ptx::mbar_try_wait(&full[u % S], (uint32_t)(u / S) & 1u) && clock64() - t0 < ptx::kWaitCycles) {
+                }
+            }
+        }
+    }
 }
 
 bool g_mma_enabled = true;
+int g_sm_count = 0;
 
 template <int TYPE, int MT>
 int set_attr() {
-    using C = Cfg<TYPE, MT>;
+    using Cf = Cfg<TYPE, MT>;
     cudaError_t e = cudaFuncSetAttribute(mma_gemv_kernel<TYPE, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)C::smem);
+                                         (int)Cf::smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute (mma_gemv)");
     return NXQ_OK;
 }
 
+// Split of the reduction across a cluster: C = 1 (whole tiles per CTA, one
+// wave of at most one CTA per SM, several tiles per CTA beyond that) or, when
+// the weight has fewer tiles than SMs, C ranks per tile with one tile per
+// cluster.  Picks the C with the fewest tile-chunks per CTA (the smallest C
+// among equals).
+void pick_split(const TiledShape& s, int cmax, int* C, int* clusters) {
+    const int64_t T = s.tiles, Kc = s.chunks, P = g_sm_count;
+    int best_c = 1;
+    int64_t best = ((T + P - 1) / P) * Kc;
+    for (int c = 2; c <= cmax && c <= Kc; c *= 2) {
+        if (T * c > P) break;
+        const int64_t cost = (Kc + c - 1) / c;
+        if (cost < best) {
+            best = cost;
+            best_c = c;
+        }
+    }
+    *C = best_c;
+    *clusters = (int)(best_c == 1 ? (T < P ? T : P) : T);
+}
+
 template <int TYPE, int MT>
-int launch(const Weight* w, const __half* x, void* y, int y_dtype, int64_t M, StreamScratch* sc, int grid,
-           cudaStream_t st) {
+int launch(const Weight* w, const __half* x, void* y, int y_dtype, int64_t M, cudaStream_t st) {
+    using Cf = Cfg<TYPE, MT>;
     MmaParams p;
     p.w = w->dev;
     p.s = w->shape;
@@ -524,12 +578,25 @@ int launch(const Weight* w, const __half* x, void* y, int y_dtype, int64_t M, St
     p.M = M;
     p.y = y;
     p.y_dtype = y_dtype;
-    p.ws = sc->ws;
-    p.counters = sc->counters;
-    p.units = w->shape.tiles * w->shape.chunks;
-    p.grid = grid;
-    mma_gemv_kernel<TYPE, MT><<<grid, kThreads, Cfg<TYPE, MT>::smem, st>>>(p);
-    cudaError_t e = cudaGetLastError();
+    pick_split(w->shape, Cf::CMAX, &p.C, &p.clusters);
+    p.status = context_status();
+    // Launched with programmatic stream serialization (see the kernel's
+    // griddepcontrol.wait): it may start while the previous kernel drains.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(p.clusters * p.C));
+    cfg.blockDim = dim3(kAll);
+    cfg.dynamicSmemBytes = Cf::smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)p.C;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = p.C > 1 ? 2 : 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, mma_gemv_kernel<TYPE, MT>, p);
     note_launches(1);
     if (e != cudaSuccess) return cuda_fail(e, "mma_gemv launch");
     return NXQ_OK;
@@ -537,22 +604,12 @@ int launch(const Weight* w, const __half* x, void* y, int y_dtype, int64_t M, St
 
 bool type_ok(int type) { return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || type == T_Q3_K; }
 
-int cps_of(int type, int mt) {
-#define NXQ_CPS(T) \
-    if (type == T) return mt == 8 ? Cfg<T, 8>::CPS : mt == 16 ? Cfg<T, 16>::CPS : Cfg<T, 32>::CPS;
-    NXQ_CPS(T_Q4_K)
-    NXQ_CPS(T_Q4_0)
-    NXQ_CPS(T_Q8_0)
-    NXQ_CPS(T_Q3_K)
-#undef NXQ_CPS
-    return 1;
-}
-
 }  // namespace
 
 int mma_init(int) {
     const char* env = getenv("NXQ_DECODE_KERNEL");
     g_mma_enabled = !(env && env[0] && env[0] != 'm');  // "tc" / "simt" select another decode kernel
+    g_sm_count = context_sm_count();
     int rc;
 #define NXQ_ATTR(T)                                       \
     if ((rc = set_attr<T, 8>()) != NXQ_OK) return rc;  \
@@ -566,10 +623,8 @@ int mma_init(int) {
     return NXQ_OK;
 }
 
-// Batches of up to 8 tokens: at 9..32 tokens the tcgen05 kernel, whose
-// per-instruction cost does not grow with N, is faster (measured).
 bool mma_supported(const TiledShape& s, int64_t M) {
-    return g_mma_enabled && type_ok(s.type) && M >= 1 && M <= 8;
+    return g_mma_enabled && type_ok(s.type) && M >= 1 && M <= kMaxMT;
 }
 
 void mma_kernel_name(const TiledShape& s, int64_t M, char* buf, size_t n) {
@@ -579,27 +634,22 @@ void mma_kernel_name(const TiledShape& s, int64_t M, char* buf, size_t n) {
 int mma_qmatmul(const Weight* w, const void* x, int x_dtype, void* y, int y_dtype, int64_t M, cudaStream_t st) {
     const TiledShape& s = w->shape;
     if (!mma_supported(s, M)) return NXQ_ERR_UNSUPPORTED;
-    const int64_t units = s.tiles * s.chunks;
     const int mt = M <= 8 ? 8 : M <= 16 ? 16 : 32;
-    const int cps = cps_of(s.type, mt);
-    int grid = cps * context_sm_count();
-    if (grid > units) grid = (int)units;
     const bool direct = x_dtype == NXQ_F16 && ((uintptr_t)x % 16) == 0;
-    StreamScratch* sc = nullptr;
-    int rc = scratch_for(st, (size_t)grid * 2 * kMaxMT * TILE_ROWS, (size_t)s.tiles,
-                         direct ? 0 : (size_t)(M * s.K), &sc);
-    if (rc) return rc;
     const __half* xh = static_cast<const __half*>(x);
     if (!direct) {
+        StreamScratch* sc = nullptr;
+        int rc = scratch_for(st, 0, 0, (size_t)(M * s.K), &sc);
+        if (rc) return rc;
         cudaError_t e = launch_to_half(x, x_dtype, sc->xh, M * s.K, st);
         if (e != cudaSuccess) return cuda_fail(e, "to_half launch");
         xh = sc->xh;
     }
-#define NXQ_CASE(T)                                                        \
-    case T:                                                                \
-        return mt == 8    ? launch<T, 8>(w, xh, y, y_dtype, M, sc, grid, st)  \
-               : mt == 16 ? launch<T, 16>(w, xh, y, y_dtype, M, sc, grid, st) \
-                          : launch<T, 32>(w, xh, y, y_dtype, M, sc, grid, st);
+#define NXQ_CASE(T)                                                \
+    case T:                                                        \
+        return mt == 8    ? launch<T, 8>(w, xh, y, y_dtype, M, st)  \
+               : mt == 16 ? launch<T, 16>(w, xh, y, y_dtype, M, st) \
+                          : launch<T, 32>(w, xh, y, y_dtype, M, st);
     switch (s.type) {
         NXQ_CASE(T_Q4_K)
         NXQ_CASE(T_Q4_0)

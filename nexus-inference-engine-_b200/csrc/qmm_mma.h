@@ -5,6 +5,7 @@
 namespace nxq {
 
 int context_sm_count();
+DeviceStatus* context_status();
 
 // Kernel attributes; reads NXQ_DECODE_KERNEL ("tc" or "simt" select another
 // decode kernel, for comparisons).

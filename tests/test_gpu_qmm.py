@@ -179,16 +179,14 @@ def test_qmm_errors(gpu):
 
 @pytest.mark.parametrize("t", MAIN_TYPES, ids=lambda t: NAMES[t])
 def test_decode_kernel_is_selected(gpu, t):
-    """The block types of the benchmark configs run decode batches of up to 8
-    tokens on the register-fragment mma.sync kernel and 9..32 tokens on the
-    tcgen05 kernel; larger M and the other types run the exact CUDA-core path."""
+    """The block types of the benchmark configs run decode batches (up to 32
+    tokens) on the register-fragment mma.sync kernel, in variants for 8, 16
+    and 32 token columns."""
     blocks = synth.make_blocks(t, 256, 1024, seed=1)
     w = gpu.Weight.register(blocks, t, 256, 1024)
     try:
-        for M in (1, 4, 8):
-            assert gpu.kernel_name(w, M) == f"mma_gemv<{NAMES[t]},m8>"
-        for M, nt in ((9, 16), (16, 16), (17, 32), (32, 32)):
-            assert gpu.kernel_name(w, M) == f"tc_gemv<{NAMES[t]},n{nt}>"
+        for M, mt in ((1, 8), (4, 8), (8, 8), (9, 16), (16, 16), (17, 32), (32, 32)):
+            assert gpu.kernel_name(w, M) == f"mma_gemv<{NAMES[t]},m{mt}>"
     finally:
         w.release()
 
