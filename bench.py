@@ -25,9 +25,8 @@ cpu_baseline = the reference's CPU path (its own decoders from
              dot products) on a bounded row sample of the same workload
 
 With --gpus N > 1 (torchrun, one process per GPU) every rank runs the same
-per-GPU workload (weak scaling); the tensor-parallel config-5 layer is
-reported as "tp".  --impl reference times the reference CPU path instead, on
-rank 0 only.
+per-GPU workload on its own weights (weak scaling).  --impl reference times
+the reference CPU path instead, on rank 0 only.
 """
 from __future__ import annotations
 
@@ -248,18 +247,29 @@ def run_reference_arm(args, rank, world):
 
 
 # ---------------------------------------------------------------- GPU arm
-def traffic_lookup(kernel: str, shape: str):
+def traffic_lookup(kernel: str, shape_launches: dict):
+    """DRAM bytes per launch of `kernel` (dram__bytes_read.sum + write.sum from
+    one ncu capture per shape, profiles/dram_traffic.txt), averaged over the
+    shapes it ran with in proportion to their launches; None if a shape has no
+    capture."""
     p = ROOT / "profiles" / "dram_traffic.txt"
     if not p.exists():
         return None
+    table = {}
     for ln in p.read_text().splitlines():
         parts = ln.split()
-        if len(parts) >= 3 and not ln.startswith("#") and parts[0] == kernel and parts[1] == shape:
+        if len(parts) >= 3 and not ln.startswith("#"):
             try:
-                return float(parts[2])
+                table[(parts[0], parts[1])] = float(parts[2])
             except ValueError:
-                return None
-    return None
+                pass
+    total, n = 0.0, 0
+    for shape, launches in shape_launches.items():
+        if (kernel, shape) not in table:
+            return None
+        total += table[(kernel, shape)] * launches
+        n += launches
+    return total / n if n else None
 
 
 def run_gpu_arm(args, rank, world, local):
@@ -309,8 +319,9 @@ def run_gpu_arm(args, rank, world, local):
         with torch.cuda.graph(g, stream=stream):
             step_calls(r)
         step_graphs.append(g)
-    for r in range(args.warmup):
-        step_graphs[r % reps].replay()
+    with torch.cuda.stream(stream):
+        for r in range(args.warmup):
+            step_graphs[r % reps].replay()
     torch.cuda.synchronize()
 
     # --- timed region: K step-graph replays ------------------------------------
@@ -345,7 +356,9 @@ def run_gpu_arm(args, rank, world, local):
         with torch.cuda.graph(g, stream=stream):
             for r in range(reps):
                 nxq.qmatmul(weights[name][r], xs[M][K], out=ys[M][N], stream=stream)
-        g.replay()
+        with torch.cuda.stream(stream):
+            g.replay()  # warm, on the timing stream and finished before timing
+        torch.cuda.synchronize()
         a_ev, b_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
             a_ev.record(stream)
@@ -356,11 +369,12 @@ def run_gpu_arm(args, rank, world, local):
         n_l = 3 * reps
         d = a_ev.elapsed_time(b_ev)
         kname = names[(name, M)]
-        k = per_kernel.setdefault(kname, {"ms": 0.0, "bytes": 0, "launches": 0, "shapes": set()})
+        k = per_kernel.setdefault(kname, {"ms": 0.0, "bytes": 0, "launches": 0, "shapes": {}})
         k["ms"] += d
         k["bytes"] += call_bytes(M, K, N) * n_l
         k["launches"] += n_l
-        k["shapes"].add(f"K{K}xN{N}xM{M}")
+        shp = f"K{K}xN{N}xM{M}"
+        k["shapes"][shp] = k["shapes"].get(shp, 0) + n_l
         c = per_case.setdefault(f"{name}_M{M}", {"ms": 0.0, "bytes": 0})
         c["ms"] += d
         c["bytes"] += call_bytes(M, K, N) * n_l
@@ -369,13 +383,14 @@ def run_gpu_arm(args, rank, world, local):
     total_k = sum(k["ms"] for k in per_kernel.values())
     dom_name, dom = max(per_kernel.items(), key=lambda kv: kv[1]["ms"])
     achieved = dom["bytes"] / (dom["ms"] / 1e3) / 1e9
-    dom_shape = sorted(dom["shapes"])[0] if len(dom["shapes"]) == 1 else "mixed"
-    traffic = traffic_lookup(dom_name, dom_shape)
+    traffic = traffic_lookup(dom_name, dom["shapes"])
     roofline = {"bound": "hbm", "kernel": dom_name, "achieved": achieved, "peak": pk["hbm_gbs"],
                 "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": traffic,
                 "peak_source": f"{pk_kind} hbm_gbs", "share_of_step": dom["ms"] / total_k,
                 "algorithmic_bytes_per_launch": dom["bytes"] / dom["launches"],
-                "avg_launch_us": dom["ms"] / dom["launches"] * 1e3}
+                "avg_launch_us": dom["ms"] / dom["launches"] * 1e3, "shapes": sorted(dom["shapes"]),
+                "timing": "CUDA events on the launching stream around graph replays of back-to-back "
+                          "launches of each shape (PDL overlap between launches included)"}
     cases_out = {k: round(v["bytes"] / (v["ms"] / 1e3) / 1e9, 1) for k, v in per_case.items()}
     kernels_out = {k: {"launches": v["launches"], "ms": round(v["ms"], 3),
                        "GB/s": round(v["bytes"] / (v["ms"] / 1e3) / 1e9, 1),
@@ -439,7 +454,8 @@ def run_gpu_arm(args, rank, world, local):
             with torch.cuda.graph(g, stream=stream):
                 for _ in range(iters):
                     nxq.qmatmul(w, x, out=y, stream=stream)
-            g.replay()
+            with torch.cuda.stream(stream):
+                g.replay()
             torch.cuda.synchronize()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             barrier(world)
