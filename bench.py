@@ -20,6 +20,12 @@ roofline   = the dominant kernel's algorithmic GB/s against the measured HBM
              copy bandwidth in MEASURED_PEAKS.json
 prefill    = BASELINE.json config 4: Q4_K GEMM at M in {512, 2048, 8192},
              K=4096, N=14336, bf16 activations and bf16 output, TFLOP/s
+config1 / config3 = BASELINE.json configs 1 (Q4_0 GEMV M=1, 4096x4096, fp32 x)
+             and 3 (Q8_0 GEMV M=1 over the 7 projections of a Llama-3-8B layer),
+             one GPU
+tp_config5 = BASELINE.json config 5 (Q3_K 405B-shaped layer, M in {1,8,32}),
+             tensor-parallel over the launched ranks (NCCL allreduce after the
+             row-split projections); max over ranks
 cpu_baseline = the reference's CPU path (its own decoders from
              oracle/_ref when built, else the oracle restatement, plus fp32
              dot products) on a bounded row sample of the same workload
@@ -272,6 +278,196 @@ def traffic_lookup(kernel: str, shape_launches: dict):
     return total / n if n else None
 
 
+def graph_time_ms(issue, stream, replays: int = 3) -> float:
+    """Capture `issue()` (launches on `stream`) in a CUDA graph, replay it once
+    to warm up, then time `replays` replays with CUDA events on `stream`;
+    returns ms per replay."""
+    import torch
+
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        issue()
+    with torch.cuda.stream(stream):
+        g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        a.record(stream)
+        for _ in range(replays):
+            g.replay()
+        b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / replays
+    del g
+    return ms
+
+
+def replicas_for(nbytes: int) -> int:
+    """Weight copies whose total exceeds 4x L2, so back-to-back calls stream from HBM."""
+    return max(2, -(-4 * L2_BYTES // nbytes) + 1)
+
+
+def bench_config1(dev, stream, pk) -> dict:
+    """Q4_0 GEMV, M=1, K=N=4096, fp32 x and y."""
+    import torch
+
+    import nxq
+    from nxq import synth
+
+    K = N = 4096
+    blocks = synth.make_blocks(2, N, K, seed=1001)
+    wb = N * (K // 32) * 18
+    R = replicas_for(wb)
+    ws = [nxq.Weight.register(blocks, 2, N, K) for _ in range(R)]
+    x = torch.randn(1, K, generator=torch.Generator().manual_seed(11), dtype=torch.float32).to(dev)
+    y = torch.empty(1, N, dtype=torch.float32, device=dev)
+
+    def issue():
+        for w in ws:
+            nxq.qmatmul(w, x, out=y, stream=stream)
+
+    with torch.cuda.stream(stream):
+        issue()
+    stream.synchronize()
+    ms = graph_time_ms(issue, stream) / R
+    nb = wb + K * 4 + N * 4
+    out = {"workload": "BASELINE config 1: Q4_0 GEMV M=1 K=N=4096, fp32 x (converted to f16 in the call), fp32 y",
+           "kernel": nxq.kernel_name(ws[0], 1, nxq.F32, nxq.F32), "us_per_call": ms * 1e3,
+           "GB/s": nb / (ms / 1e3) / 1e9, "frac_of_hbm": nb / (ms / 1e3) / 1e9 / pk["hbm_gbs"],
+           "replicas": R}
+    for w in ws:
+        w.release()
+    return out
+
+
+def bench_config3(dev, stream, pk) -> dict:
+    """Q8_0 GEMV M=1 over the 7 projections of a Llama-3-8B layer."""
+    import torch
+
+    import nxq
+    from nxq import synth
+
+    projs = [("q", 4096, 4096), ("k", 4096, 1024), ("v", 4096, 1024), ("o", 4096, 4096),
+             ("gate", 4096, 14336), ("up", 4096, 14336), ("down", 14336, 4096)]  # name, K, N
+    layer_bytes = sum(N * (K // 32) * 34 for _, K, N in projs)
+    L = replicas_for(layer_bytes)
+    xs = {K: torch.randn(1, K, generator=torch.Generator().manual_seed(K), dtype=torch.float32)
+          .to(torch.float16).to(dev) for K in (4096, 14336)}
+    ys = {N: torch.empty(1, N, dtype=torch.float32, device=dev) for N in (1024, 4096, 14336)}
+    per = {}
+    layer = {name: [] for name, _, _ in projs}
+    for i, (name, K, N) in enumerate(projs):
+        blocks = synth.make_blocks(8, N, K, seed=3000 + i)
+        wb = N * (K // 32) * 34
+        R = max(L, replicas_for(wb))
+        ws = [nxq.Weight.register(blocks, 8, N, K) for _ in range(R)]
+        del blocks
+
+        def issue(ws=ws, K=K, N=N):
+            for w in ws:
+                nxq.qmatmul(w, xs[K], out=ys[N], stream=stream)
+
+        with torch.cuda.stream(stream):
+            issue()
+        stream.synchronize()
+        ms = graph_time_ms(issue, stream) / R
+        nb = wb + K * 2 + N * 4
+        per[name] = {"us": round(ms * 1e3, 2), "GB/s": round(nb / (ms / 1e3) / 1e9, 1)}
+        layer[name] = ws[:L]
+        for w in ws[L:]:
+            w.release()
+
+    def issue_layer():
+        for r in range(L):
+            for name, K, N in projs:
+                nxq.qmatmul(layer[name][r], xs[K], out=ys[N], stream=stream)
+
+    ms = graph_time_ms(issue_layer, stream) / L
+    nb = layer_bytes + sum(K * 2 + N * 4 for _, K, N in projs)
+    out = {"workload": "BASELINE config 3: Q8_0 GEMV M=1, the 7 projections of a Llama-3-8B layer "
+                       "(q/o 4096x4096, k/v 4096->1024, gate/up 4096->14336, down 14336->4096), f16 x, fp32 y",
+           "kernel": nxq.kernel_name(layer["q"][0], 1), "per_projection": per,
+           "layer_us": ms * 1e3, "layer_GB/s": nb / (ms / 1e3) / 1e9,
+           "layer_frac_of_hbm": nb / (ms / 1e3) / 1e9 / pk["hbm_gbs"], "layer_replicas": L}
+    for ws in layer.values():
+        for w in ws:
+            w.release()
+    return out
+
+
+def bench_tp_layer(dev, stream, pk, rank: int, world: int) -> dict:
+    """one Llama-3.1-405B-shaped layer with Q3_K weights
+    (hidden 16384, FFN 53248, 128 query / 8 KV heads of dim 128), decode M in
+    {1, 8, 32}, tensor-parallel over the `world` ranks: q/k/v/gate/up split by
+    column (each rank holds N/world rows), o/down split by row (K/world of every
+    row) and summed with the library's NCCL allreduce.  Each rank generates its
+    own shard (synthetic data of the config's distribution).  The timed step is
+    the layer's 7 matmuls + 2 allreduces (attention and SwiGLU are not part of
+    the path), captured in one CUDA graph; time = max over ranks."""
+    import torch
+
+    import nxq
+    from nxq import synth
+
+    Q3 = 11
+    H, F, KV = 16384, 53248, 1024
+    projs = [("q", H, H, 0), ("k", H, KV, 0), ("v", H, KV, 0), ("o", H, H, 1),
+             ("gate", H, F, 0), ("up", H, F, 0), ("down", F, H, 1)]  # name, K, N, split (0 col, 1 row)
+    loc = []
+    for name, K, N, split in projs:
+        n_l, k_l = (N // world, K) if split == 0 else (N, K // world)
+        loc.append((name, k_l, n_l, split))
+    shard_bytes = sum(n * (k // 256) * 110 for _, k, n, _ in loc)
+    R = max(1, -(-4 * L2_BYTES // shard_bytes))
+    if world > 1:
+        import torch.distributed as dist
+
+        uid = [nxq.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        nxq.tp_init(rank, world, uid[0])
+    weights = {}
+    for i, (name, k_l, n_l, split) in enumerate(loc):
+        blocks = synth.make_blocks(Q3, n_l, k_l, seed=5000 + 97 * i + rank)
+        weights[name] = [nxq.Weight.register(blocks, Q3, n_l, k_l) for _ in range(R)]
+        del blocks
+    cases = {}
+    for M in (1, 8, 32):
+        x = {k: torch.randn(M, k, generator=torch.Generator().manual_seed(M + k), dtype=torch.float32)
+             .to(torch.float16).to(dev) for k in {k_l for _, k_l, _, _ in loc}}
+        y = {(name, n_l): torch.empty(M, n_l, dtype=torch.float32, device=dev) for name, _, n_l, _ in loc}
+
+        def issue(M=M, x=x, y=y):
+            for r in range(R):
+                for name, k_l, n_l, split in loc:
+                    w = weights[name][r]
+                    if world > 1:
+                        nxq.tp_qmatmul(w, x[k_l], y[(name, n_l)], nxq.SPLIT_ROW if split else nxq.SPLIT_COL,
+                                       stream=stream)
+                    else:
+                        nxq.qmatmul(w, x[k_l], out=y[(name, n_l)], stream=stream)
+
+        with torch.cuda.stream(stream):
+            issue()
+        stream.synchronize()
+        barrier(world)
+        ms = max_over_ranks(graph_time_ms(issue, stream) / R, world)
+        total_b = sum(N * (K // 256) * 110 for _, K, N, _ in projs)
+        cases[f"M{M}"] = {"us_per_layer": round(ms * 1e3, 2),
+                          "GB/s": round(total_b / (ms / 1e3) / 1e9, 1),
+                          "frac_of_hbm_per_gpu": round(total_b / world / (ms / 1e3) / 1e9 / pk["hbm_gbs"], 3)}
+        del x, y
+    for ws in weights.values():
+        for w in ws:
+            w.release()
+    if world > 1:
+        nxq.tp_shutdown()
+    return {"workload": "BASELINE config 5: Llama-3.1-405B-shaped layer, Q3_K, decode, 7 projections + "
+                        "2 allreduces per step", "tp": world, "cases": cases,
+            "layer_weight_bytes": sum(N * (K // 256) * 110 for _, K, N, _ in projs),
+            "shard_bytes_per_gpu": shard_bytes, "replicas": R,
+            "timing": "CUDA graph of R layer steps, CUDA events, max over ranks"}
+
+
 def run_gpu_arm(args, rank, world, local):
     import torch
 
@@ -477,6 +673,15 @@ def run_gpu_arm(args, rank, world, local):
         prefill["workload"] = "BASELINE config 4: Q4_K GEMM K=4096 N=14336, bf16 x, bf16 y, fp32 accumulate"
         prefill["peak_source"] = f"{pk_kind} bf16_tflops / bf16_tflops_sustained"
 
+    # --- configs 1 and 3 (one GPU), config 5 (tensor parallel over the ranks) -------
+    extra = {}
+    if not args.no_configs:
+        if world == 1:
+            extra["config1"] = bench_config1(dev, stream, pk)
+            extra["config3"] = bench_config3(dev, stream, pk)
+        extra["tp_config5"] = bench_tp_layer(dev, stream, pk, rank, world)
+        torch.cuda.empty_cache()
+
     # --- CPU baseline (rank 0, N=1) -------------------------------------------------
     cpu = None
     if world == 1 and not args.no_cpu:
@@ -500,6 +705,7 @@ def run_gpu_arm(args, rank, world, local):
             "gpu_launches": launches, "clocks": clk, "e2e": e2e, "prefill": prefill,
             "cpu_baseline": cpu, "nominal_hbm_frac": value / world / 8000.0,
         }
+        line.update(extra)
         print(json.dumps(line), flush=True)
     return 0
 
@@ -513,6 +719,7 @@ def main() -> int:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip configs 1, 3 and 5")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
     if args.warmup < 3:

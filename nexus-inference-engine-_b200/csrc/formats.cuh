@@ -169,16 +169,13 @@ __host__ __device__ inline int q4_gguf_code(int type, const uint8_t* g, int e) {
     return (e & 1) ? (g[e >> 1] >> 4) : (g[e >> 1] & 15);
 }
 
-// Writes the 16 code bytes of one 32-element group in the tiled order.
-__host__ __device__ inline void q4_reorder_group(int type, const uint8_t* gguf, uint8_t* out) {
-    uint8_t b[16];
-    for (int i = 0; i < 16; ++i) b[i] = 0;
-    for (int e = 0; e < 32; ++e) {
-        int byte, shift;
-        q4_code_pos(e, &byte, &shift);
-        b[byte] = (uint8_t)(b[byte] | (q4_gguf_code(type, gguf, e) << shift));
-    }
-    for (int i = 0; i < 16; ++i) out[i] = b[i];
+// Byte `ob` (0..15) of a 32-element group in the tiled order: byte 4w + k
+// holds elements 8w + {0,4,1,5}[k] (low nibble) and 8w + {2,6,3,7}[k] (high),
+// the inverse of q4_code_pos.
+__host__ __device__ inline uint8_t q4_tiled_byte(int type, const uint8_t* gguf, int ob) {
+    const int w = ob >> 2, k = ob & 3;
+    const int lo = 8 * w + ((k & 1) << 2) + (k >> 1), hi = lo + 2;
+    return (uint8_t)(q4_gguf_code(type, gguf, lo) | (q4_gguf_code(type, gguf, hi) << 4));
 }
 
 __device__ __forceinline__ int q4_tiled_code(const uint8_t* g, int e) {

@@ -5,42 +5,52 @@
 
 namespace nxq {
 
-// One thread per (row, block): copies the block's byte segments to their
-// tiled positions.  `src` holds `rows` rows of `src_row_blocks` blocks; blocks
-// [blk0, blk0 + K/QK) of each source row become row (row0 + i) of the weight.
-// (The offsets let a tensor-parallel rank take a column slice of each row.)
+// One warp per (row, block): the lanes copy the block's byte segments to their
+// tiled positions (consecutive lanes, consecutive bytes) and, for Q4_0 / Q4_K,
+// write the code bytes in the tiled order.  `src` holds `rows` rows of
+// `src_row_blocks` blocks; blocks [blk0, blk0 + K/QK) of each source row become
+// row (row0 + i) of the weight.  (The offsets let a tensor-parallel rank take a
+// column slice of each row.)
 __global__ void repack_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
                               TiledShape s, int64_t row0, int64_t rows, int64_t blk0,
                               int64_t src_row_blocks) {
     const int64_t kb = s.K / s.g.qk;  // blocks per destination row
     const int64_t total = rows * kb;
     const int per_chunk = CHUNK_K / s.g.qk;
-    for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
-         idx += (int64_t)gridDim.x * blockDim.x) {
-        int64_t i = idx / kb, b = idx % kb;
-        int64_t n = row0 + i;
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t idx = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; idx < total; idx += nwarps) {
+        const int64_t i = idx / kb, b = idx - (idx / kb) * kb;
+        const int64_t n = row0 + i;
         const uint8_t* blk = src + (i * src_row_blocks + blk0 + b) * s.g.bb;
-        int64_t tile = n / TILE_ROWS, r = n % TILE_ROWS;
-        int64_t chunk = b / per_chunk, j = b % per_chunk;
+        const int64_t tile = n / TILE_ROWS, r = n % TILE_ROWS;
+        const int64_t chunk = b / per_chunk, j = b % per_chunk;
         uint8_t* base = dst + s.chunk_offset(tile, chunk);
         Segment seg[3];
-        int ns = block_segments(s.type, (int)r, (int)j, seg);
+        const int ns = block_segments(s.type, (int)r, (int)j, seg);
+        // Bytes [c0, c1) of the block are 4-bit codes stored in the tiled order.
+        const int c0 = s.type == T_Q4_0 ? 2 : s.type == T_Q4_K ? 16 : s.g.bb;
+        const int c1 = s.type == T_Q4_0 ? 18 : s.type == T_Q4_K ? 144 : s.g.bb;
         for (int q = 0; q < ns; ++q)
-            for (int t = 0; t < seg[q].len; ++t) base[seg[q].dst + t] = blk[seg[q].src + t];
-        // 4-bit codes go in the tiled order (formats.cuh, q4_code_pos).
-        if (s.type == T_Q4_0) {
-            q4_reorder_group(T_Q4_0, blk + 2, base + seg[1].dst);
-        } else if (s.type == T_Q4_K) {
-            for (int g = 0; g < 8; ++g) q4_reorder_group(T_Q4_K, blk + 16 + 16 * g, base + seg[0].dst + 16 + 16 * g);
-        }
+            for (int t = lane; t < seg[q].len; t += 32) {
+                const int sb = seg[q].src + t;
+                uint8_t v;
+                if (sb >= c0 && sb < c1) {
+                    const int g = (sb - c0) >> 4;
+                    v = q4_tiled_byte(s.type, blk + c0 + 16 * g, (sb - c0) & 15);
+                } else {
+                    v = blk[sb];
+                }
+                base[seg[q].dst + t] = v;
+            }
     }
 }
 
 cudaError_t launch_repack(const uint8_t* src, uint8_t* dst, const TiledShape& s, int64_t row0,
                           int64_t rows, int64_t blk0, int64_t src_row_blocks, cudaStream_t st) {
-    int64_t total = rows * (s.K / s.g.qk);
-    int64_t grid = (total + 255) / 256;
-    if (grid > 65535 * 8) grid = 65535 * 8;
+    const int64_t total = rows * (s.K / s.g.qk);  // blocks, one warp each
+    int64_t grid = (total + 7) / 8;
+    if (grid > 148 * 64) grid = 148 * 64;
     if (grid < 1) grid = 1;
     repack_kernel<<<(unsigned)grid, 256, 0, st>>>(src, dst, s, row0, rows, blk0, src_row_blocks);
     note_launches(1);
