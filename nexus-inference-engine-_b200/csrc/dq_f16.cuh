@@ -22,15 +22,22 @@ __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__
 template <int TYPE>
 struct Group;
 
+// (a & b) | c in one LOP3 (truth table 0xEA).
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
 // Four f16 pairs of a code word in the tiled 4-bit order (formats.cuh,
 // q4_code_pos): elements (8w, 8w+1) .. (8w+6, 8w+7) as fl16(q * s + o).
 __device__ __forceinline__ void q4_word_pairs(uint32_t w, __half2 s2, __half2 o2, uint32_t* o) {
     const __half2 m_lo = u2h(0x64006400u), m_hi = u2h(0x54005400u);  // 1024, 64
     const uint32_t w8 = w >> 8;
-    o[0] = h2u(__hfma2(__hsub2(u2h((w & 0x000F000Fu) | 0x64006400u), m_lo), s2, o2));
-    o[1] = h2u(__hfma2(__hsub2(u2h((w & 0x00F000F0u) | 0x54005400u), m_hi), s2, o2));
-    o[2] = h2u(__hfma2(__hsub2(u2h((w8 & 0x000F000Fu) | 0x64006400u), m_lo), s2, o2));
-    o[3] = h2u(__hfma2(__hsub2(u2h((w8 & 0x00F000F0u) | 0x54005400u), m_hi), s2, o2));
+    o[0] = h2u(__hfma2(__hsub2(u2h(and_or(w, 0x000F000Fu, 0x64006400u)), m_lo), s2, o2));
+    o[1] = h2u(__hfma2(__hsub2(u2h(and_or(w, 0x00F000F0u, 0x54005400u)), m_hi), s2, o2));
+    o[2] = h2u(__hfma2(__hsub2(u2h(and_or(w8, 0x000F000Fu, 0x64006400u)), m_lo), s2, o2));
+    o[3] = h2u(__hfma2(__hsub2(u2h(and_or(w8, 0x00F000F0u, 0x54005400u)), m_hi), s2, o2));
 }
 
 // Q4_K (gguf_importer.cpp:838-873): record = (d, dmin, scales[12], qs[128]);

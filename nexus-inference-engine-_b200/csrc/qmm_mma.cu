@@ -105,20 +105,22 @@ struct Lane<T_Q4_K> {
         const uint4 hd = *reinterpret_cast<const uint4*>(rec);
         q0 = *reinterpret_cast<const uint4*>(rec + 16 + 32 * t);
         q1 = *reinterpret_cast<const uint4*>(rec + 32 + 32 * t);
-        const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFFu)));
-        const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
-        // Sub-blocks 2t, 2t+1: scale bytes 2t, 2t+1 and nibbles of bytes 8 + 2(t&1) + {0,1}.
-        const uint32_t sbw = ((t < 2 ? hd.y : hd.z) >> (16 * (t & 1))) & 0xFFFFu;
-        const uint32_t ebw = ((hd.w >> (16 * (t & 1))) >> (4 * (t >> 1))) & 0x0F0Fu;
-#pragma unroll
-        for (int sub = 0; sub < 2; ++sub) {
-            const uint32_t sb = (sbw >> (8 * sub)) & 0xFFu;
-            const uint32_t eb = (ebw >> (8 * sub)) & 0xFu;
-            const int S = (int)(sb & 63u);
-            const int Mn = (int)((sb >> 6) | (eb << 2));
-            s2[sub] = __float2half2_rn(d * (float)S);
-            o2[sub] = __float2half2_rn(-(dmin * (float)Mn));
-        }
+        // Sub-blocks 2t, 2t+1: scale bytes 2t, 2t+1 (6-bit scale, low 2 bits of
+        // the min) and nibbles of bytes 8 + 2(t&1) + {0,1} (high 4 bits of the
+        // min).  (scale, min) pairs become exact f16 integers by the magic
+        // number; one f16 multiply by (d, d) / (-dmin, -dmin) then rounds
+        // d*sc and -dmin*m once each, as fp32 math followed by one rounding would.
+        const uint32_t v = __byte_perm(((t < 2 ? hd.y : hd.z) >> (16 * (t & 1))), 0u, 0x4140u);
+        const uint32_t e = __byte_perm(((hd.w >> (16 * (t & 1))) >> (4 * (t >> 1))), 0u, 0x4140u);
+        const __half2 magic = u2h(0x64006400u);
+        const __half2 sc = __hsub2(u2h((v & 0x003F003Fu) | 0x64006400u), magic);
+        const __half2 mn = __hsub2(u2h(((v >> 6) & 0x00030003u) | ((e & 0x000F000Fu) << 2) | 0x64006400u), magic);
+        const uint32_t sp = h2u(__hmul2(sc, u2h(__byte_perm(hd.x, 0u, 0x1010u))));
+        const uint32_t op = h2u(__hmul2(mn, u2h(__byte_perm(hd.x, 0u, 0x3232u) ^ 0x80008000u)));
+        s2[0] = u2h(__byte_perm(sp, 0u, 0x1010u));
+        s2[1] = u2h(__byte_perm(sp, 0u, 0x3232u));
+        o2[0] = u2h(__byte_perm(op, 0u, 0x1010u));
+        o2[1] = u2h(__byte_perm(op, 0u, 0x3232u));
     }
     __device__ __forceinline__ void pairs(int m, uint32_t (&p)[4]) const {
         dq::q4_word_pairs(word_of(m < 4 ? q0 : q1, m & 3), s2[m >> 2], o2[m >> 2], p);
@@ -191,18 +193,24 @@ struct Lane<T_Q3_K> {
         qs = *reinterpret_cast<const uint4*>(rec + 32 + 16 * t);
         hm = *reinterpret_cast<const uint2*>(rec + 8 * t);
         const uint16_t* tl = reinterpret_cast<const uint16_t*>(st + TILE_ROWS * 96 + row * 14);
-        const uint32_t sc0 = tl[0] | ((uint32_t)tl[1] << 16);  // scale bytes 0..3
-        const uint32_t sc1 = tl[2] | ((uint32_t)tl[3] << 16);  // 4..7
-        const uint32_t sc2 = tl[4] | ((uint32_t)tl[5] << 16);  // 8..11
-        const float d = __half2float(__ushort_as_half(tl[6]));
+        // Groups G = 4t + gg (gg = 0..3): i8 = G & 7 = 4(t&1) + gg; the low 4
+        // bits of the 6-bit scale are nibble (t >> 1) of scale byte i8, the
+        // high 2 bits are bits 2(t >> 1) + {0,1} of nibble (gg & 1) of byte
+        // 8 + 2(t&1) + (gg >> 1).  (scale - 32) * d as one f16 rounding of the
+        // exact product, through exact f16 integers.
+        const uint32_t lo4 = ((t & 1) ? (tl[2] | ((uint32_t)tl[3] << 16)) : (tl[0] | ((uint32_t)tl[1] << 16)));
+        const uint32_t hi2 = (uint32_t)tl[4 + (t & 1)];  // bytes 8 + 2(t&1), +1
+        const uint32_t sh = 4 * (t >> 1), hs = 2 * (t >> 1);
+        const __half2 d2 = u2h(__byte_perm((uint32_t)tl[6], 0u, 0x1010u));
+        const __half2 bias = u2h(0x64206420u);  // 1056 = magic + 32
 #pragma unroll
-        for (int gg = 0; gg < 4; ++gg) {
-            // group G = 4t + gg; i8 = G & 7 = 4(t&1) + gg; G < 8 iff t < 2
-            const uint32_t lowb = (((t & 1) ? sc1 : sc0) >> (8 * gg)) & 0xFFu;
-            const uint32_t hib = (sc2 >> (8 * (2 * (t & 1) + (gg >> 1)))) >> (4 * (gg & 1));
-            const int S = t < 2 ? (int)((lowb & 15u) | ((hib & 3u) << 4))
-                                : (int)((lowb >> 4) | (((hib >> 2) & 3u) << 4));
-            s2[gg] = __float2half2_rn(d * (float)(S - 32));
+        for (int pr = 0; pr < 2; ++pr) {  // groups gg = 2pr, 2pr+1
+            const uint32_t l = (__byte_perm(lo4, 0u, 0x4040u | ((2 * pr + 1) << 8) | (2 * pr)) >> sh) & 0x000F000Fu;
+            const uint32_t hb = (hi2 >> (8 * pr)) & 0xFFu;  // byte for gg = 2pr, 2pr+1: nibbles 0, 1
+            const uint32_t h = (((hb >> hs) & 3u) | ((((hb >> 4) >> hs) & 3u) << 16)) << 4;
+            const uint32_t sp = h2u(__hmul2(__hsub2(u2h(l | h | 0x64006400u), bias), d2));
+            s2[2 * pr] = u2h(__byte_perm(sp, 0u, 0x1010u));
+            s2[2 * pr + 1] = u2h(__byte_perm(sp, 0u, 0x3232u));
         }
     }
     // Elements 8m+4h .. 8m+4h+3: code byte Q (fields at bits 0-1, 2-3, 4-5,
@@ -240,10 +248,19 @@ __device__ __forceinline__ void named_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-constexpr int kGroups = 2;                      // consumer warpgroups of 8 warps
-constexpr int kConsumers = kGroups * kThreads;  // 512
-constexpr int kAll = kConsumers + 32;           // + the producer warp
 constexpr int kMaxCluster = 8;
+
+// Shared-memory budget of a variant with `groups` consumer warpgroups.
+template <int TYPE, int MT, int GROUPS, int CMAX>
+struct Budget {
+    static constexpr int NT = MT / 8;
+    static constexpr int WB = Lane<TYPE>::kStage;
+    static constexpr int XB = NT * 8 * 32 * 16;
+    static constexpr int PB = NT * 8 * TILE_ROWS * 4;
+    static constexpr int RECV = (CMAX - 1) * PB;
+    static constexpr int COMB = 2 * (GROUPS - 1) * PB;
+    static constexpr int S0 = (227 * 1024 - 2048 - RECV - COMB) / (WB + XB);
+};
 
 template <int TYPE, int MT>
 struct Cfg {
@@ -252,10 +269,15 @@ struct Cfg {
     static constexpr int XB = NT * 8 * 32 * 16;         // pieces (n8 tile, m, lane) of 16 B
     static constexpr int PB = NT * 8 * TILE_ROWS * 4;   // one tile's fp32 partial, [row][token]
     static constexpr int CMAX = NT >= 4 ? (WB > 20000 ? 2 : 4) : kMaxCluster;
+    // Two consumer warpgroups (measured: a third one, with its tighter
+    // register budget, is slower).
+    static constexpr int G = 2;
     static constexpr int RECV = (CMAX - 1) * PB;        // cluster leader: the other ranks' partials
-    static constexpr int COMB = 2 * PB;                 // group 1 -> group 0 hand-over, two tiles deep
-    static constexpr int S0 = (227 * 1024 - 2048 - RECV - COMB) / (WB + XB);
+    static constexpr int COMB = 2 * (G - 1) * PB;       // groups 1.. -> group 0 hand-over, two tiles deep
+    static constexpr int S0 = Budget<TYPE, MT, G, CMAX>::S0;
     static constexpr int S = S0 > 8 ? 8 : S0;
+    static constexpr int kConsumers = G * kThreads;
+    static constexpr int kAll = kConsumers + 32;        // + the producer warp
     static constexpr size_t smem = (size_t)S * (WB + XB) + COMB + RECV;
     static_assert(S >= 3, "pipeline too shallow");
 };
@@ -292,8 +314,8 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// One CTA per SM: warps 0-15 are two consumer groups that take the CTA's units
-// alternately (group = unit parity), warp 16 is the producer.  CTA rank r of
+// One CTA per SM: warps 0 .. 8G-1 are G consumer groups that take the CTA's
+// units in turn (group = unit index mod G), warp 8G is the producer.  CTA rank r of
 // cluster q takes chunks [r K/C, (r+1) K/C) of every tile of the cluster, so
 // with C = 1 a CTA owns whole tiles and writes y directly; with C > 1 the
 // cluster owns one tile and ranks 1..C-1 push their partial sums into rank
@@ -301,14 +323,15 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
 // which adds them in rank order: no global-memory round trip and a result
 // that does not depend on timing.
 template <int TYPE, int MT>
-__global__ void __launch_bounds__(kAll, 1) mma_gemv_kernel(const MmaParams p) {
+__global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const MmaParams p) {
     using Cf = Cfg<TYPE, MT>;
     constexpr int S = Cf::S, WB = Cf::WB, XB = Cf::XB, NT = Cf::NT, PB = Cf::PB;
+    constexpr int kGroups = Cf::G, kConsumers = Cf::kConsumers, kAll = Cf::kAll;
     constexpr int RS = NT * 8;  // floats per row in a partial
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* wst = smem;                                       // S x WB
     uint8_t* xst = smem + (size_t)S * WB;                      // S x XB
-    float* comb = reinterpret_cast<float*>(xst + (size_t)S * XB);           // 2 x PB
+    float* comb = reinterpret_cast<float*>(xst + (size_t)S * XB);           // (G-1) x 2 x PB
     float* recv = reinterpret_cast<float*>(xst + (size_t)S * XB + Cf::COMB);  // (CMAX-1) x PB
     __shared__ uint64_t full[S];   // unit landed: tile-chunk bytes + 32 producer cp.async arrivals + 1
     __shared__ uint64_t empty[S];  // the 8 warps of the consuming group are done with the stage
@@ -354,7 +377,7 @@ __global__ void __launch_bounds__(kAll, 1) mma_gemv_kernel(const MmaParams p) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     int w_issued = 0;  // producer lane 0: tile-chunk copies issued
-    if (warp == 2 * kWarps) {
+    if (warp == kGroups * kWarps) {
         // ---- producer: lane 0 issues the tile-chunk bulk copies, all 32
         // lanes the x pieces: piece (token, t4, m) holds the 8 elements
         // x[token][k0 + 64 t4 + 8m ..] at index ((token / 8) * 8 + m) * 32 +
@@ -396,7 +419,7 @@ __global__ void __launch_bounds__(kAll, 1) mma_gemv_kernel(const MmaParams p) {
             cp_async_arrive(&full[stg]);
         }
     } else {
-        // ---- consumers: group gi takes the units of parity gi of each tile ----
+        // ---- consumers: group gi takes the units c = gi mod G of each tile ----
         asm volatile("griddepcontrol.wait;" ::: "memory");
         const int gi = warp >> 3, wg = warp & 7;
         bool dead = false;
@@ -432,10 +455,10 @@ __global__ void __launch_bounds__(kAll, 1) mma_gemv_kernel(const MmaParams p) {
                 __syncwarp();
                 if (lane == 0) ptx::mbar_arrive(&empty[stg]);
             }
-            // ---- tile end: group 1 hands its partial to group 0 ----
-            float* cb = comb + (ti & 1) * (PB / 4);
+            // ---- tile end: groups 1.. hand their partials to group 0 ----
             const int r0 = 16 * wg + g;
-            if (gi == 1) {
+            if (gi > 0) {
+                float* cb = comb + ((gi - 1) * 2 + (ti & 1)) * (PB / 4);
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     *reinterpret_cast<float2*>(cb + r0 * RS + 8 * nt + 2 * tq) = make_float2(acc[nt][0], acc[nt][1]);
@@ -443,15 +466,18 @@ __global__ void __launch_bounds__(kAll, 1) mma_gemv_kernel(const MmaParams p) {
                 }
             }
             named_sync(1, kConsumers);
-            if (gi == 1) continue;
+            if (gi > 0) continue;
+            for (int gg = 1; gg < kGroups; ++gg) {
+                const float* cb = comb + ((gg - 1) * 2 + (ti & 1)) * (PB / 4);
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                const float2 a = *reinterpret_cast<const float2*>(cb + r0 * RS + 8 * nt + 2 * tq);
-                const float2 b = *reinterpret_cast<const float2*>(cb + (r0 + 8) * RS + 8 * nt + 2 * tq);
-                acc[nt][0] += a.x;
-                acc[nt][1] += a.y;
-                acc[nt][2] += b.x;
-                acc[nt][3] += b.y;
+                for (int nt = 0; nt < NT; ++nt) {
+                    const float2 a = *reinterpret_cast<const float2*>(cb + r0 * RS + 8 * nt + 2 * tq);
+                    const float2 b = *reinterpret_cast<const float2*>(cb + (r0 + 8) * RS + 8 * nt + 2 * tq);
+                    acc[nt][0] += a.x;
+                    acc[nt][1] += a.y;
+                    acc[nt][2] += b.x;
+                    acc[nt][3] += b.y;
+                }
             }
             const int64_t tile = q + (int64_t)ti * p.clusters;
             if (C == 1) {
@@ -525,7 +551,7 @@ __global__ void __launch_bounds__(kAll, 1) mma_gemv_kernel(const MmaParams p) {
         // Let the copies still in flight land (bounded) before the CTA's shared
         // memory goes away: only the last S tile-chunks issued can be pending.
         cp_wait<0>();
-        if (tid == 2 * kThreads) {
+        if (tid == kConsumers) {
             for (int u = w_issued > S ? w_issued - S : 0; u < w_issued; ++u) {
                 const long long t0 = clock64();
                 while (!ptx::mbar_try_wait(&full[u % S], (uint32_t)(u / S) & 1u) && clock64() - t0 < ptx::kWaitCycles) {
@@ -584,7 +610,7 @@ int launch(const Weight* w, const __half* x, void* y, int y_dtype, int64_t M, cu
     // griddepcontrol.wait): it may start while the previous kernel drains.
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(p.clusters * p.C));
-    cfg.blockDim = dim3(kAll);
+    cfg.blockDim = dim3(Cf::kAll);
     cfg.dynamicSmemBytes = Cf::smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
