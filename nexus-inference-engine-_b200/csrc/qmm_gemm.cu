@@ -8,9 +8,10 @@
 //
 // Work: a persistent grid of one CTA per SM walks (weight tile, token tile)
 // work tiles of 128 weight rows x 256 tokens.  Per 64-element k-step:
-//   warp 0       producer: the packed tile-chunk (256 k) by one 1-D bulk copy
-//                per chunk, and the 256 x 64 f16 activation box by TMA
-//                (128-byte swizzle, no multicast)
+//   warp 26      producer: the packed tile-chunk (256 k) by one 1-D bulk copy
+//                per chunk, up to four chunks ahead
+//   warp 0       producer: the 256 x 64 f16 activation box by TMA (128-byte
+//                swizzle, no multicast), four k-steps ahead
 //   warps 2-17   four dequant warpgroups: thread r decodes row r's 32-element
 //                group to f16 and writes it to TMEM with tcgen05.st - the
 //                MMA's A operand; a k-step's two groups go to two warpgroups,
@@ -43,16 +44,25 @@ namespace {
 constexpr int kDeqGroups = 4;  // dequant warpgroups
 constexpr int kEpiWarps = 8;   // two per TMEM lane quadrant
 constexpr int kWarpProducer = 0, kWarpMma = 1, kWarpDeq0 = 2, kWarpEpi0 = 2 + 4 * kDeqGroups;
-constexpr int kThreads = 32 * (kWarpEpi0 + kEpiWarps);
+constexpr int kWarpWProducer = kWarpEpi0 + kEpiWarps;  // issues the tile-chunk copies
+constexpr int kThreads = 32 * (kWarpWProducer + 1);
 constexpr int kNT = 256;              // tokens per work tile (MMA N)
 constexpr int kKS = 64;               // reduction elements per k-step (one swizzle atom)
 constexpr int kStepsPerChunk = CHUNK_K / kKS;
 constexpr int kXStages = 4;
-constexpr int kWStages = 2;
 constexpr int kAStages = 4;           // TMEM A buffers of 32 columns
 constexpr uint32_t kColD = 256;       // accumulator: columns 256..511
 constexpr uint32_t kTmemCols = 512;
 constexpr int kXBytes = kNT * kKS * 2;  // 32 KB per k-step
+
+// Tile-chunk ring depth: as many stages (up to 4) as fit next to the x ring.
+template <int TYPE>
+struct WRing {
+    static constexpr int WB = dq::Group<TYPE>::kStage;
+    static constexpr int fit = (227 * 1024 - 1024 - 256 - kXStages * kXBytes) / WB;
+    static constexpr int kStages = fit > 4 ? 4 : fit;
+    static_assert(kStages >= 2, "tile-chunk ring too shallow");
+};
 
 struct GemmParams {
     const uint8_t* w;
@@ -93,6 +103,7 @@ __device__ __forceinline__ void dq_step(const uint8_t* stage, int r, int h, uint
 template <int TYPE>
 __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p, const __grid_constant__ CUtensorMap xmap) {
     constexpr int WB = dq::Group<TYPE>::kStage;
+    constexpr int kWStages = WRing<TYPE>::kStages;
     constexpr uint32_t IDESC = ptx::idesc_f16_f32(128, kNT);
 
     extern __shared__ uint8_t smem_raw[];
@@ -145,19 +156,36 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p
     const int chunks = (int)p.s.chunks;
     const int G = gridDim.x;
 
-    if (warp == kWarpProducer) {
+    if (warp == kWarpWProducer) {
         if (lane == 0) {
-            ptx::prefetch_tmap(&xmap);
-            uint32_t qx = 0, qw = 0;
+            uint32_t qw = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < p.tiles && ok; tile += G) {
-                const int wt = tile / p.m_tiles, mt = tile - wt * p.m_tiles;
+                const int wt = tile / p.m_tiles;
                 for (int c = 0; c < chunks && ok; ++c, ++qw) {
                     const int sw = qw % kWStages;
                     if (qw >= kWStages && !(ok = ptx::mbar_wait(&w_empty[sw], ((qw / kWStages) & 1) ^ 1u, ctl, 11)))
                         break;
                     ptx::mbar_arrive_expect_tx(&w_full[sw], WB);
                     ptx::bulk_g2s(ws + sw * WB, p.w + p.s.chunk_offset(wt, c), WB, &w_full[sw]);
+                }
+            }
+            // Do not leave with copies in flight (bounded, ignoring the abort flag).
+            for (uint32_t k = qw >= kWStages ? qw - kWStages : 0; k < qw; ++k) {
+                const long long t0 = clock64();
+                while (!ptx::mbar_try_wait(&w_full[k % kWStages], (k / kWStages) & 1) && clock64() - t0 < ptx::kWaitCycles) {
+                }
+            }
+        }
+    } else if (warp == kWarpProducer) {
+        if (lane == 0) {
+            ptx::prefetch_tmap(&xmap);
+            uint32_t qx = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < p.tiles && ok; tile += G) {
+                const int wt = tile / p.m_tiles, mt = tile - wt * p.m_tiles;
+                (void)wt;
+                for (int c = 0; c < chunks && ok; ++c) {
                     for (int st = 0; st < kStepsPerChunk; ++st, ++qx) {
                         const int sx = qx % kXStages;
                         if (qx >= kXStages &&
@@ -172,11 +200,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p
             for (uint32_t k = qx >= kXStages ? qx - kXStages : 0; k < qx; ++k) {
                 const long long t0 = clock64();
                 while (!ptx::mbar_try_wait(&x_full[k % kXStages], (k / kXStages) & 1) && clock64() - t0 < ptx::kWaitCycles) {
-                }
-            }
-            for (uint32_t k = qw >= kWStages ? qw - kWStages : 0; k < qw; ++k) {
-                const long long t0 = clock64();
-                while (!ptx::mbar_try_wait(&w_full[k % kWStages], (k / kWStages) & 1) && clock64() - t0 < ptx::kWaitCycles) {
                 }
             }
         }
@@ -288,7 +311,7 @@ bool g_gemm_enabled = true;
 
 template <int TYPE>
 size_t smem_bytes() {
-    return 1024 + (size_t)kXStages * kXBytes + (size_t)kWStages * dq::Group<TYPE>::kStage + 256;
+    return 1024 + (size_t)kXStages * kXBytes + (size_t)WRing<TYPE>::kStages * dq::Group<TYPE>::kStage + 256;
 }
 
 template <int TYPE>
