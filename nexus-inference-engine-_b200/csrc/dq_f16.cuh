@@ -107,9 +107,42 @@ struct Group<T_Q8_0> {
     }
 };
 
-// Q3_K (gguf_importer.cpp:791-833): plane A = [hmask 32][qs 64] at r*96,
-// plane B = [scales 12][d] at 128*96 + r*14; group G = elements 32G..32G+31,
-// scale groups 2G and 2G+1.
+// a | (b & c) in one LOP3 (truth table 0xF8).
+__device__ __forceinline__ uint32_t or_and(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xF8;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Pair K of a Q3_K code word (formats.cuh, q3_lo_pos / q3_hi_pos): low codes
+// at bits {2K, 2K+1} (+16), high bits at {2K+2} (+16) of `hs`, placed in the
+// mantissa of a magic number whose unit is bit 2K (1024, 256, 64, 16), so
+// subtracting magic + 4 leaves u - 4 exactly; times s = fl16(d * (sc - 32)).
+template <int K>
+__device__ __forceinline__ uint32_t q3_pair(uint32_t ls, uint32_t hs, __half2 s2) {
+    constexpr uint32_t MG = K == 0 ? 0x64006400u : K == 1 ? 0x5C005C00u : K == 2 ? 0x54005400u : 0x4C004C00u;
+    constexpr uint32_t BI = K == 0 ? 0x64046404u : K == 1 ? 0x5C105C10u : K == 2 ? 0x54405440u : 0x4D004D00u;
+    const uint32_t v = or_and(and_or(ls, 0x00030003u << (2 * K), MG), hs, 0x00040004u << (2 * K));
+    return h2u(__hmul2(__hsub2(u2h(v), u2h(BI)), s2));
+}
+
+// Pairs (2i, 2i+1), i = 0..7, of the 16 elements of one L word; `h` is the
+// high-bit word already rotated for L1.
+__device__ __forceinline__ void q3_word_pairs(uint32_t l, uint32_t h, __half2 s2, uint32_t* o) {
+    o[0] = q3_pair<0>(l, h, s2);
+    o[1] = q3_pair<1>(l, h, s2);
+    o[2] = q3_pair<2>(l, h, s2);
+    o[3] = q3_pair<3>(l, h, s2);
+    const uint32_t l8 = l >> 8, h1 = h >> 1;
+    o[4] = q3_pair<0>(l8, h1, s2);
+    o[5] = q3_pair<1>(l8, h1, s2);
+    o[6] = q3_pair<2>(l8, h1, s2);
+    o[7] = q3_pair<3>(l8, h1, s2);
+}
+
+// Q3_K (gguf_importer.cpp:791-833): plane A = 8 x [L0 L1 H] (tiled code order)
+// at r*96, plane B = [scales 12][d] at 128*96 + r*14; group G = elements
+// 32G..32G+31, scale groups 2G (L0) and 2G+1 (L1).
 template <>
 struct Group<T_Q3_K> {
     static constexpr int kStage = TILE_ROWS * 110;
@@ -128,18 +161,10 @@ struct Group<T_Q3_K> {
             const int S = g < 8 ? (int)((lo & 15u) | ((hi & 3u) << 4)) : (int)((lo >> 4) | (((hi >> 2) & 3u) << 4));
             s2[gg] = __float2half2_rn(d * (float)(S - 32));
         }
-        const uint32_t hm = *reinterpret_cast<const uint32_t*>(rec + 4 * G);
-        const uint2 qq = *reinterpret_cast<const uint2*>(rec + 32 + 8 * G);
-        const __half2 bias = u2h(0x64046404u);  // 1028: removes the magic and the -4 offset
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-            const uint32_t qw = c < 8 ? qq.x : qq.y;
-            const uint32_t lo = (qw >> (4 * (c & 7))) & 0xFu;  // two 2-bit fields
-            const uint32_t hb = (hm >> (2 * c)) & 3u;           // their two high bits
-            const uint32_t qa = (lo & 3u) | ((hb & 1u) << 2);
-            const uint32_t qb = ((lo >> 2) & 3u) | ((hb >> 1) << 2);
-            o[c] = h2u(__hmul2(__hsub2(u2h(qa | (qb << 16) | 0x64006400u), bias), s2[c >> 3]));
-        }
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(rec + 12 * G);
+        const uint32_t h = w[2];
+        q3_word_pairs(w[0], h, s2[0], &o[0]);
+        q3_word_pairs(w[1], __funnelshift_r(h, h, 8), s2[1], &o[8]);
     }
 };
 

@@ -16,10 +16,12 @@
 // that owns row r reads 16-byte aligned words (see place_block() below).
 // Rows beyond N and blocks beyond K are zero bytes, which every format decodes
 // to zero.  Decoding the tiled copy gives exactly the values of decoding the
-// GGUF bytes.  Scales and most codes are copied byte for byte; the one
-// transformation is the order of the 4-bit codes of Q4_0 and Q4_K inside each
-// 32-element group (see q4_code_pos()), chosen so that one AND/OR of a 32-bit
-// code word yields two consecutive elements as an f16 pair.
+// GGUF bytes.  Scales and most codes are copied byte for byte; the
+// transformations are the order of the 4-bit codes of Q4_0 and Q4_K inside
+// each 32-element group (q4_code_pos) and of the 2-bit codes and high-mask
+// bits of Q3_K (q3_lo_pos, q3_hi_pos), chosen so that one or two AND/OR
+// operations of a 32-bit code word yield two consecutive elements as an f16
+// pair.
 #pragma once
 #include <cstdint>
 #include <cuda_fp16.h>
@@ -99,7 +101,8 @@ inline bool make_tiled_shape(int type, int64_t N, int64_t K, TiledShape* s) {
 //   Q4_K  record 144 B: the block itself (d, dmin, scales[12], qs[128]), qs in
 //         tiled code order
 //   Q5_K  record 176 B: the block itself
-//   Q3_K  plane A 128 x 96 B (hmask[32], qs[64]); plane B 128 x 14 B (scales[12], d)
+//   Q3_K  plane A 128 x 96 B (hmask + qs regrouped: 8 x [L0 L1 H], see
+//         q3_lo_pos); plane B 128 x 14 B (scales[12], d)
 //   Q2_K  plane A 128 x 80 B (scales[16], qs[64]); plane B 128 x 4 B (dmin, d)
 //   Q6_K  plane A 128 x 192 B (ql, qh); plane B 128 x 16 B (scales); plane C 128 x 2 B (d)
 // ---------------------------------------------------------------------------
@@ -176,6 +179,62 @@ __host__ __device__ inline uint8_t q4_tiled_byte(int type, const uint8_t* gguf, 
     const int w = ob >> 2, k = ob & 3;
     const int lo = 8 * w + ((k & 1) << 2) + (k >> 1), hi = lo + 2;
     return (uint8_t)(q4_gguf_code(type, gguf, lo) | (q4_gguf_code(type, gguf, hi) << 4));
+}
+
+// ---------------------------------------------------------------------------
+// Q3_K code order in the tiled copy.  Each 32-element group (two 16-element
+// scale groups) becomes three 32-bit words [L0][L1][H], the 12 bytes that the
+// GGUF block spends on it (8 of qs, 4 of hmask).  L0 holds the 2-bit low codes
+// of elements 0..15, L1 of 16..31: element e at bit 2*(e>>1) + 16*(e&1) of its
+// word, so the pair (2i, 2i+1) sits in bits {2i, 2i+1} and {16+2i, 17+2i}.  H
+// holds the 32 high bits: for a pair k = i&3 of the low byte half (i < 4) the
+// high bits sit 2 above the code ({2k+2, 2k+18}), for i >= 4 one more (read
+// through H >> 1); the bits of L1's elements are those positions plus 8
+// (mod 32, read through a rotate by 8).  So a pair is (L & mask | magic) |
+// (H' & mask') with a magic number whose unit is the code's lowest bit.
+// Where the GGUF block holds element j (gguf_importer.cpp:809-827):
+//   low code  (qs[j/4] >> 2(j%4)) & 3   (qs at block offset 32)
+//   high bit  (hmask[j/8] >> (j%8)) & 1 (hmask at block offset 0)
+// ---------------------------------------------------------------------------
+__host__ __device__ inline int q3_lo_pos(int e16) { return 2 * (e16 >> 1) + 16 * (e16 & 1); }
+__host__ __device__ inline int q3_hi_pos(int e32) {
+    const int e = e32 & 15, i = e >> 1;
+    const int p = 2 * (i & 3) + 2 + (i >> 2) + 16 * (e & 1);
+    return e32 < 16 ? p : (p + 8) & 31;
+}
+
+// Byte `ob` (0..95) of the tiled Q3_K plane-A record of one GGUF block.
+__host__ __device__ inline uint8_t q3_tiled_byte(const uint8_t* blk, int ob) {
+    const int G = ob / 12, wb = ob % 12, word = wb >> 2;
+    uint32_t v = 0;
+    for (int bit = 0; bit < 8; ++bit) {
+        const int p = 8 * (wb & 3) + bit;
+        uint32_t b;
+        if (word < 2) {
+            // p = 2i + 16s + f: element 2i + s of the word, bit f of its code
+            const int s = p >> 4, i = (p & 15) >> 1, f = p & 1;
+            const int j = 32 * G + 16 * word + 2 * i + s;
+            b = (blk[32 + (j >> 2)] >> (2 * (j & 3) + f)) & 1u;
+        } else {
+            // invert q3_hi_pos: positions with (p & 15) in [2, 9] belong to L0
+            const bool low = ((p & 15) >= 2) && ((p & 15) <= 9);
+            const int pa = low ? p : ((p - 8) & 31);
+            const int s = pa >> 4, q = (pa & 15) - 2;  // q = 2k + (i >> 2)
+            const int i = 4 * (q & 1) + (q >> 1);
+            const int j = 32 * G + (low ? 0 : 16) + 2 * i + s;
+            b = (blk[j >> 3] >> (j & 7)) & 1u;
+        }
+        v |= b << bit;
+    }
+    return (uint8_t)v;
+}
+
+__device__ __forceinline__ int q3_tiled_code(const uint8_t* rec, int e) {
+    const int G = e >> 5, e32 = e & 31;
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(rec + 12 * G);
+    const uint32_t lo = (w[e32 >> 4] >> q3_lo_pos(e32 & 15)) & 3u;
+    const uint32_t hb = (w[2] >> q3_hi_pos(e32)) & 1u;
+    return (int)(lo | (hb << 2));
 }
 
 __device__ __forceinline__ int q4_tiled_code(const uint8_t* g, int e) {
@@ -277,11 +336,7 @@ __device__ inline void decode8(int type, const uint8_t* chunk, int r, int e0, fl
                            : ((tail[i8] >> 4) | (((hi >> 2) & 3) << 4));
             sc -= 32;
             float ds = __fmul_rn(d, (float)sc);
-            for (int i = 0; i < 8; ++i) {
-                int e = e0 + i;
-                int q = ((rec[32 + (e >> 2)] >> (2 * (e & 3))) & 3) | (((rec[e >> 3] >> (e & 7)) & 1) << 2);
-                out[i] = __fmul_rn(ds, __fsub_rn((float)q, 4.0f));
-            }
+            for (int i = 0; i < 8; ++i) out[i] = __fmul_rn(ds, __fsub_rn((float)q3_tiled_code(rec, e0 + i), 4.0f));
             break;
         }
         case T_Q4_K: {  // :838-873

@@ -28,7 +28,8 @@ __global__ void repack_kernel(const uint8_t* __restrict__ src, uint8_t* __restri
         uint8_t* base = dst + s.chunk_offset(tile, chunk);
         Segment seg[3];
         const int ns = block_segments(s.type, (int)r, (int)j, seg);
-        // Bytes [c0, c1) of the block are 4-bit codes stored in the tiled order.
+        // Bytes [c0, c1) of the block are 4-bit codes stored in the tiled order;
+        // Q3_K's first 96 bytes (hmask, qs) are regrouped (q3_tiled_byte).
         const int c0 = s.type == T_Q4_0 ? 2 : s.type == T_Q4_K ? 16 : s.g.bb;
         const int c1 = s.type == T_Q4_0 ? 18 : s.type == T_Q4_K ? 144 : s.g.bb;
         for (int q = 0; q < ns; ++q)
@@ -38,6 +39,8 @@ __global__ void repack_kernel(const uint8_t* __restrict__ src, uint8_t* __restri
                 if (sb >= c0 && sb < c1) {
                     const int g = (sb - c0) >> 4;
                     v = q4_tiled_byte(s.type, blk + c0 + 16 * g, (sb - c0) & 15);
+                } else if (s.type == T_Q3_K && sb < 96) {
+                    v = q3_tiled_byte(blk, sb);
                 } else {
                     v = blk[sb];
                 }

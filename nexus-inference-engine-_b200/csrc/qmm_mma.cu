@@ -178,20 +178,28 @@ struct Lane<T_Q8_0> {
     }
 };
 
-// Q3_K (gguf_importer.cpp:791-833): plane A = [hmask 32][qs 64] at row*96,
-// plane B = [scales 12][d] at 128*96 + row*14.  The slice's elements are qs
-// bytes 16t.. (2 bits each, element e at bits 2(e&3) of byte e/4) and hmask
-// bytes 8t.. (bit e), in four 16-element scale groups.
+// Q3_K (gguf_importer.cpp:791-833): plane A = 8 x [L0 L1 H] per row (tiled
+// code order, formats.cuh q3_lo_pos), plane B = [scales 12][d] at 128*96 +
+// row*14.  The slice's elements are groups 2t, 2t+1 = bytes 24t .. 24t+23 of
+// the row's plane-A record, in four 16-element scale groups.
 template <>
 struct Lane<T_Q3_K> {
     static constexpr int kStage = TILE_ROWS * 110;
-    uint4 qs;
-    uint2 hm;
+    uint32_t L[4], H[2], Hr[2];  // L0, L1 of group 2t, then of 2t+1; their high-bit words
     __half2 s2[4];
     __device__ __forceinline__ void load(const uint8_t* st, int row, int t) {
-        const uint8_t* rec = st + row * 96;
-        qs = *reinterpret_cast<const uint4*>(rec + 32 + 16 * t);
-        hm = *reinterpret_cast<const uint2*>(rec + 8 * t);
+        const uint8_t* rec = st + row * 96 + 24 * t;
+        const uint2 a = *reinterpret_cast<const uint2*>(rec);
+        const uint2 b = *reinterpret_cast<const uint2*>(rec + 8);
+        const uint2 c = *reinterpret_cast<const uint2*>(rec + 16);
+        L[0] = a.x;
+        L[1] = a.y;
+        H[0] = b.x;
+        L[2] = b.y;
+        L[3] = c.x;
+        H[1] = c.y;
+        Hr[0] = __funnelshift_r(H[0], H[0], 8);
+        Hr[1] = __funnelshift_r(H[1], H[1], 8);
         const uint16_t* tl = reinterpret_cast<const uint16_t*>(st + TILE_ROWS * 96 + row * 14);
         // Groups G = 4t + gg (gg = 0..3): i8 = G & 7 = 4(t&1) + gg; the low 4
         // bits of the 6-bit scale are nibble (t >> 1) of scale byte i8, the
@@ -213,24 +221,20 @@ struct Lane<T_Q3_K> {
             s2[2 * pr + 1] = u2h(__byte_perm(sp, 0u, 0x3232u));
         }
     }
-    // Elements 8m+4h .. 8m+4h+3: code byte Q (fields at bits 0-1, 2-3, 4-5,
-    // 6-7) and high bits H (bits 0..3).  The 3-bit value u = lo + 4*hb of
-    // each element goes into an f16 mantissa whose unit sits at the field's
-    // bit: (e0, e1) -> (1024 + u0, 256 + u1), (e2, e3) -> (64 + u2, 16 + u3);
-    // subtracting (magic + 4) leaves u - 4 exactly.
-    __device__ __forceinline__ void quad(uint32_t qw, int byte, uint32_t h4, __half2 s, uint32_t* p) const {
-        const uint32_t tq = __byte_perm(qw, 0u, 0x4040u | (byte << 8) | byte);  // Q in bytes 0 and 2
-        const uint32_t v01 = ((tq & 0x000C0003u) | 0x5C006400u) | ((h4 * 0x00080004u) & 0x00100004u);
-        const uint32_t v23 = ((tq & 0x00C00030u) | 0x4C005400u) | ((h4 * 0x00200010u) & 0x01000040u);
-        p[0] = h2u(__hmul2(__hsub2(u2h(v01), u2h(0x5C106404u)), s));  // (1028, 260)
-        p[1] = h2u(__hmul2(__hsub2(u2h(v23), u2h(0x4D005440u)), s));  // (68, 20)
-    }
+    // Elements 8m .. 8m+7 of the slice: group m >> 2, L word (m & 3) >> 1,
+    // pairs 4((m & 3) & 1) .. +3 of that word.
     __device__ __forceinline__ void pairs(int m, uint32_t (&p)[4]) const {
-        const uint32_t qw = word_of(qs, m >> 1);
-        const uint32_t hw = (m < 4 ? hm.x : hm.y) >> (8 * (m & 3));
+        const int g = m >> 2, j = (m & 3) >> 1;
+        uint32_t l = L[2 * g + j], h = j ? Hr[g] : H[g];
+        if (m & 1) {
+            l >>= 8;
+            h >>= 1;
+        }
         const __half2 s = s2[m >> 1];
-        quad(qw, 2 * (m & 1), hw & 0xFu, s, &p[0]);
-        quad(qw, 2 * (m & 1) + 1, (hw >> 4) & 0xFu, s, &p[2]);
+        p[0] = dq::q3_pair<0>(l, h, s);
+        p[1] = dq::q3_pair<1>(l, h, s);
+        p[2] = dq::q3_pair<2>(l, h, s);
+        p[3] = dq::q3_pair<3>(l, h, s);
     }
 };
 
