@@ -38,6 +38,7 @@ struct Context {
     void* hy = nullptr;
     size_t hy_bytes = 0;
     DeviceStatus* status = nullptr;  // bounded-wait error word (device memory)
+    DeviceStatus* status_host = nullptr;  // pinned copy read by the host entry point
     std::mutex mu;                   // registration, host entry point, teardown
     std::unordered_set<Weight*> live;
 };
@@ -81,16 +82,20 @@ int grow(void** buf, size_t* have, size_t need) {
 
 // Reads the device status word after a synchronize; a nonzero code means a
 // bounded wait inside a kernel gave up.
-int check_device_status() {
-    DeviceStatus st{};
-    cudaError_t e = cudaMemcpy(&st, g_ctx.status, sizeof st, cudaMemcpyDeviceToHost);
-    if (e != cudaSuccess) return cuda_fail(e, "read device status");
+int report_status(const DeviceStatus& st) {
     if (st.code) {
         cudaMemset(g_ctx.status, 0, sizeof(DeviceStatus));
         return fail(NXQ_ERR_TIMEOUT, "device-side bounded wait expired (code %u at %u)", st.code,
                     st.where);
     }
     return NXQ_OK;
+}
+
+int check_device_status() {
+    DeviceStatus st{};
+    cudaError_t e = cudaMemcpy(&st, g_ctx.status, sizeof st, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "read device status");
+    return report_status(st);
 }
 
 // Registers N rows of K from GGUF blocks.  `src` is host (is_host) or device
@@ -276,6 +281,7 @@ NXQ_API int nxq_init(int device) {
     NXQ_CUDA(cudaStreamCreateWithFlags(&g_ctx.host_stream, cudaStreamNonBlocking));
     NXQ_CUDA(cudaMalloc(&g_ctx.status, sizeof(DeviceStatus)));
     NXQ_CUDA(cudaMemset(g_ctx.status, 0, sizeof(DeviceStatus)));
+    NXQ_CUDA(cudaMallocHost(&g_ctx.status_host, sizeof(DeviceStatus)));
     // Keep stream-ordered scratch in the pool between calls instead of
     // returning it to the driver after every synchronize.
     cudaMemPool_t pool;
@@ -311,6 +317,8 @@ NXQ_API int nxq_shutdown(void) {
     g_ctx.hx_bytes = g_ctx.hy_bytes = 0;
     if (g_ctx.status) cudaFree(g_ctx.status);
     g_ctx.status = nullptr;
+    if (g_ctx.status_host) cudaFreeHost(g_ctx.status_host);
+    g_ctx.status_host = nullptr;
     if (g_ctx.host_stream) cudaStreamDestroy(g_ctx.host_stream);
     g_ctx.host_stream = nullptr;
     g_ctx.ready = false;
@@ -502,8 +510,10 @@ NXQ_API int nxq_qmatmul_host(nxq_weight_t h, const float* x_host, float* y_host,
     rc = qmatmul_dispatch(w, g_ctx.hx, NXQ_F32, g_ctx.hy, NXQ_F32, M, st);
     if (rc) return rc;
     NXQ_CUDA(cudaMemcpyAsync(y_host, g_ctx.hy, yb, cudaMemcpyDeviceToHost, st));
+    // The status word travels with the result: one synchronize per call.
+    NXQ_CUDA(cudaMemcpyAsync(g_ctx.status_host, g_ctx.status, sizeof(DeviceStatus), cudaMemcpyDeviceToHost, st));
     NXQ_CUDA(cudaStreamSynchronize(st));
-    return check_device_status();
+    return report_status(*g_ctx.status_host);
 }
 
 NXQ_API int nxq_qmatmul_kernel_name(nxq_weight_t h, int64_t M, int x_dtype, int y_dtype, char* buf,

@@ -289,7 +289,8 @@ struct Cfg {
 struct MmaParams {
     const uint8_t* w;
     TiledShape s;
-    const __half* x;
+    const void* x;  // f16, or (M <= 2) fp32 / bf16 rounded to f16 by the producer
+    int x_dtype;
     int64_t M;
     void* y;
     int y_dtype;
@@ -397,10 +398,12 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
                 ptx::bulk_g2s(wst + u * WB, w_src(u), WB, &full[u]);
             }
         asm volatile("griddepcontrol.wait;" ::: "memory");
-        for (int u = 0; u < n; ++u) {
-            const int stg = u % S;
+        // Refills stage u % S with unit u's tile-chunk once its consumers are
+        // done with unit u - S (lane 0); false if the wait gave up.
+        auto refill = [&](int u) {
+            int ok = 1;
             if (u >= S) {
-                int ok = 0;
+                const int stg = u % S;
                 if (lane == 0) {
                     ok = ptx::mbar_wait(&empty[stg], (uint32_t)(u / S - 1) & 1u, ctl, 32) ? 1 : 0;
                     if (ok) {
@@ -409,18 +412,87 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
                         ++w_issued;
                     }
                 }
-                if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) break;
+                ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
             }
-            uint4* xd = reinterpret_cast<uint4*>(xst + stg * XB);
+            return ok != 0;
+        };
+        auto chunk_k0 = [&](int u) {
             const int ti = u / kr;
-            const int64_t k0 = (int64_t)(kc0 + u - ti * kr) * CHUNK_K;
-            for (int i = lane; i < M * 32; i += 32) {
-                const int tok = i >> 5, t4 = (i >> 3) & 3, m = i & 7;
-                const int64_t k = k0 + 64 * t4 + 8 * m;
-                cp_async16_zfill(xd + ((tok >> 3) * 8 + m) * 32 + 4 * (tok & 7) + t4,
-                                 p.x + (int64_t)tok * K + (k < K ? k : 0), k < K ? 16u : 0u);
+            return (int64_t)(kc0 + u - ti * kr) * CHUNK_K;
+        };
+        if (p.x_dtype == NXQ_F16) {
+            const __half* xh = static_cast<const __half*>(p.x);
+            for (int u = 0; u < n; ++u) {
+                if (!refill(u)) break;
+                uint4* xd = reinterpret_cast<uint4*>(xst + (u % S) * XB);
+                const int64_t k0 = chunk_k0(u);
+                for (int i = lane; i < M * 32; i += 32) {
+                    const int tok = i >> 5, t4 = (i >> 3) & 3, m = i & 7;
+                    const int64_t k = k0 + 64 * t4 + 8 * m;
+                    cp_async16_zfill(xd + ((tok >> 3) * 8 + m) * 32 + 4 * (tok & 7) + t4,
+                                     xh + (int64_t)tok * K + (k < K ? k : 0), k < K ? 16u : 0u);
+                }
+                cp_async_arrive(&full[u % S]);
             }
-            cp_async_arrive(&full[stg]);
+        } else {
+            // fp32 / bf16 activations, M <= 2 (at most 2 pieces per lane):
+            // loaded here and rounded to f16 as __float2half_rn does.  The
+            // loads of unit u stay in flight over the next refill; unit u is
+            // converted, stored and signalled in the next iteration.
+            const bool f32 = p.x_dtype == NXQ_F32;
+            float4 ra[2], rb[2];
+            auto issue = [&](int u) {
+                const int64_t k0 = chunk_k0(u);
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const int i = lane + 32 * j;
+                    const int tok = i >> 5, t4 = (i >> 3) & 3, m = i & 7;
+                    const int64_t k = k0 + 64 * t4 + 8 * m;
+                    ra[j] = rb[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (i < M * 32 && k < K) {
+                        if (f32) {
+                            const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.x) +
+                                                                                (int64_t)tok * K + k);
+                            ra[j] = __ldg(src);
+                            rb[j] = __ldg(src + 1);
+                        } else {
+                            const uint4 q = __ldg(reinterpret_cast<const uint4*>(
+                                static_cast<const __nv_bfloat16*>(p.x) + (int64_t)tok * K + k));
+                            ra[j] = make_float4(__uint_as_float(q.x), __uint_as_float(q.y), __uint_as_float(q.z),
+                                                __uint_as_float(q.w));
+                        }
+                    }
+                }
+            };
+            auto bf2h = [](uint32_t w) {
+                return h2u(__float22half2_rn(__bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w))));
+            };
+            auto finish = [&](int u) {
+                uint4* xd = reinterpret_cast<uint4*>(xst + (u % S) * XB);
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const int i = lane + 32 * j;
+                    if (i >= M * 32) continue;
+                    const int tok = i >> 5, t4 = (i >> 3) & 3, m = i & 7;
+                    uint4 h;
+                    if (f32) {
+                        h = make_uint4(h2u(__floats2half2_rn(ra[j].x, ra[j].y)), h2u(__floats2half2_rn(ra[j].z, ra[j].w)),
+                                       h2u(__floats2half2_rn(rb[j].x, rb[j].y)), h2u(__floats2half2_rn(rb[j].z, rb[j].w)));
+                    } else {
+                        h = make_uint4(bf2h(__float_as_uint(ra[j].x)), bf2h(__float_as_uint(ra[j].y)),
+                                       bf2h(__float_as_uint(ra[j].z)), bf2h(__float_as_uint(ra[j].w)));
+                    }
+                    xd[((tok >> 3) * 8 + m) * 32 + 4 * (tok & 7) + t4] = h;
+                }
+                ptx::mbar_arrive(&full[u % S]);
+            };
+            int u = 0;
+            for (; u < n; ++u) {
+                if (!refill(u)) break;
+                if (u > 0) finish(u - 1);
+                issue(u);
+            }
+            if (u == n && n > 0) finish(n - 1);
         }
     } else {
         // ---- consumers: group gi takes the units c = gi mod G of each tile ----
@@ -599,12 +671,13 @@ void pick_split(const TiledShape& s, int cmax, int* C, int* clusters) {
 }
 
 template <int TYPE, int MT>
-int launch(const Weight* w, const __half* x, void* y, int y_dtype, int64_t M, cudaStream_t st) {
+int launch(const Weight* w, const void* x, int x_dtype, void* y, int y_dtype, int64_t M, cudaStream_t st) {
     using Cf = Cfg<TYPE, MT>;
     MmaParams p;
     p.w = w->dev;
     p.s = w->shape;
     p.x = x;
+    p.x_dtype = x_dtype;
     p.M = M;
     p.y = y;
     p.y_dtype = y_dtype;
@@ -665,8 +738,12 @@ int mma_qmatmul(const Weight* w, const void* x, int x_dtype, void* y, int y_dtyp
     const TiledShape& s = w->shape;
     if (!mma_supported(s, M)) return NXQ_ERR_UNSUPPORTED;
     const int mt = M <= 8 ? 8 : M <= 16 ? 16 : 32;
-    const bool direct = x_dtype == NXQ_F16 && ((uintptr_t)x % 16) == 0;
-    const __half* xh = static_cast<const __half*>(x);
+    // f16 activations are read as they are; fp32 / bf16 ones are rounded to
+    // f16 by the kernel's producer when M <= 2, else by a conversion kernel.
+    const bool aligned = ((uintptr_t)x % 16) == 0;
+    const bool direct = aligned && (x_dtype == NXQ_F16 || (M <= 2 && (x_dtype == NXQ_F32 || x_dtype == NXQ_BF16)));
+    const void* xh = x;
+    int xdt = x_dtype;
     if (!direct) {
         StreamScratch* sc = nullptr;
         int rc = scratch_for(st, 0, 0, (size_t)(M * s.K), &sc);
@@ -674,12 +751,13 @@ int mma_qmatmul(const Weight* w, const void* x, int x_dtype, void* y, int y_dtyp
         cudaError_t e = launch_to_half(x, x_dtype, sc->xh, M * s.K, st);
         if (e != cudaSuccess) return cuda_fail(e, "to_half launch");
         xh = sc->xh;
+        xdt = NXQ_F16;
     }
 #define NXQ_CASE(T)                                                \
     case T:                                                        \
-        return mt == 8    ? launch<T, 8>(w, xh, y, y_dtype, M, st)  \
-               : mt == 16 ? launch<T, 16>(w, xh, y, y_dtype, M, st) \
-                          : launch<T, 32>(w, xh, y, y_dtype, M, st);
+        return mt == 8    ? launch<T, 8>(w, xh, xdt, y, y_dtype, M, st)  \
+               : mt == 16 ? launch<T, 16>(w, xh, xdt, y, y_dtype, M, st) \
+                          : launch<T, 32>(w, xh, xdt, y, y_dtype, M, st);
     switch (s.type) {
         NXQ_CASE(T_Q4_K)
         NXQ_CASE(T_Q4_0)

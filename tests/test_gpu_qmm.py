@@ -248,3 +248,30 @@ def test_prefill_gemm_shapes(gpu, t, M, N, K):
         assert synth.rel_l2(y.cpu().numpy(), want) < TOL
     finally:
         w.release()
+
+
+@pytest.mark.parametrize("t", MAIN_TYPES, ids=lambda t: NAMES[t])
+@pytest.mark.parametrize("x_dt", ["f32", "bf16"])
+def test_qmm_small_batch_fp32_bf16_activations(gpu, t, x_dt):
+    """Decode calls of 1-2 tokens with fp32 or bf16 activations round them to
+    f16 inside the GEMV; from 3 tokens on a conversion kernel does it first.
+    Both roundings are the same: the rows of an M=2 call equal the first two
+    rows of an M=3 call bit for bit, and both meet the bar against the oracle."""
+    torch = _torch()
+    dt = {"f32": torch.float32, "bf16": torch.bfloat16}[x_dt]
+    N, K = 1000, 4096
+    blocks = synth.make_blocks(t, N, K, seed=61)
+    x = torch.from_numpy(synth.make_activations(3, K, seed=62, dtype=np.float32)).to(dt)
+    w = gpu.Weight.register(blocks, t, N, K)
+    try:
+        xd = x.cuda()
+        y1 = gpu.qmatmul(w, xd[:1].contiguous())
+        y2 = gpu.qmatmul(w, xd[:2].contiguous())
+        y3 = gpu.qmatmul(w, xd)
+        torch.cuda.synchronize()
+        gpu.stream_sync()
+        assert torch.equal(y2, y3[:2]) and torch.equal(y1, y3[:1])
+        want = loader.qmatmul(t, blocks, N, K, x.float().numpy())
+        assert synth.rel_l2(y3.cpu().numpy(), want) < TOL
+    finally:
+        w.release()
