@@ -281,7 +281,10 @@ struct Cfg {
     static constexpr int S0 = Budget<TYPE, MT, G, CMAX>::S0;
     static constexpr int S = S0 > 8 ? 8 : S0;
     static constexpr int kConsumers = G * kThreads;
-    static constexpr int kAll = kConsumers + 32;        // + the producer warp
+    // Producer warps; warp w stages tokens 8w..8w+7 (one is enough up to 8
+    // tokens, measured: extra warps there cost 3 % at M = 1).
+    static constexpr int kXWarps = NT >= 2 ? 4 : 1;
+    static constexpr int kAll = kConsumers + 32 * kXWarps;
     static constexpr size_t smem = (size_t)S * (WB + XB) + COMB + RECV;
     static_assert(S >= 3, "pipeline too shallow");
 };
@@ -320,7 +323,9 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
 }
 
 // One CTA per SM: warps 0 .. 8G-1 are G consumer groups that take the CTA's
-// units in turn (group = unit index mod G), warp 8G is the producer.  CTA rank r of
+// units in turn (group = unit index mod G), the warps after them are producers
+// (one for up to 8 tokens, else four; the first also issues the tile-chunk
+// copies).  CTA rank r of
 // cluster q takes chunks [r K/C, (r+1) K/C) of every tile of the cluster, so
 // with C = 1 a CTA owns whole tiles and writes y directly; with C > 1 the
 // cluster owns one tile and ranks 1..C-1 push their partial sums into rank
@@ -331,14 +336,14 @@ template <int TYPE, int MT>
 __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const MmaParams p) {
     using Cf = Cfg<TYPE, MT>;
     constexpr int S = Cf::S, WB = Cf::WB, XB = Cf::XB, NT = Cf::NT, PB = Cf::PB;
-    constexpr int kGroups = Cf::G, kConsumers = Cf::kConsumers, kAll = Cf::kAll;
+    constexpr int kGroups = Cf::G, kConsumers = Cf::kConsumers, kAll = Cf::kAll, kXWarps = Cf::kXWarps;
     constexpr int RS = NT * 8;  // floats per row in a partial
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* wst = smem;                                       // S x WB
     uint8_t* xst = smem + (size_t)S * WB;                      // S x XB
     float* comb = reinterpret_cast<float*>(xst + (size_t)S * XB);           // (G-1) x 2 x PB
     float* recv = reinterpret_cast<float*>(xst + (size_t)S * XB + Cf::COMB);  // (CMAX-1) x PB
-    __shared__ uint64_t full[S];   // unit landed: tile-chunk bytes + 32 producer cp.async arrivals + 1
+    __shared__ uint64_t full[S];   // unit landed: tile-chunk bytes + one arrival per producer thread + 1
     __shared__ uint64_t empty[S];  // the 8 warps of the consuming group are done with the stage
     __shared__ uint64_t recv_full;  // cluster leader: the C-1 partials have landed
     __shared__ int s_abort;
@@ -358,7 +363,7 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
     for (int i = tid; i < S * XB / 16; i += kAll) reinterpret_cast<uint4*>(xst)[i] = make_uint4(0u, 0u, 0u, 0u);
     if (tid == 0) {
         for (int st = 0; st < S; ++st) {
-            ptx::mbar_init(&full[st], 33);
+            ptx::mbar_init(&full[st], 1 + 32 * kXWarps);
             ptx::mbar_init(&empty[st], kWarps);
         }
         ptx::mbar_init(&recv_full, 1);
@@ -382,17 +387,20 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     int w_issued = 0;  // producer lane 0: tile-chunk copies issued
-    if (warp == kGroups * kWarps) {
-        // ---- producer: lane 0 issues the tile-chunk bulk copies, all 32
-        // lanes the x pieces: piece (token, t4, m) holds the 8 elements
-        // x[token][k0 + 64 t4 + 8m ..] at index ((token / 8) * 8 + m) * 32 +
-        // 4 (token % 8) + t4.
+    if (warp >= kGroups * kWarps) {
+        // ---- producers: lane 0 of the first issues the tile-chunk bulk
+        // copies; producer warp pw copies the x pieces of tokens 8pw..8pw+7:
+        // piece (token, t4, m) holds the 8 elements x[token][k0 + 64 t4 + 8m ..]
+        // at index ((token / 8) * 8 + m) * 32 + 4 (token % 8) + t4.  Every
+        // producer thread arrives once per unit on the unit's full barrier,
+        // after the stage's previous unit was released.
+        const int pw = kXWarps == 1 ? 0 : warp - kGroups * kWarps;
         auto w_src = [&](int u) {
             const int ti = u / kr;
             return p.w + p.s.chunk_offset(q + (int64_t)ti * p.clusters, kc0 + (u - ti * kr));
         };
         const int pre = n < S ? n : S;
-        if (lane == 0)
+        if (pw == 0 && lane == 0)
             for (int u = 0; u < pre; ++u, ++w_issued) {
                 ptx::mbar_arrive_expect_tx(&full[u], WB);
                 ptx::bulk_g2s(wst + u * WB, w_src(u), WB, &full[u]);
@@ -406,7 +414,7 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
                 const int stg = u % S;
                 if (lane == 0) {
                     ok = ptx::mbar_wait(&empty[stg], (uint32_t)(u / S - 1) & 1u, ctl, 32) ? 1 : 0;
-                    if (ok) {
+                    if (ok && pw == 0) {
                         ptx::mbar_arrive_expect_tx(&full[stg], WB);
                         ptx::bulk_g2s(wst + stg * WB, w_src(u), WB, &full[stg]);
                         ++w_issued;
@@ -421,17 +429,19 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
             return (int64_t)(kc0 + u - ti * kr) * CHUNK_K;
         };
         if (p.x_dtype == NXQ_F16) {
+            // Lane (t4, m) = ((lane >> 3) & 3, lane & 7) copies piece (token, t4,
+            // m) of every token: one source row and one destination step apart.
             const __half* xh = static_cast<const __half*>(p.x);
+            const int t4 = (lane >> 3) & 3, m = lane & 7;
+            const int tok0 = 8 * pw, tok1 = M < tok0 + 8 ? M : tok0 + 8;
             for (int u = 0; u < n; ++u) {
                 if (!refill(u)) break;
-                uint4* xd = reinterpret_cast<uint4*>(xst + (u % S) * XB);
-                const int64_t k0 = chunk_k0(u);
-                for (int i = lane; i < M * 32; i += 32) {
-                    const int tok = i >> 5, t4 = (i >> 3) & 3, m = i & 7;
-                    const int64_t k = k0 + 64 * t4 + 8 * m;
-                    cp_async16_zfill(xd + ((tok >> 3) * 8 + m) * 32 + 4 * (tok & 7) + t4,
-                                     xh + (int64_t)tok * K + (k < K ? k : 0), k < K ? 16u : 0u);
-                }
+                uint4* xd = reinterpret_cast<uint4*>(xst + (u % S) * XB) + m * 32 + t4;
+                const int64_t k = chunk_k0(u) + 64 * t4 + 8 * m;
+                const uint32_t bytes = k < K ? 16u : 0u;
+                const __half* src = xh + (k < K ? k : 0) + (int64_t)tok0 * K;
+                for (int tok = tok0; tok < tok1; ++tok, src += K)
+                    cp_async16_zfill(xd + ((tok >> 3) << 8) + ((tok & 7) << 2), src, bytes);
                 cp_async_arrive(&full[u % S]);
             }
         } else {
@@ -487,12 +497,19 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
                 ptx::mbar_arrive(&full[u % S]);
             };
             int u = 0;
-            for (; u < n; ++u) {
-                if (!refill(u)) break;
-                if (u > 0) finish(u - 1);
-                issue(u);
+            if (pw == 0) {
+                for (; u < n; ++u) {
+                    if (!refill(u)) break;
+                    if (u > 0) finish(u - 1);
+                    issue(u);
+                }
+                if (u == n && n > 0) finish(n - 1);
+            } else {
+                for (; u < n; ++u) {
+                    if (!refill(u)) break;
+                    ptx::mbar_arrive(&full[u % S]);
+                }
             }
-            if (u == n && n > 0) finish(n - 1);
         }
     } else {
         // ---- consumers: group gi takes the units c = gi mod G of each tile ----
