@@ -21,22 +21,22 @@
 //   - the activations are staged in their natural order, 8 elements per
 //     16-byte piece, in lane order so the fragment loads are conflict-free.
 //
-// Decomposition (shared with the tcgen05 kernels): the weight is stored tiled
-// (formats.cuh), a unit is one tile-chunk (128 rows x 256 k, contiguous in
-// HBM), and a persistent grid of one or two CTAs per SM takes contiguous unit
-// ranges (stream-K).  A tile split between CTAs is summed by the last of them
-// to finish (per-tile counter, fp32 partials in a workspace, CTA order), so
-// the result is deterministic; each CTA processes its split tiles first, so
-// those fixups overlap the rest of its work instead of trailing it.
+// Decomposition: the weight is stored tiled (formats.cuh: 128-row tiles x
+// 256-k chunks, each tile-chunk contiguous, a tile's chunks in order).  A
+// unit is one tile-chunk, one bulk copy.  One CTA per SM; cluster q of Q owns
+// a contiguous range of tiles, and the C CTAs of a cluster split K, their
+// partial sums meeting in the leader's shared memory.  (Measured: cutting the
+// rows finer than tiles, so that every SM gets the same share, was slower -
+// a unit that straddles two tiles costs more than the balance gains.)
 //
-// Per CTA, 8 warps; warp w owns weight rows 16w..16w+15 of the tile.  Lane
+// Per consumer group, 8 warps; warp w owns rows 16w..16w+15 of the tile.  Lane
 // (g, t) (g = lane/4, t = lane%4) holds rows 16w+g and 16w+8+g, and the mma's
 // k-slots {2t, 2t+1, 2t+8, 2t+9} of k-step j map to chunk elements
 // 64t + 4j + {0, 1, 2, 3}, for x and W alike: every lane decodes one private
 // 64-element slice of two rows, exactly the sub-blocks whose scales it alone
-// needs.  Units are staged with cp.async into an S-deep shared-memory ring:
-// the packed tile-chunk byte for byte, and x as 16-byte pieces
-// x[token][64t + 8m .. 64t + 8m + 7] at piece index (n8 tile, m, lane).
+// needs.  Units are staged into an S-deep shared-memory ring: the window's
+// row records byte for byte by bulk copies, and x by cp.async as 16-byte
+// pieces x[token][64t + 8m .. 64t + 8m + 7] at piece index (n8 tile, m, lane).
 //
 // Numerics: each weight is formed in f16 as fl16(q * fl16(d*sc) + fl16(-dmin*m))
 // (Q4_K; the other types analogously), products are exact and accumulate in
@@ -298,7 +298,8 @@ struct MmaParams {
     void* y;
     int y_dtype;
     int C;         // CTAs per cluster: the reduction is split C ways inside a cluster
-    int clusters;  // cluster q takes tiles q, q + clusters, ...
+    int clusters;  // Q
+    int tile_base, tile_rem;  // cluster q owns tile_base + (q < tile_rem) tiles, in order
     DeviceStatus* status;
 };
 
@@ -325,13 +326,13 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
 // One CTA per SM: warps 0 .. 8G-1 are G consumer groups that take the CTA's
 // units in turn (group = unit index mod G), the warps after them are producers
 // (one for up to 8 tokens, else four; the first also issues the tile-chunk
-// copies).  CTA rank r of
-// cluster q takes chunks [r K/C, (r+1) K/C) of every tile of the cluster, so
-// with C = 1 a CTA owns whole tiles and writes y directly; with C > 1 the
-// cluster owns one tile and ranks 1..C-1 push their partial sums into rank
-// 0's shared memory (one bulk copy each, completing on an mbarrier there),
-// which adds them in rank order: no global-memory round trip and a result
-// that does not depend on timing.
+// copies).  Cluster q owns a contiguous range of tiles; CTA rank r of the
+// cluster takes chunks [r K/C, (r+1) K/C) of each, so with C = 1 a CTA owns
+// whole tiles and writes y directly; with C > 1 the cluster owns one tile and
+// ranks 1..C-1 push their partial sums into rank 0's shared memory (one bulk
+// copy each, completing on an mbarrier there), which adds them in rank order:
+// no global-memory round trip and a result that does not depend on timing.
+// A CTA's units are consecutive tile-chunks in memory in either case.
 template <int TYPE, int MT>
 __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const MmaParams p) {
     using Cf = Cfg<TYPE, MT>;
@@ -351,17 +352,29 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, tq = lane & 3;
     const int C = p.C, rank = (int)(blockIdx.x % (unsigned)C), q = (int)(blockIdx.x / (unsigned)C);
-    const int T = (int)p.s.tiles, Kc = (int)p.s.chunks;
+    const int Kc = (int)p.s.chunks;
     const int kc0 = rank * Kc / C, kr = (rank + 1) * Kc / C - kc0;
-    const int ntiles = q < T ? (T - 1 - q) / p.clusters + 1 : 0;
+    const int t0 = q * p.tile_base + (q < p.tile_rem ? q : p.tile_rem);
+    const int ntiles = p.tile_base + (q < p.tile_rem ? 1 : 0);
     const int n = ntiles * kr;
     const int64_t K = p.s.K, N = p.s.N;
     const int M = (int)p.M;
 
-    // Token slots at or beyond M are never loaded; zero them once so the
-    // fragment loads need no predicate.
-    for (int i = tid; i < S * XB / 16; i += kAll) reinterpret_cast<uint4*>(xst)[i] = make_uint4(0u, 0u, 0u, 0u);
-    if (tid == 0) {
+    // Unit u's tile-chunk: tiles t0 .. t0 + ntiles - 1 hold chunks kc0 ..
+    // kc0 + kr - 1 each, and either ntiles = 1 or kr = all chunks, so the
+    // units are consecutive tile-chunks from w_base on.
+    const uint8_t* const w_base = p.w + p.s.chunk_offset(t0, kc0);
+    auto w_issue = [&](int u, int stg) {
+        ptx::mbar_arrive_expect_tx(&full[stg], WB);
+        ptx::bulk_g2s(wst + stg * WB, w_base + (int64_t)u * WB, WB, &full[stg]);
+    };
+
+    int w_issued = 0;  // producer lane 0: tile-chunk copies issued
+    if (tid == kConsumers) {
+        // Barriers first, then the first units' weight copies at once: the
+        // weights are immutable once registered, so they are requested before
+        // griddepcontrol.wait (programmatic dependent launch, below) and
+        // before the rest of the CTA has finished its set-up.
         for (int st = 0; st < S; ++st) {
             ptx::mbar_init(&full[st], 1 + 32 * kXWarps);
             ptx::mbar_init(&empty[st], kWarps);
@@ -373,7 +386,11 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
                          : "memory");
         s_abort = 0;
         ptx::fence_mbar_init();
+        for (; w_issued < (n < S ? n : S); ++w_issued) w_issue(w_issued, w_issued);
     }
+    // Token slots at or beyond M are never loaded; zero them once so the
+    // fragment loads need no predicate.
+    for (int i = tid; i < S * XB / 16; i += kAll) reinterpret_cast<uint4*>(xst)[i] = make_uint4(0u, 0u, 0u, 0u);
     if (C > 1)
         cluster_sync();  // barriers initialised before any rank pushes to the leader
     else
@@ -382,11 +399,9 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
     // Programmatic dependent launch: the next kernel of the stream may be
     // scheduled as soon as every CTA of this grid has started; this grid reads
     // x and writes y only after griddepcontrol.wait (the previous kernel has
-    // completed and its memory is visible).  The weights are immutable once
-    // registered, so the producer requests the first tile-chunks before it.
+    // completed and its memory is visible).
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-    int w_issued = 0;  // producer lane 0: tile-chunk copies issued
     if (warp >= kGroups * kWarps) {
         // ---- producers: lane 0 of the first issues the tile-chunk bulk
         // copies; producer warp pw copies the x pieces of tokens 8pw..8pw+7:
@@ -395,16 +410,6 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
         // producer thread arrives once per unit on the unit's full barrier,
         // after the stage's previous unit was released.
         const int pw = kXWarps == 1 ? 0 : warp - kGroups * kWarps;
-        auto w_src = [&](int u) {
-            const int ti = u / kr;
-            return p.w + p.s.chunk_offset(q + (int64_t)ti * p.clusters, kc0 + (u - ti * kr));
-        };
-        const int pre = n < S ? n : S;
-        if (pw == 0 && lane == 0)
-            for (int u = 0; u < pre; ++u, ++w_issued) {
-                ptx::mbar_arrive_expect_tx(&full[u], WB);
-                ptx::bulk_g2s(wst + u * WB, w_src(u), WB, &full[u]);
-            }
         asm volatile("griddepcontrol.wait;" ::: "memory");
         // Refills stage u % S with unit u's tile-chunk once its consumers are
         // done with unit u - S (lane 0); false if the wait gave up.
@@ -415,8 +420,7 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
                 if (lane == 0) {
                     ok = ptx::mbar_wait(&empty[stg], (uint32_t)(u / S - 1) & 1u, ctl, 32) ? 1 : 0;
                     if (ok && pw == 0) {
-                        ptx::mbar_arrive_expect_tx(&full[stg], WB);
-                        ptx::bulk_g2s(wst + stg * WB, w_src(u), WB, &full[stg]);
+                        w_issue(u, stg);
                         ++w_issued;
                     }
                 }
@@ -434,10 +438,10 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
             const __half* xh = static_cast<const __half*>(p.x);
             const int t4 = (lane >> 3) & 3, m = lane & 7;
             const int tok0 = 8 * pw, tok1 = M < tok0 + 8 ? M : tok0 + 8;
-            for (int u = 0; u < n; ++u) {
+            for (int u = 0, c = 0; u < n; ++u, c = c + 1 == kr ? 0 : c + 1) {
                 if (!refill(u)) break;
                 uint4* xd = reinterpret_cast<uint4*>(xst + (u % S) * XB) + m * 32 + t4;
-                const int64_t k = chunk_k0(u) + 64 * t4 + 8 * m;
+                const int64_t k = (int64_t)(kc0 + c) * CHUNK_K + 64 * t4 + 8 * m;
                 const uint32_t bytes = k < K ? 16u : 0u;
                 const __half* src = xh + (k < K ? k : 0) + (int64_t)tok0 * K;
                 for (int tok = tok0; tok < tok1; ++tok, src += K)
@@ -572,7 +576,7 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
                     acc[nt][3] += b.y;
                 }
             }
-            const int64_t tile = q + (int64_t)ti * p.clusters;
+            const int64_t tile = t0 + ti;
             if (C == 1) {
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
@@ -657,34 +661,66 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
 bool g_mma_enabled = true;
 int g_sm_count = 0;
 
+// How many clusters of 2, 4, 8 CTAs of a variant fit on the GPU at once
+// (index log2 C); a split never launches more, so it runs in one wave.
+template <int TYPE, int MT>
+int* max_clusters() {
+    static int q[4] = {0, 0, 0, 0};
+    return q;
+}
+
 template <int TYPE, int MT>
 int set_attr() {
     using Cf = Cfg<TYPE, MT>;
     cudaError_t e = cudaFuncSetAttribute(mma_gemv_kernel<TYPE, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)Cf::smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute (mma_gemv)");
+    int* mq = max_clusters<TYPE, MT>();
+    mq[0] = g_sm_count;
+    for (int lc = 1, c = 2; c <= Cf::CMAX; ++lc, c *= 2) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(c * 64));
+        cfg.blockDim = dim3(Cf::kAll);
+        cfg.dynamicSmemBytes = Cf::smem;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = (unsigned)c;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int nq = 0;
+        e = cudaOccupancyMaxActiveClusters(&nq, mma_gemv_kernel<TYPE, MT>, &cfg);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters (mma_gemv)");
+        mq[lc] = nq;
+    }
     return NXQ_OK;
 }
 
-// Split of the reduction across a cluster: C = 1 (whole tiles per CTA, one
-// wave of at most one CTA per SM, several tiles per CTA beyond that) or, when
-// the weight has fewer tiles than SMs, C ranks per tile with one tile per
-// cluster.  Picks the C with the fewest tile-chunks per CTA (the smallest C
-// among equals).
-void pick_split(const TiledShape& s, int cmax, int* C, int* clusters) {
-    const int64_t T = s.tiles, Kc = s.chunks, P = g_sm_count;
+// Work split: C CTAs per cluster (K cut C ways) and Q clusters, at most as
+// many as fit on the GPU at once (one wave).  C = 1: every CTA owns
+// ceil or floor of T / P whole tiles; C > 1 (only when the weight has few
+// enough tiles): one tile per cluster.  Picks the split with the fewest units
+// per CTA, the smallest C among equals.
+void pick_split(const TiledShape& s, const int* maxq, int cmax, MmaParams* p) {
+    const int64_t T = s.tiles, Kc = s.chunks;
     int best_c = 1;
-    int64_t best = ((T + P - 1) / P) * Kc;
-    for (int c = 2; c <= cmax && c <= Kc; c *= 2) {
-        if (T * c > P) break;
+    int64_t best_q = T < g_sm_count ? T : g_sm_count;
+    int64_t best = ((T + best_q - 1) / best_q) * Kc;
+    for (int lc = 1, c = 2; c <= cmax && c <= Kc; ++lc, c *= 2) {
+        const int64_t qmax = g_sm_count / c < maxq[lc] ? g_sm_count / c : maxq[lc];
+        if (T > qmax) continue;
         const int64_t cost = (Kc + c - 1) / c;
         if (cost < best) {
             best = cost;
             best_c = c;
+            best_q = T;
         }
     }
-    *C = best_c;
-    *clusters = (int)(best_c == 1 ? (T < P ? T : P) : T);
+    p->C = best_c;
+    p->clusters = (int)best_q;
+    p->tile_base = (int)(T / best_q);
+    p->tile_rem = (int)(T % best_q);
 }
 
 template <int TYPE, int MT>
@@ -698,7 +734,8 @@ int launch(const Weight* w, const void* x, int x_dtype, void* y, int y_dtype, in
     p.M = M;
     p.y = y;
     p.y_dtype = y_dtype;
-    pick_split(w->shape, Cf::CMAX, &p.C, &p.clusters);
+    if (w->shape.tile_chunk_bytes != Cf::WB) return fail(NXQ_ERR_SHAPE, "mma_gemv: tile-chunk of %lld bytes, kernel stage %d", (long long)w->shape.tile_chunk_bytes, Cf::WB);
+    pick_split(w->shape, max_clusters<TYPE, MT>(), Cf::CMAX, &p);
     p.status = context_status();
     // Launched with programmatic stream serialization (see the kernel's
     // griddepcontrol.wait): it may start while the previous kernel drains.
