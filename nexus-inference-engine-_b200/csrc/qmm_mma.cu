@@ -285,6 +285,11 @@ struct Cfg {
     // tokens, measured: extra warps there cost 3 % at M = 1).
     static constexpr int kXWarps = NT >= 2 ? 4 : 1;
     static constexpr int kAll = kConsumers + 32 * kXWarps;
+    // A warp's 16 mma per unit chain through its accumulators; with one n8
+    // tile Q4_K alternates two accumulator sets (two chains of 8, added at the
+    // tile's end).  Measured: 2-3 % faster there, no gain or slower for the
+    // other formats and for more tiles.
+    static constexpr int kAccSets = (NT == 1 && TYPE == T_Q4_K) ? 2 : 1;
     static constexpr size_t smem = (size_t)S * (WB + XB) + COMB + RECV;
     static_assert(S >= 3, "pipeline too shallow");
 };
@@ -523,11 +528,16 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
         for (int ti = 0; ti < ntiles; ++ti) {
             // acc[n8 token tile][c0..c3]: c0/c1 = row 16wg+g, tokens 8nt+2t,
             // 8nt+2t+1; c2/c3 = row 16wg+8+g.
-            float acc[NT][4];
+            float acc[NT][4], acc2[Cf::kAccSets == 2 ? NT : 1][4];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) acc[nt][e] = 0.0f;
+            if constexpr (Cf::kAccSets == 2)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) acc2[nt][e] = 0.0f;
             for (int c = gi; c < kr; c += kGroups) {
                 const int u = ti * kr + c, stg = u % S;
                 if (!dead && !ptx::mbar_wait(&full[stg], (uint32_t)(u / S) & 1u, ctl, 31)) dead = true;
@@ -545,13 +555,21 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
                         for (int nt = 0; nt < NT; ++nt) {
                             const uint4 xv = xs[(nt * 8 + m) * 32];
                             mma16816(acc[nt], pa[0], pb[0], pa[1], pb[1], xv.x, xv.y);
-                            mma16816(acc[nt], pa[2], pb[2], pa[3], pb[3], xv.z, xv.w);
+                            if constexpr (Cf::kAccSets == 2)
+                                mma16816(acc2[nt], pa[2], pb[2], pa[3], pb[3], xv.z, xv.w);
+                            else
+                                mma16816(acc[nt], pa[2], pb[2], pa[3], pb[3], xv.z, xv.w);
                         }
                     }
                 }
                 __syncwarp();
                 if (lane == 0) ptx::mbar_arrive(&empty[stg]);
             }
+            if constexpr (Cf::kAccSets == 2)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) acc[nt][e] += acc2[nt][e];
             // ---- tile end: groups 1.. hand their partials to group 0 ----
             const int r0 = 16 * wg + g;
             if (gi > 0) {
