@@ -9,7 +9,7 @@
 // Work: a persistent grid of one CTA per SM walks (weight tile, token tile)
 // work tiles of 128 weight rows x 256 tokens.  Per 64-element k-step:
 //   warp 26      producer: the packed tile-chunk (256 k) by one 1-D bulk copy
-//                per chunk, up to four chunks ahead
+//                per chunk, up to four chunks ahead (Rings)
 //   warp 0       producer: the 256 x 64 f16 activation box by TMA (128-byte
 //                swizzle, no multicast), four k-steps ahead
 //   warps 2-17   four dequant warpgroups: thread r decodes row r's 32-element
@@ -20,7 +20,10 @@
 //                (A from TMEM, B from shared memory) into a 256-column fp32
 //                accumulator in TMEM
 //   warps 18-25  epilogue: tcgen05.ld of the accumulator (two warps per lane
-//                quadrant, half the token columns each), conversion, store
+//                quadrant), conversion, store
+// (Measured: two N=128 mma per K=16 into accumulator halves handed back
+// separately, so the next tile starts while the second half drains, ran 18 %
+// slower than one N=256 mma.)
 // Every wait is bounded (sm100_ptx.cuh).
 //
 // Numerics as the decode kernels: weights rounded once to f16, activations
@@ -49,19 +52,23 @@ constexpr int kThreads = 32 * (kWarpWProducer + 1);
 constexpr int kNT = 256;              // tokens per work tile (MMA N)
 constexpr int kKS = 64;               // reduction elements per k-step (one swizzle atom)
 constexpr int kStepsPerChunk = CHUNK_K / kKS;
-constexpr int kXStages = 4;
 constexpr int kAStages = 4;           // TMEM A buffers of 32 columns
 constexpr uint32_t kColD = 256;       // accumulator: columns 256..511
 constexpr uint32_t kTmemCols = 512;
 constexpr int kXBytes = kNT * kKS * 2;  // 32 KB per k-step
 
 // Tile-chunk ring depth: as many stages (up to 4) as fit next to the x ring.
+// Ring depths: four activation stages (measured: a fifth, in place of a
+// tile-chunk stage, gains nothing), then as many tile-chunk stages (up to 4)
+// as fit.
 template <int TYPE>
-struct WRing {
+struct Rings {
     static constexpr int WB = dq::Group<TYPE>::kStage;
-    static constexpr int fit = (227 * 1024 - 1024 - 256 - kXStages * kXBytes) / WB;
-    static constexpr int kStages = fit > 4 ? 4 : fit;
-    static_assert(kStages >= 2, "tile-chunk ring too shallow");
+    static constexpr int kBudget = 227 * 1024 - 1024 - 256;
+    static constexpr int kX = 4;
+    static constexpr int fit = (kBudget - kX * kXBytes) / WB;
+    static constexpr int kW = fit > 4 ? 4 : fit;
+    static_assert(kW >= 2, "tile-chunk ring too shallow");
 };
 
 struct GemmParams {
@@ -75,13 +82,27 @@ struct GemmParams {
     DeviceStatus* status;
 };
 
-__device__ __forceinline__ void store_y(void* y, int dt, int64_t i, float v) {
-    if (dt == NXQ_F32)
-        reinterpret_cast<float*>(y)[i] = v;
-    else if (dt == NXQ_F16)
-        reinterpret_cast<__half*>(y)[i] = __float2half_rn(v);
-    else
-        reinterpret_cast<__nv_bfloat16*>(y)[i] = __float2bfloat16_rn(v);
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// y[m0 + j][n] = v[j] for j < cnt (element offset `off` = m0 * N + n).
+template <typename T>
+__device__ __forceinline__ void store_col(void* y, int64_t off, int64_t N, int cnt, const uint32_t (&v)[32]) {
+    T* q = reinterpret_cast<T*>(y) + off;
+    if (cnt == 32) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j, q += N) *q = from_f32<T>(__uint_as_float(v[j]));
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j, q += N)
+            if (j < cnt) *q = from_f32<T>(__uint_as_float(v[j]));
+    }
 }
 
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const ptx::WaitCtl& c, unsigned where) {
@@ -103,7 +124,7 @@ __device__ __forceinline__ void dq_step(const uint8_t* stage, int r, int h, uint
 template <int TYPE>
 __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p, const __grid_constant__ CUtensorMap xmap) {
     constexpr int WB = dq::Group<TYPE>::kStage;
-    constexpr int kWStages = WRing<TYPE>::kStages;
+    constexpr int kXStages = Rings<TYPE>::kX, kWStages = Rings<TYPE>::kW;
     constexpr uint32_t IDESC = ptx::idesc_f16_f32(128, kNT);
 
     extern __shared__ uint8_t smem_raw[];
@@ -264,8 +285,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p
             }
         }
     } else {
-        const int ew = warp - kWarpEpi0, quad = warp & 3, r = quad * 32 + lane;
-        const int half = ew >> 2;  // which 128 token columns
+        // Epilogue: warp (quad, sub) reads TMEM lanes 32 quad .. (its lane
+        // quadrant) = weight row n, and token columns 128 sub .. 128 sub + 127.
+        const int ew = warp - kWarpEpi0, quad = warp & 3, r = quad * 32 + lane, sub = ew >> 2;
         const int64_t M = p.M, N = p.s.N;
         uint32_t nt = 0;
         for (int tile = blockIdx.x; tile < p.tiles; tile += G, ++nt) {
@@ -273,20 +295,23 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p
             ptx::tc_fence_after();
             const int wt = tile / p.m_tiles, mt = tile - wt * p.m_tiles;
             const int64_t n = (int64_t)wt * TILE_ROWS + r;
-            const int64_t m0 = (int64_t)mt * kNT + half * (kNT / 2);
 #pragma unroll 1
-            for (int cb = 0; cb < kNT / 2 / 32; ++cb) {
+            for (int cb = 0; cb < 4; ++cb) {
                 uint32_t v[32];
-                const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + kColD + half * (kNT / 2) + 32 * cb;
+                const int c0 = sub * (kNT / 2) + 32 * cb;  // token column in the tile
+                const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + kColD + c0;
                 ptx::tmem_ld16(ta, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
                 ptx::tmem_ld16(ta + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
                 ptx::tmem_wait_ld();
-                if (n < N) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int64_t m = m0 + 32 * cb + j;
-                        if (m < M) store_y(p.y, p.y_dtype, m * N + n, __uint_as_float(v[j]));
-                    }
+                const int64_t m0 = (int64_t)mt * kNT + c0;
+                const int cnt = M - m0 >= 32 ? 32 : (int)(M - m0);
+                if (n < N && cnt > 0) {
+                    if (p.y_dtype == NXQ_BF16)
+                        store_col<__nv_bfloat16>(p.y, m0 * N + n, N, cnt, v);
+                    else if (p.y_dtype == NXQ_F16)
+                        store_col<__half>(p.y, m0 * N + n, N, cnt, v);
+                    else
+                        store_col<float>(p.y, m0 * N + n, N, cnt, v);
                 }
             }
             ptx::tc_fence_before();
@@ -311,7 +336,7 @@ bool g_gemm_enabled = true;
 
 template <int TYPE>
 size_t smem_bytes() {
-    return 1024 + (size_t)kXStages * kXBytes + (size_t)WRing<TYPE>::kStages * dq::Group<TYPE>::kStage + 256;
+    return 1024 + (size_t)Rings<TYPE>::kX * kXBytes + (size_t)Rings<TYPE>::kW * dq::Group<TYPE>::kStage + 256;
 }
 
 template <int TYPE>
