@@ -52,7 +52,8 @@ constexpr int kThreads = 32 * (kWarpWProducer + 1);
 constexpr int kNT = 256;              // tokens per work tile (MMA N)
 constexpr int kKS = 64;               // reduction elements per k-step (one swizzle atom)
 constexpr int kStepsPerChunk = CHUNK_K / kKS;
-constexpr int kAStages = 4;           // TMEM A buffers of 32 columns
+constexpr int kAStages = 4;           // TMEM A buffers of 32 columns (measured: 8 gain nothing)
+constexpr int kBarBytes = 512;        // mbarriers, TMEM address, abort flag
 constexpr uint32_t kColD = 256;       // accumulator: columns 256..511
 constexpr uint32_t kTmemCols = 512;
 constexpr int kXBytes = kNT * kKS * 2;  // 32 KB per k-step
@@ -64,7 +65,7 @@ constexpr int kXBytes = kNT * kKS * 2;  // 32 KB per k-step
 template <int TYPE>
 struct Rings {
     static constexpr int WB = dq::Group<TYPE>::kStage;
-    static constexpr int kBudget = 227 * 1024 - 1024 - 256;
+    static constexpr int kBudget = 227 * 1024 - 1024 - kBarBytes;
     static constexpr int kX = 4;
     static constexpr int fit = (kBudget - kX * kXBytes) / WB;
     static constexpr int kW = fit > 4 ? 4 : fit;
@@ -125,6 +126,8 @@ template <int TYPE>
 __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p, const __grid_constant__ CUtensorMap xmap) {
     constexpr int WB = dq::Group<TYPE>::kStage;
     constexpr int kXStages = Rings<TYPE>::kX, kWStages = Rings<TYPE>::kW;
+    static_assert((2 * kXStages + 2 * kWStages + 2 * kAStages + 3) * 8 + 8 <= kBarBytes, "barrier area too small");
+    static_assert(kAStages * 32 <= (int)kColD, "A stages overlap the accumulator");
     constexpr uint32_t IDESC = ptx::idesc_f16_f32(128, kNT);
 
     extern __shared__ uint8_t smem_raw[];
@@ -336,7 +339,7 @@ bool g_gemm_enabled = true;
 
 template <int TYPE>
 size_t smem_bytes() {
-    return 1024 + (size_t)Rings<TYPE>::kX * kXBytes + (size_t)Rings<TYPE>::kW * dq::Group<TYPE>::kStage + 256;
+    return 1024 + (size_t)Rings<TYPE>::kX * kXBytes + (size_t)Rings<TYPE>::kW * dq::Group<TYPE>::kStage + kBarBytes;
 }
 
 template <int TYPE>
