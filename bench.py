@@ -68,6 +68,19 @@ def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
 
+# The result line goes to a private copy of the original stdout; file
+# descriptor 1 itself is pointed at stderr, so banners that native libraries
+# write there (NCCL prints its version at communicator set-up) cannot land
+# next to the one JSON line.
+_RESULT = None
+
+
+def emit(line: dict) -> None:
+    out = _RESULT if _RESULT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def peaks() -> tuple[dict, str]:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -248,7 +261,7 @@ def run_reference_arm(args, rank, world):
                        "sample": sample},
             "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
             "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -706,7 +719,7 @@ def run_gpu_arm(args, rank, world, local):
             "cpu_baseline": cpu, "nominal_hbm_frac": value / world / 8000.0,
         }
         line.update(extra)
-        print(json.dumps(line), flush=True)
+        emit(line)
     return 0
 
 
@@ -722,6 +735,10 @@ def main() -> int:
     ap.add_argument("--no-configs", action="store_true", help="skip configs 1, 3 and 5")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
+    global _RESULT
+    sys.stdout.flush()
+    _RESULT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     if args.warmup < 3:
         log("warmup raised to 3 (minimum)")
         args.warmup = 3

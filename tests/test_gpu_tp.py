@@ -1,0 +1,115 @@
+"""GPU, world_size 2 (skipped with fewer than two GPUs): the tensor-parallel
+entry point nxq_tp_qmatmul over NCCL against the unsharded oracle output.
+
+Each rank registers its shard with nxq_weight_register_shard and runs the COL
+split (the full x, its [M][N/2] slice of y) and the ROW split (its K/2 slice
+of x; the library's fp32 NCCL allreduce leaves the full [M][N] on every rank).
+The COL slices are gathered over gloo; both results must be within the parity
+bar (rel-L2 <= 1e-3, fp32 accumulation) of loader.qmatmul on the whole weight,
+for decode (M <= 32, mma_gemv) and prefill (M > 32, tc_gemm) batch sizes.
+"""
+from __future__ import annotations
+
+import os
+import socket
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+ROOT = Path(__file__).resolve().parents[1]
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, t, N, K, Ms, q):
+    sys.path.insert(0, str(ROOT))
+    sys.path.insert(0, str(ROOT / "nexus-inference-engine-_b200"))
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import nxq
+    from nxq import synth
+    from oracle import loader
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    joined = False
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        nxq.init(rank)
+        uid = [nxq.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        nxq.tp_init(rank, world, uid[0])
+        joined = True
+        blocks = synth.make_blocks(t, N, K, seed=91)
+        res = {}
+        for M in Ms:
+            xh = torch.from_numpy(synth.make_activations(M, K, seed=92 + M).astype(np.float32)).half()
+            full = loader.qmatmul(t, blocks, N, K, xh.float().numpy(), nthreads=4)
+
+            w = nxq.Weight.register_shard(blocks, t, N, K, nxq.SPLIT_COL, rank, world)
+            y = torch.empty(M, N // world, dtype=torch.float32, device=dev)
+            nxq.tp_qmatmul(w, xh.to(dev), y, nxq.SPLIT_COL)
+            torch.cuda.synchronize(dev)
+            w.release()
+            parts = [torch.zeros(M, N // world) for _ in range(world)]
+            dist.all_gather(parts, y.cpu())
+            res[("col", M)] = synth.rel_l2(torch.cat(parts, dim=1).numpy(), full)
+
+            k_loc = K // world
+            w = nxq.Weight.register_shard(blocks, t, N, K, nxq.SPLIT_ROW, rank, world)
+            xs = xh[:, rank * k_loc:(rank + 1) * k_loc].contiguous().to(dev)
+            y = torch.empty(M, N, dtype=torch.float32, device=dev)
+            nxq.tp_qmatmul(w, xs, y, nxq.SPLIT_ROW)
+            torch.cuda.synchronize(dev)
+            w.release()
+            res[("row", M)] = synth.rel_l2(y.cpu().numpy(), full)
+        q.put((rank, res))
+    finally:
+        if joined:
+            nxq.tp_shutdown()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("t", [11, 12], ids=["Q3_K", "Q4_K"])
+def test_tp_qmatmul_two_gpus_matches_full(t):
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    world, N, K, Ms = 2, 1024, 4096, (1, 8, 40)
+    procs = [ctx.Process(target=_worker, args=(r, world, port, t, N, K, Ms, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        for p in procs:
+            p.join(300)
+            assert p.exitcode == 0
+    finally:
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+    out = dict(q.get(timeout=5) for _ in range(world))
+    for rank in range(world):
+        for key, err in out[rank].items():
+            assert err < TOL, (rank, key, err)
