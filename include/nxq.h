@@ -51,7 +51,8 @@ typedef enum {
     NXQ_ERR_NOMEM = -6,       /* device or host allocation failed              */
     NXQ_ERR_STATE = -7,       /* not initialised / wrong device / TP not set up */
     NXQ_ERR_NCCL = -8,        /* NCCL unavailable or a collective failed       */
-    NXQ_ERR_UNSUPPORTED = -9  /* no GPU of the required architecture           */
+    NXQ_ERR_UNSUPPORTED = -9, /* no GPU of the required architecture           */
+    NXQ_ERR_FORMAT = -10      /* a file that is not GGUF v2/v3 or is truncated */
 } nxq_status;
 
 /* Block types: the GGUF type ids of nexus/src/import/gguf_importer.h:28-57. */
@@ -212,6 +213,68 @@ NXQ_API int nxq_tp_qmatmul(nxq_weight_t shard, const void* x_dev, int x_dtype, v
 
 /* Sum `count` fp32 values across the TP group in place on `stream`. */
 NXQ_API int nxq_tp_allreduce_f32(float* buf_dev, int64_t count, void* stream);
+
+/* ---- residency loader: GGUF v2/v3 files straight into HBM ---------------------
+ * Replaces the reference's import path (GGUFImporter::parse_gguf,
+ * gguf_importer.cpp:359-455: header, metadata key/values, tensor index, data
+ * section aligned to general.alignment, default 32) followed by mmap +
+ * wrap_pointer streaming (compute_dispatch.cpp:142-154): the file is mapped
+ * read-only, every field is bounds-checked against the file size, and a
+ * tensor's blocks go from the mapping to the tiled HBM copy in one
+ * registration.  Parsing needs no GPU; registration needs nxq_init.  Metadata
+ * arrays are skipped (their element type and count are kept), as the
+ * reference does.  A malformed or truncated file is NXQ_ERR_FORMAT. */
+typedef struct nxq_gguf_s* nxq_gguf_t;
+
+/* GGUF metadata value types (GGUFValueType, gguf_importer.h:60-74). */
+typedef enum {
+    NXQ_GGUF_U8 = 0, NXQ_GGUF_I8 = 1, NXQ_GGUF_U16 = 2, NXQ_GGUF_I16 = 3,
+    NXQ_GGUF_U32 = 4, NXQ_GGUF_I32 = 5, NXQ_GGUF_F32 = 6, NXQ_GGUF_BOOL = 7,
+    NXQ_GGUF_STRING = 8, NXQ_GGUF_ARRAY = 9, NXQ_GGUF_U64 = 10, NXQ_GGUF_I64 = 11,
+    NXQ_GGUF_F64 = 12
+} nxq_gguf_value_type;
+
+NXQ_API int nxq_gguf_open(const char* path, nxq_gguf_t* out);
+NXQ_API int nxq_gguf_close(nxq_gguf_t g);
+
+/* Format version (2 or 3), data-section alignment and offset. */
+NXQ_API int nxq_gguf_header(nxq_gguf_t g, uint32_t* version, uint64_t* alignment,
+                            uint64_t* data_start);
+
+NXQ_API int nxq_gguf_tensor_count(nxq_gguf_t g, int64_t* n);
+
+/* Tensor i of the index: name (NUL-terminated, truncated to name_len), GGUF type
+ * id, dims (dims[0] is the fastest-varying; up to 4, unused ones 1), offset from
+ * the data section and size in bytes (0 for a type nxq does not know). */
+NXQ_API int nxq_gguf_tensor_info(nxq_gguf_t g, int64_t i, char* name, size_t name_len, int* type,
+                                 int* n_dims, int64_t dims[4], uint64_t* offset, uint64_t* bytes);
+
+/* Index of the tensor called `name`; NXQ_ERR_ARG if there is none. */
+NXQ_API int nxq_gguf_find(nxq_gguf_t g, const char* name, int64_t* index);
+
+/* Host pointer to tensor i's bytes inside the mapping (valid until close). */
+NXQ_API int nxq_gguf_tensor_data(nxq_gguf_t g, int64_t i, const void** data, uint64_t* bytes);
+
+/* Metadata: key i and its value type; scalar values by key (integers and bool
+ * as uint64 / int64, floats as double), strings (NUL-terminated, truncated to
+ * n), and an array's element type and length. */
+NXQ_API int nxq_gguf_meta_count(nxq_gguf_t g, int64_t* n);
+NXQ_API int nxq_gguf_meta_key(nxq_gguf_t g, int64_t i, char* key, size_t n, int* value_type);
+NXQ_API int nxq_gguf_meta_uint(nxq_gguf_t g, const char* key, uint64_t* v);
+NXQ_API int nxq_gguf_meta_int(nxq_gguf_t g, const char* key, int64_t* v);
+NXQ_API int nxq_gguf_meta_float(nxq_gguf_t g, const char* key, double* v);
+NXQ_API int nxq_gguf_meta_string(nxq_gguf_t g, const char* key, char* buf, size_t n);
+NXQ_API int nxq_gguf_meta_array(nxq_gguf_t g, const char* key, int* elem_type, uint64_t* count);
+
+/* Register tensor i as a weight [N][K]: K = dims[0], N = dims[1] (2-D, or higher
+ * dimensions of size 1).  For a 3-D tensor [E][N][K] (stacked experts) `slice`
+ * picks expert `slice`; pass 0 otherwise. */
+NXQ_API int nxq_gguf_register(nxq_gguf_t g, int64_t i, int64_t slice, nxq_weight_t* out);
+
+/* As nxq_gguf_register, this rank's tensor-parallel shard only
+ * (nxq_weight_register_shard rules). */
+NXQ_API int nxq_gguf_register_shard(nxq_gguf_t g, int64_t i, int64_t slice, int split, int rank,
+                                    int world, nxq_weight_t* out);
 
 #ifdef __cplusplus
 }

@@ -21,7 +21,7 @@ __all__ = [
     "NxqError", "lib", "init", "shutdown", "Weight", "qmatmul", "qmatmul_host", "stream_sync",
     "kernel_name", "launch_count",
     "TYPES", "GEOMETRY", "F32", "F16", "BF16", "SPLIT_COL", "SPLIT_ROW", "declared_symbols",
-    "tp_unique_id", "tp_init", "tp_shutdown", "tp_qmatmul", "tp_allreduce_f32",
+    "tp_unique_id", "tp_init", "tp_shutdown", "tp_qmatmul", "tp_allreduce_f32", "GGUF",
 ]
 
 LIB_PATH = Path(__file__).with_name("libnxq.so")
@@ -36,7 +36,8 @@ F32, F16, BF16 = 0, 1, 2
 SPLIT_COL, SPLIT_ROW = 0, 1
 
 STATUS = {0: "OK", -1: "ERR_ARG", -2: "ERR_CODEC", -3: "ERR_SHAPE", -4: "ERR_CUDA",
-          -5: "ERR_TIMEOUT", -6: "ERR_NOMEM", -7: "ERR_STATE", -8: "ERR_NCCL", -9: "ERR_UNSUPPORTED"}
+          -5: "ERR_TIMEOUT", -6: "ERR_NOMEM", -7: "ERR_STATE", -8: "ERR_NCCL", -9: "ERR_UNSUPPORTED",
+          -10: "ERR_FORMAT"}
 
 
 class NxqError(RuntimeError):
@@ -82,6 +83,25 @@ _SIGS = {
     "nxq_tp_qmatmul": [_c.c_void_p, _c.c_void_p, _c.c_int, _c.c_void_p, _c.c_int, _c.c_int64,
                        _c.c_int, _c.c_void_p],
     "nxq_tp_allreduce_f32": [_c.c_void_p, _c.c_int64, _c.c_void_p],
+    "nxq_gguf_open": [_c.c_char_p, _c.POINTER(_c.c_void_p)],
+    "nxq_gguf_close": [_c.c_void_p],
+    "nxq_gguf_header": [_c.c_void_p, _c.POINTER(_c.c_uint32), _c.POINTER(_c.c_uint64), _c.POINTER(_c.c_uint64)],
+    "nxq_gguf_tensor_count": [_c.c_void_p, _c.POINTER(_c.c_int64)],
+    "nxq_gguf_tensor_info": [_c.c_void_p, _c.c_int64, _c.c_char_p, _c.c_size_t, _c.POINTER(_c.c_int),
+                             _c.POINTER(_c.c_int), _c.POINTER(_c.c_int64), _c.POINTER(_c.c_uint64),
+                             _c.POINTER(_c.c_uint64)],
+    "nxq_gguf_find": [_c.c_void_p, _c.c_char_p, _c.POINTER(_c.c_int64)],
+    "nxq_gguf_tensor_data": [_c.c_void_p, _c.c_int64, _c.POINTER(_c.c_void_p), _c.POINTER(_c.c_uint64)],
+    "nxq_gguf_meta_count": [_c.c_void_p, _c.POINTER(_c.c_int64)],
+    "nxq_gguf_meta_key": [_c.c_void_p, _c.c_int64, _c.c_char_p, _c.c_size_t, _c.POINTER(_c.c_int)],
+    "nxq_gguf_meta_uint": [_c.c_void_p, _c.c_char_p, _c.POINTER(_c.c_uint64)],
+    "nxq_gguf_meta_int": [_c.c_void_p, _c.c_char_p, _c.POINTER(_c.c_int64)],
+    "nxq_gguf_meta_float": [_c.c_void_p, _c.c_char_p, _c.POINTER(_c.c_double)],
+    "nxq_gguf_meta_string": [_c.c_void_p, _c.c_char_p, _c.c_char_p, _c.c_size_t],
+    "nxq_gguf_meta_array": [_c.c_void_p, _c.c_char_p, _c.POINTER(_c.c_int), _c.POINTER(_c.c_uint64)],
+    "nxq_gguf_register": [_c.c_void_p, _c.c_int64, _c.c_int64, _c.POINTER(_c.c_void_p)],
+    "nxq_gguf_register_shard": [_c.c_void_p, _c.c_int64, _c.c_int64, _c.c_int, _c.c_int, _c.c_int,
+                                _c.POINTER(_c.c_void_p)],
 }
 
 
@@ -255,6 +275,121 @@ def launch_count() -> int:
     v = ctypes.c_uint64()
     _check(lib().nxq_launch_count(ctypes.byref(v)))
     return v.value
+
+
+# ---- residency loader: GGUF files --------------------------------------------
+
+class GGUF:
+    """A GGUF v2/v3 file opened by the library's loader (mapped read-only; the
+    index is parsed and bounds-checked on the host, no GPU needed).  Use as a
+    context manager or call close()."""
+
+    def __init__(self, path):
+        h = ctypes.c_void_p()
+        _check(lib().nxq_gguf_open(str(path).encode(), ctypes.byref(h)))
+        self._h = h
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        if self._h is None:
+            raise NxqError(-1, "GGUF file already closed")
+        return self._h
+
+    def close(self) -> None:
+        if self._h is not None:
+            _check(lib().nxq_gguf_close(self._h))
+            self._h = None
+
+    def __enter__(self) -> "GGUF":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
+    def header(self) -> dict:
+        v, a, d = ctypes.c_uint32(), ctypes.c_uint64(), ctypes.c_uint64()
+        _check(lib().nxq_gguf_header(self.handle, ctypes.byref(v), ctypes.byref(a), ctypes.byref(d)))
+        return {"version": v.value, "alignment": a.value, "data_start": d.value}
+
+    def tensors(self) -> list[dict]:
+        n = ctypes.c_int64()
+        _check(lib().nxq_gguf_tensor_count(self.handle, ctypes.byref(n)))
+        return [self.tensor_info(i) for i in range(n.value)]
+
+    def tensor_info(self, i: int) -> dict:
+        name = ctypes.create_string_buffer(512)
+        t, nd = ctypes.c_int(), ctypes.c_int()
+        dims = (ctypes.c_int64 * 4)()
+        off, nb = ctypes.c_uint64(), ctypes.c_uint64()
+        _check(lib().nxq_gguf_tensor_info(self.handle, i, name, 512, ctypes.byref(t), ctypes.byref(nd), dims,
+                                          ctypes.byref(off), ctypes.byref(nb)))
+        return {"name": name.value.decode(), "type": t.value, "dims": list(dims)[:nd.value],
+                "offset": off.value, "bytes": nb.value}
+
+    def find(self, name: str) -> int:
+        i = ctypes.c_int64()
+        _check(lib().nxq_gguf_find(self.handle, name.encode(), ctypes.byref(i)))
+        return i.value
+
+    def tensor_bytes(self, i: int) -> np.ndarray:
+        """The tensor's bytes in the mapping (a copy)."""
+        p, nb = ctypes.c_void_p(), ctypes.c_uint64()
+        _check(lib().nxq_gguf_tensor_data(self.handle, i, ctypes.byref(p), ctypes.byref(nb)))
+        return np.ctypeslib.as_array((ctypes.c_uint8 * nb.value).from_address(p.value)).copy()
+
+    def metadata(self) -> dict:
+        """key -> value type id (NXQ_GGUF_*)."""
+        n = ctypes.c_int64()
+        _check(lib().nxq_gguf_meta_count(self.handle, ctypes.byref(n)))
+        out = {}
+        for i in range(n.value):
+            key = ctypes.create_string_buffer(1024)
+            t = ctypes.c_int()
+            _check(lib().nxq_gguf_meta_key(self.handle, i, key, 1024, ctypes.byref(t)))
+            out[key.value.decode()] = t.value
+        return out
+
+    def meta_uint(self, key: str) -> int:
+        v = ctypes.c_uint64()
+        _check(lib().nxq_gguf_meta_uint(self.handle, key.encode(), ctypes.byref(v)))
+        return v.value
+
+    def meta_int(self, key: str) -> int:
+        v = ctypes.c_int64()
+        _check(lib().nxq_gguf_meta_int(self.handle, key.encode(), ctypes.byref(v)))
+        return v.value
+
+    def meta_float(self, key: str) -> float:
+        v = ctypes.c_double()
+        _check(lib().nxq_gguf_meta_float(self.handle, key.encode(), ctypes.byref(v)))
+        return v.value
+
+    def meta_string(self, key: str, n: int = 4096) -> str:
+        buf = ctypes.create_string_buffer(n)
+        _check(lib().nxq_gguf_meta_string(self.handle, key.encode(), buf, n))
+        return buf.value.decode()
+
+    def meta_array(self, key: str) -> tuple[int, int]:
+        t, n = ctypes.c_int(), ctypes.c_uint64()
+        _check(lib().nxq_gguf_meta_array(self.handle, key.encode(), ctypes.byref(t), ctypes.byref(n)))
+        return t.value, n.value
+
+    def register(self, name_or_index, slice_: int = 0) -> "Weight":
+        """Upload tensor [N][K] (expert `slice_` of a 3-D tensor) as a weight."""
+        i = self.find(name_or_index) if isinstance(name_or_index, str) else int(name_or_index)
+        info = self.tensor_info(i)
+        h = ctypes.c_void_p()
+        _check(lib().nxq_gguf_register(self.handle, i, slice_, ctypes.byref(h)))
+        return Weight(h.value, info["type"], info["dims"][1], info["dims"][0])
+
+    def register_shard(self, name_or_index, split: int, rank: int, world: int, slice_: int = 0) -> "Weight":
+        i = self.find(name_or_index) if isinstance(name_or_index, str) else int(name_or_index)
+        info = self.tensor_info(i)
+        h = ctypes.c_void_p()
+        _check(lib().nxq_gguf_register_shard(self.handle, i, slice_, split, rank, world, ctypes.byref(h)))
+        N, K = info["dims"][1], info["dims"][0]
+        return Weight(h.value, info["type"], N // world if split == SPLIT_COL else N,
+                      K // world if split == SPLIT_ROW else K)
 
 
 # ---- tensor parallelism ------------------------------------------------------
