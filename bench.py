@@ -397,11 +397,32 @@ def bench_config3(dev, stream, pk) -> dict:
 
     ms = graph_time_ms(issue_layer, stream) / L
     nb = layer_bytes + sum(K * 2 + N * 4 for _, K, N in projs)
+
+    # The same layer with the projections that share an input grouped:
+    # q/k/v and gate/up as one launch each (nxq_qmatmul_grouped), 4 launches.
+    yg = {name: torch.empty(1, N, dtype=torch.float32, device=dev) for name, _, N in projs}
+
+    def issue_grouped():
+        for r in range(L):
+            nxq.qmatmul_grouped([layer[n][r] for n in ("q", "k", "v")], [xs[4096]] * 3,
+                                outs=[yg[n] for n in ("q", "k", "v")], stream=stream)
+            nxq.qmatmul(layer["o"][r], xs[4096], out=yg["o"], stream=stream)
+            nxq.qmatmul_grouped([layer[n][r] for n in ("gate", "up")], [xs[4096]] * 2,
+                                outs=[yg[n] for n in ("gate", "up")], stream=stream)
+            nxq.qmatmul(layer["down"][r], xs[14336], out=yg["down"], stream=stream)
+
+    with torch.cuda.stream(stream):
+        issue_grouped()
+    stream.synchronize()
+    ms_g = graph_time_ms(issue_grouped, stream) / L
     out = {"workload": "BASELINE config 3: Q8_0 GEMV M=1, the 7 projections of a Llama-3-8B layer "
                        "(q/o 4096x4096, k/v 4096->1024, gate/up 4096->14336, down 14336->4096), f16 x, fp32 y",
            "kernel": nxq.kernel_name(layer["q"][0], 1), "per_projection": per,
            "layer_us": ms * 1e3, "layer_GB/s": nb / (ms / 1e3) / 1e9,
-           "layer_frac_of_hbm": nb / (ms / 1e3) / 1e9 / pk["hbm_gbs"], "layer_replicas": L}
+           "layer_frac_of_hbm": nb / (ms / 1e3) / 1e9 / pk["hbm_gbs"], "layer_replicas": L,
+           "layer_grouped": {"us": ms_g * 1e3, "GB/s": nb / (ms_g / 1e3) / 1e9,
+                             "frac_of_hbm": nb / (ms_g / 1e3) / 1e9 / pk["hbm_gbs"], "launches": 4,
+                             "how": "q/k/v and gate/up each one nxq_qmatmul_grouped launch"}}
     for ws in layer.values():
         for w in ws:
             w.release()

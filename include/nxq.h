@@ -170,6 +170,19 @@ NXQ_API int nxq_qmatmul(nxq_weight_t w, const void* x_dev, int x_dtype, void* y_
 NXQ_API int nxq_qmatmul_noalloc(nxq_weight_t w, const void* x_dev, int x_dtype, void* y_dev,
                                 int y_dtype, int64_t M, void* stream);
 
+/* Several projections in as few launches as possible: y_dev[i][M[i]][N_i] =
+ * x_dev[i][M[i]][K_i] * W_i^T for i < count, on `stream`.  The grouped/MoE
+ * GEMV: all active experts of a layer (batched_moe_ffn's single dispatch,
+ * compute_dispatch.cpp:211-275, batched_expert_gemv.metal:47-160), or the
+ * projections that share an input (q/k/v, gate/up) - the caller passes the same
+ * x_dev for those.  Weights of one block type with 1 <= M[i] <= 32 and f16
+ * activations (fp32/bf16 with M[i] <= 2) run as one decode launch per 16
+ * weights; anything else runs as nxq_qmatmul calls in order.  M[i] = 0 skips
+ * item i.  Results within the matmul tolerance of separate nxq_qmatmul calls. */
+NXQ_API int nxq_qmatmul_grouped(const nxq_weight_t* w, int count, const void* const* x_dev,
+                                int x_dtype, void* const* y_dev, int y_dtype, const int64_t* M,
+                                void* stream);
+
 /* Host-buffer form, synchronous: the drop-in for ComputeDispatch::gemm_int4
  * (compute_dispatch.h:59-61, .cpp:142-176) - fp32 activations [M][K] in, fp32
  * output [M][N] out, weights resident.  The reference ignores M

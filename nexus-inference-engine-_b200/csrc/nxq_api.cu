@@ -12,6 +12,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <vector>
 #include <unordered_set>
 
 #include "nxq_internal.h"
@@ -476,6 +477,27 @@ NXQ_API int nxq_qmatmul(nxq_weight_t h, const void* x_dev, int x_dtype, void* y_
     if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return fail(NXQ_ERR_ARG, "bad dtype");
     if ((rc = check_ready())) return rc;
     return qmatmul_dispatch(w, x_dev, x_dtype, y_dev, y_dtype, M, (cudaStream_t)stream);
+}
+
+NXQ_API int nxq_qmatmul_grouped(const nxq_weight_t* hs, int count, const void* const* x_dev, int x_dtype,
+                                void* const* y_dev, int y_dtype, const int64_t* M, void* stream) {
+    if (count < 0 || (count > 0 && (!hs || !x_dev || !y_dev || !M))) return fail(NXQ_ERR_ARG, "grouped: bad arrays");
+    if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return fail(NXQ_ERR_ARG, "bad dtype");
+    std::vector<Weight*> ws((size_t)count);
+    for (int i = 0; i < count; ++i) {
+        if (int rc = check_weight(hs[i], &ws[i])) return rc;
+        if (M[i] < 0) return fail(NXQ_ERR_ARG, "grouped: M[%d]=%lld", i, (long long)M[i]);
+        if (M[i] > 0 && (!x_dev[i] || !y_dev[i])) return fail(NXQ_ERR_ARG, "grouped: null activation or output %d", i);
+    }
+    if (int rc = check_ready()) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    int rc = mma_qmatmul_grouped(ws.data(), count, x_dev, x_dtype, y_dev, y_dtype, M, st);
+    if (rc != NXQ_ERR_UNSUPPORTED) return rc;
+    // Mixed block types, prefill batch sizes or activations that need a
+    // conversion pass: the items one after another on the same stream.
+    for (int i = 0; i < count; ++i)
+        if ((rc = qmatmul_dispatch(ws[i], x_dev[i], x_dtype, y_dev[i], y_dtype, M[i], st))) return rc;
+    return NXQ_OK;
 }
 
 NXQ_API int nxq_qmatmul_noalloc(nxq_weight_t h, const void* x_dev, int x_dtype, void* y_dev, int y_dtype,

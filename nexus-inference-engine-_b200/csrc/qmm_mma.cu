@@ -253,6 +253,7 @@ __device__ __forceinline__ void named_sync(int id, int threads) {
 }
 
 constexpr int kMaxCluster = 8;
+constexpr int kMaxItems = 16;
 
 // Shared-memory budget of a variant with `groups` consumer warpgroups.
 template <int TYPE, int MT, int GROUPS, int CMAX>
@@ -294,17 +295,25 @@ struct Cfg {
     static_assert(S >= 3, "pipeline too shallow");
 };
 
+// One weight of a launch: the single call is a launch of one item; a grouped
+// call (nxq_qmatmul_grouped: MoE experts, the projections that share an
+// input) puts up to kMaxItems weights of one block type in one launch.
+struct MmaItem {
+    const uint8_t* w;  // tiled weight
+    const void* x;     // [M][K]: f16, or (M <= 2) fp32 / bf16 rounded to f16 by the producer
+    void* y;           // [M][N]
+    int64_t N, K;
+    int chunks;        // K chunks per row
+    int M;
+    int cluster0;      // first cluster of this item
+    int tile_base, tile_rem;  // its cluster q owns tile_base + (q < tile_rem) tiles, in order
+};
+
 struct MmaParams {
-    const uint8_t* w;
-    TiledShape s;
-    const void* x;  // f16, or (M <= 2) fp32 / bf16 rounded to f16 by the producer
-    int x_dtype;
-    int64_t M;
-    void* y;
-    int y_dtype;
-    int C;         // CTAs per cluster: the reduction is split C ways inside a cluster
-    int clusters;  // Q
-    int tile_base, tile_rem;  // cluster q owns tile_base + (q < tile_rem) tiles, in order
+    MmaItem it[kMaxItems];
+    int n_items;
+    int x_dtype, y_dtype;
+    int C;  // CTAs per cluster: the reduction is split C ways inside a cluster
     DeviceStatus* status;
 };
 
@@ -338,7 +347,12 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
 // copy each, completing on an mbarrier there), which adds them in rank order:
 // no global-memory round trip and a result that does not depend on timing.
 // A CTA's units are consecutive tile-chunks in memory in either case.
-template <int TYPE, int MT>
+// LOOKUP = true: the CTA looks its item up from its cluster index, and the
+// item's fields live in registers; false: a launch of one item, read at fixed
+// offsets of the kernel parameters.  Grouped launches need the lookup; single
+// ones use it too up to 16 tokens (measured 1-3 % faster there), but not at
+// 32 tokens, where it is 4 % slower (registers at the 96 cap).
+template <int TYPE, int MT, bool LOOKUP>
 __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const MmaParams p) {
     using Cf = Cfg<TYPE, MT>;
     constexpr int S = Cf::S, WB = Cf::WB, XB = Cf::XB, NT = Cf::NT, PB = Cf::PB;
@@ -356,19 +370,25 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, tq = lane & 3;
-    const int C = p.C, rank = (int)(blockIdx.x % (unsigned)C), q = (int)(blockIdx.x / (unsigned)C);
-    const int Kc = (int)p.s.chunks;
+    const int C = p.C, rank = (int)(blockIdx.x % (unsigned)C), qg = (int)(blockIdx.x / (unsigned)C);
+    int ii = 0;
+    if (LOOKUP)
+        for (int j = 1; j < p.n_items; ++j)
+            if (qg >= p.it[j].cluster0) ii = j;
+    const MmaItem& I = p.it[LOOKUP ? ii : 0];
+    const int q = qg - I.cluster0;
+    const int Kc = I.chunks;
     const int kc0 = rank * Kc / C, kr = (rank + 1) * Kc / C - kc0;
-    const int t0 = q * p.tile_base + (q < p.tile_rem ? q : p.tile_rem);
-    const int ntiles = p.tile_base + (q < p.tile_rem ? 1 : 0);
+    const int t0 = q * I.tile_base + (q < I.tile_rem ? q : I.tile_rem);
+    const int ntiles = I.tile_base + (q < I.tile_rem ? 1 : 0);
     const int n = ntiles * kr;
-    const int64_t K = p.s.K, N = p.s.N;
-    const int M = (int)p.M;
+    const int64_t K = I.K, N = I.N;
+    const int M = I.M;
 
     // Unit u's tile-chunk: tiles t0 .. t0 + ntiles - 1 hold chunks kc0 ..
     // kc0 + kr - 1 each, and either ntiles = 1 or kr = all chunks, so the
     // units are consecutive tile-chunks from w_base on.
-    const uint8_t* const w_base = p.w + p.s.chunk_offset(t0, kc0);
+    const uint8_t* const w_base = I.w + ((int64_t)t0 * Kc + kc0) * WB;
     auto w_issue = [&](int u, int stg) {
         ptx::mbar_arrive_expect_tx(&full[stg], WB);
         ptx::bulk_g2s(wst + stg * WB, w_base + (int64_t)u * WB, WB, &full[stg]);
@@ -440,7 +460,7 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
         if (p.x_dtype == NXQ_F16) {
             // Lane (t4, m) = ((lane >> 3) & 3, lane & 7) copies piece (token, t4,
             // m) of every token: one source row and one destination step apart.
-            const __half* xh = static_cast<const __half*>(p.x);
+            const __half* xh = static_cast<const __half*>(I.x);
             const int t4 = (lane >> 3) & 3, m = lane & 7;
             const int tok0 = 8 * pw, tok1 = M < tok0 + 8 ? M : tok0 + 8;
             for (int u = 0, c = 0; u < n; ++u, c = c + 1 == kr ? 0 : c + 1) {
@@ -470,13 +490,13 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
                     ra[j] = rb[j] = make_float4(0.f, 0.f, 0.f, 0.f);
                     if (i < M * 32 && k < K) {
                         if (f32) {
-                            const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.x) +
+                            const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(I.x) +
                                                                                 (int64_t)tok * K + k);
                             ra[j] = __ldg(src);
                             rb[j] = __ldg(src + 1);
                         } else {
                             const uint4 q = __ldg(reinterpret_cast<const uint4*>(
-                                static_cast<const __nv_bfloat16*>(p.x) + (int64_t)tok * K + k));
+                                static_cast<const __nv_bfloat16*>(I.x) + (int64_t)tok * K + k));
                             ra[j] = make_float4(__uint_as_float(q.x), __uint_as_float(q.y), __uint_as_float(q.z),
                                                 __uint_as_float(q.w));
                         }
@@ -602,7 +622,7 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
                     for (int e = 0; e < 4; ++e) {
                         const int tok = 8 * nt + 2 * tq + (e & 1);
                         const int64_t row = tile * TILE_ROWS + r0 + 8 * (e >> 1);
-                        if (tok < M && row < N) store_y(p.y, p.y_dtype, tok * N + row, acc[nt][e]);
+                        if (tok < M && row < N) store_y(I.y, p.y_dtype, tok * N + row, acc[nt][e]);
                     }
             } else if (rank > 0) {
                 // Push this rank's partial to the leader: stage memory is free
@@ -654,7 +674,7 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
                         for (int e = 0; e < 4; ++e) {
                             const int tok = 8 * nt + 2 * tq + (e & 1);
                             const int64_t row = tile * TILE_ROWS + r0 + 8 * (e >> 1);
-                            if (tok < M && row < N) store_y(p.y, p.y_dtype, tok * N + row, acc[nt][e]);
+                            if (tok < M && row < N) store_y(I.y, p.y_dtype, tok * N + row, acc[nt][e]);
                         }
                 }
             }
@@ -690,8 +710,11 @@ int* max_clusters() {
 template <int TYPE, int MT>
 int set_attr() {
     using Cf = Cfg<TYPE, MT>;
-    cudaError_t e = cudaFuncSetAttribute(mma_gemv_kernel<TYPE, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)Cf::smem);
+    cudaError_t e = cudaFuncSetAttribute(mma_gemv_kernel<TYPE, MT, false>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cf::smem);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(mma_gemv_kernel<TYPE, MT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)Cf::smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute (mma_gemv)");
     int* mq = max_clusters<TYPE, MT>();
     mq[0] = g_sm_count;
@@ -708,57 +731,97 @@ int set_attr() {
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
         int nq = 0;
-        e = cudaOccupancyMaxActiveClusters(&nq, mma_gemv_kernel<TYPE, MT>, &cfg);
+        e = cudaOccupancyMaxActiveClusters(&nq, mma_gemv_kernel<TYPE, MT, false>, &cfg);
         if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters (mma_gemv)");
         mq[lc] = nq;
     }
     return NXQ_OK;
 }
 
-// Work split: C CTAs per cluster (K cut C ways) and Q clusters, at most as
-// many as fit on the GPU at once (one wave).  C = 1: every CTA owns
-// ceil or floor of T / P whole tiles; C > 1 (only when the weight has few
-// enough tiles): one tile per cluster.  Picks the split with the fewest units
-// per CTA, the smallest C among equals.
-void pick_split(const TiledShape& s, const int* maxq, int cmax, MmaParams* p) {
-    const int64_t T = s.tiles, Kc = s.chunks;
+// One weight of a launch as the host sees it.
+struct HostItem {
+    const Weight* w;
+    const void* x;
+    void* y;
+    int64_t M;
+};
+
+// Work split of a launch: C CTAs per cluster (K cut C ways, the same C for
+// every item) and Q_i clusters for item i, at most as many clusters in all as
+// fit on the GPU at once (one wave).  C = 1: every CTA owns ceil or floor of
+// T_i / Q_i whole tiles of one item, and the SMs go one at a time to the item
+// whose CTAs have the most units (so a lone weight gets min(T, SMs) CTAs).
+// C > 1 (only when all items together have few enough tiles): one tile per
+// cluster.  Picks the split with the fewest units on the busiest CTA, the
+// smallest C among equals.  Returns the number of clusters.
+int pick_split(const HostItem* it, int n, const int* maxq, int cmax, MmaParams* p) {
+    int64_t T[kMaxItems], Kc[kMaxItems], q[kMaxItems], sumT = 0, minKc = INT64_MAX;
+    for (int i = 0; i < n; ++i) {
+        T[i] = it[i].w->shape.tiles;
+        Kc[i] = it[i].w->shape.chunks;
+        q[i] = 1;
+        sumT += T[i];
+        if (Kc[i] < minKc) minKc = Kc[i];
+    }
+    auto cost1 = [&](int i) { return ((T[i] + q[i] - 1) / q[i]) * Kc[i]; };
+    for (int64_t used = n; used < g_sm_count; ++used) {
+        int bi = -1;
+        for (int i = 0; i < n; ++i)
+            if (q[i] < T[i] && (bi < 0 || cost1(i) > cost1(bi))) bi = i;
+        if (bi < 0) break;
+        ++q[bi];
+    }
+    int64_t best = 0;
+    for (int i = 0; i < n; ++i) best = cost1(i) > best ? cost1(i) : best;
     int best_c = 1;
-    int64_t best_q = T < g_sm_count ? T : g_sm_count;
-    int64_t best = ((T + best_q - 1) / best_q) * Kc;
-    for (int lc = 1, c = 2; c <= cmax && c <= Kc; ++lc, c *= 2) {
+    for (int lc = 1, c = 2; c <= cmax && c <= minKc; ++lc, c *= 2) {
         const int64_t qmax = g_sm_count / c < maxq[lc] ? g_sm_count / c : maxq[lc];
-        if (T > qmax) continue;
-        const int64_t cost = (Kc + c - 1) / c;
+        if (sumT > qmax) continue;
+        int64_t cost = 0;
+        for (int i = 0; i < n; ++i) cost = (Kc[i] + c - 1) / c > cost ? (Kc[i] + c - 1) / c : cost;
         if (cost < best) {
             best = cost;
             best_c = c;
-            best_q = T;
         }
     }
     p->C = best_c;
-    p->clusters = (int)best_q;
-    p->tile_base = (int)(T / best_q);
-    p->tile_rem = (int)(T % best_q);
+    p->n_items = n;
+    int cl = 0;
+    for (int i = 0; i < n; ++i) {
+        const int64_t qi = best_c == 1 ? q[i] : T[i];
+        MmaItem& m = p->it[i];
+        m.w = it[i].w->dev;
+        m.x = it[i].x;
+        m.y = it[i].y;
+        m.N = it[i].w->shape.N;
+        m.K = it[i].w->shape.K;
+        m.chunks = (int)Kc[i];
+        m.M = (int)it[i].M;
+        m.cluster0 = cl;
+        m.tile_base = (int)(T[i] / qi);
+        m.tile_rem = (int)(T[i] % qi);
+        cl += (int)qi;
+    }
+    for (int i = n; i < kMaxItems; ++i) p->it[i] = MmaItem{};
+    return cl;
 }
 
 template <int TYPE, int MT>
-int launch(const Weight* w, const void* x, int x_dtype, void* y, int y_dtype, int64_t M, cudaStream_t st) {
+int launch(const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st) {
     using Cf = Cfg<TYPE, MT>;
     MmaParams p;
-    p.w = w->dev;
-    p.s = w->shape;
-    p.x = x;
+    for (int i = 0; i < n; ++i)
+        if (it[i].w->shape.tile_chunk_bytes != Cf::WB)
+            return fail(NXQ_ERR_SHAPE, "mma_gemv: tile-chunk of %lld bytes, kernel stage %d",
+                        (long long)it[i].w->shape.tile_chunk_bytes, Cf::WB);
+    const int clusters = pick_split(it, n, max_clusters<TYPE, MT>(), Cf::CMAX, &p);
     p.x_dtype = x_dtype;
-    p.M = M;
-    p.y = y;
     p.y_dtype = y_dtype;
-    if (w->shape.tile_chunk_bytes != Cf::WB) return fail(NXQ_ERR_SHAPE, "mma_gemv: tile-chunk of %lld bytes, kernel stage %d", (long long)w->shape.tile_chunk_bytes, Cf::WB);
-    pick_split(w->shape, max_clusters<TYPE, MT>(), Cf::CMAX, &p);
     p.status = context_status();
     // Launched with programmatic stream serialization (see the kernel's
     // griddepcontrol.wait): it may start while the previous kernel drains.
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(p.clusters * p.C));
+    cfg.gridDim = dim3((unsigned)(clusters * p.C));
     cfg.blockDim = dim3(Cf::kAll);
     cfg.dynamicSmemBytes = Cf::smem;
     cfg.stream = st;
@@ -771,13 +834,31 @@ int launch(const Weight* w, const void* x, int x_dtype, void* y, int y_dtype, in
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = p.C > 1 ? 2 : 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, mma_gemv_kernel<TYPE, MT>, p);
+    cudaError_t e = (n == 1 && MT == 32) ? cudaLaunchKernelEx(&cfg, mma_gemv_kernel<TYPE, MT, false>, p)
+                                         : cudaLaunchKernelEx(&cfg, mma_gemv_kernel<TYPE, MT, true>, p);
     note_launches(1);
     if (e != cudaSuccess) return cuda_fail(e, "mma_gemv launch");
     return NXQ_OK;
 }
 
 bool type_ok(int type) { return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || type == T_Q3_K; }
+
+int launch_items(int type, int mt, const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st) {
+#define NXQ_CASE(T)                                                               \
+    case T:                                                                       \
+        return mt == 8    ? launch<T, 8>(it, n, x_dtype, y_dtype, st)             \
+               : mt == 16 ? launch<T, 16>(it, n, x_dtype, y_dtype, st)            \
+                          : launch<T, 32>(it, n, x_dtype, y_dtype, st);
+    switch (type) {
+        NXQ_CASE(T_Q4_K)
+        NXQ_CASE(T_Q4_0)
+        NXQ_CASE(T_Q8_0)
+        NXQ_CASE(T_Q3_K)
+        default:
+            return NXQ_ERR_UNSUPPORTED;
+    }
+#undef NXQ_CASE
+}
 
 }  // namespace
 
@@ -825,20 +906,37 @@ int mma_qmatmul(const Weight* w, const void* x, int x_dtype, void* y, int y_dtyp
         xh = sc->xh;
         xdt = NXQ_F16;
     }
-#define NXQ_CASE(T)                                                \
-    case T:                                                        \
-        return mt == 8    ? launch<T, 8>(w, xh, xdt, y, y_dtype, M, st)  \
-               : mt == 16 ? launch<T, 16>(w, xh, xdt, y, y_dtype, M, st) \
-                          : launch<T, 32>(w, xh, xdt, y, y_dtype, M, st);
-    switch (s.type) {
-        NXQ_CASE(T_Q4_K)
-        NXQ_CASE(T_Q4_0)
-        NXQ_CASE(T_Q8_0)
-        NXQ_CASE(T_Q3_K)
-        default:
-            return NXQ_ERR_UNSUPPORTED;
+    const HostItem item{w, xh, y, M};
+    return launch_items(s.type, mt, &item, 1, xdt, y_dtype, st);
+}
+
+int mma_qmatmul_grouped(const Weight* const* w, int n, const void* const* x, int x_dtype, void* const* y,
+                        int y_dtype, const int64_t* M, cudaStream_t st) {
+    HostItem items[kMaxItems];
+    int type = -1, k = 0;
+    int64_t mmax = 0;
+    // Every item must be one the kernel reads as it is (no conversion pass).
+    for (int i = 0; i < n; ++i) {
+        if (M[i] == 0) continue;
+        const TiledShape& s = w[i]->shape;
+        const bool aligned = ((uintptr_t)x[i] % 16) == 0;
+        const bool direct =
+            aligned && (x_dtype == NXQ_F16 || (M[i] <= 2 && (x_dtype == NXQ_F32 || x_dtype == NXQ_BF16)));
+        if (!mma_supported(s, M[i]) || !direct || (type >= 0 && s.type != type)) return NXQ_ERR_UNSUPPORTED;
+        type = s.type;
+        mmax = M[i] > mmax ? M[i] : mmax;
     }
-#undef NXQ_CASE
+    if (type < 0) return NXQ_OK;  // nothing to do
+    const int mt = mmax <= 8 ? 8 : mmax <= 16 ? 16 : 32;
+    for (int i = 0; i < n; ++i) {
+        if (M[i] == 0) continue;
+        items[k++] = HostItem{w[i], x[i], y[i], M[i]};
+        if (k == kMaxItems) {
+            if (int rc = launch_items(type, mt, items, k, x_dtype, y_dtype, st)) return rc;
+            k = 0;
+        }
+    }
+    return k ? launch_items(type, mt, items, k, x_dtype, y_dtype, st) : NXQ_OK;
 }
 
 }  // namespace nxq

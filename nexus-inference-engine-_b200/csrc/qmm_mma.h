@@ -14,5 +14,11 @@ bool mma_supported(const TiledShape& s, int64_t M);
 void mma_kernel_name(const TiledShape& s, int64_t M, char* buf, size_t n);
 // y = x W^T; NXQ_ERR_UNSUPPORTED to decline.
 int mma_qmatmul(const Weight* w, const void* x, int x_dtype, void* y, int y_dtype, int64_t M, cudaStream_t st);
+// y_i = x_i W_i^T for n weights of one block type in as few launches as
+// possible (16 weights each); items with M_i = 0 are skipped.
+// NXQ_ERR_UNSUPPORTED (nothing launched) unless every item has 1 <= M_i <= 32
+// and activations the kernel reads as they are.
+int mma_qmatmul_grouped(const Weight* const* w, int n, const void* const* x, int x_dtype, void* const* y,
+                        int y_dtype, const int64_t* M, cudaStream_t st);
 
 }  // namespace nxq

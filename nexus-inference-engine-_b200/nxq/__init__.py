@@ -21,7 +21,7 @@ __all__ = [
     "NxqError", "lib", "init", "shutdown", "Weight", "qmatmul", "qmatmul_host", "stream_sync",
     "kernel_name", "launch_count",
     "TYPES", "GEOMETRY", "F32", "F16", "BF16", "SPLIT_COL", "SPLIT_ROW", "declared_symbols",
-    "tp_unique_id", "tp_init", "tp_shutdown", "tp_qmatmul", "tp_allreduce_f32", "GGUF",
+    "tp_unique_id", "tp_init", "tp_shutdown", "tp_qmatmul", "tp_allreduce_f32", "GGUF", "qmatmul_grouped",
 ]
 
 LIB_PATH = Path(__file__).with_name("libnxq.so")
@@ -71,6 +71,8 @@ _SIGS = {
     "nxq_qmatmul": [_c.c_void_p, _c.c_void_p, _c.c_int, _c.c_void_p, _c.c_int, _c.c_int64,
                     _c.c_void_p],
     "nxq_qmatmul_host": [_c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int64],
+    "nxq_qmatmul_grouped": [_c.POINTER(_c.c_void_p), _c.c_int, _c.POINTER(_c.c_void_p), _c.c_int,
+                            _c.POINTER(_c.c_void_p), _c.c_int, _c.POINTER(_c.c_int64), _c.c_void_p],
     "nxq_qmatmul_noalloc": [_c.c_void_p, _c.c_void_p, _c.c_int, _c.c_void_p, _c.c_int, _c.c_int64,
                             _c.c_void_p],
     "nxq_stream_sync": [_c.c_void_p],
@@ -248,6 +250,32 @@ def qmatmul(w: Weight, x, out=None, out_dtype=None, stream=None):
     _check(lib().nxq_qmatmul(w.handle, x.data_ptr(), _dtype_code(x.dtype), out.data_ptr(),
                              _dtype_code(out.dtype), M, _stream_ptr(stream)))
     return out
+
+
+def qmatmul_grouped(ws, xs, outs=None, out_dtype=None, stream=None):
+    """y_i = x_i W_i^T for every (W_i, x_i) in one decode launch per 16 weights
+    when they allow it (one block type, M_i <= 32); `xs` may repeat one tensor.
+    All activations share one dtype, all outputs another."""
+    import torch
+
+    ws, xs = list(ws), list(xs)
+    assert len(ws) == len(xs)
+    if outs is None:
+        outs = [torch.empty((x.numel() // w.K, w.N), dtype=out_dtype or torch.float32, device=x.device)
+                for w, x in zip(ws, xs)]
+    n = len(ws)
+    Ms = []
+    for w, x, y in zip(ws, xs, outs):
+        assert x.is_cuda and x.is_contiguous() and x.shape[-1] == w.K and x.dtype == xs[0].dtype
+        assert y.dtype == outs[0].dtype and y.numel() == (x.numel() // w.K) * w.N
+        Ms.append(x.numel() // w.K)
+    arr = ctypes.c_void_p * max(n, 1)
+    _check(lib().nxq_qmatmul_grouped(arr(*[w.handle.value for w in ws]), n, arr(*[x.data_ptr() for x in xs]),
+                                     _dtype_code(xs[0].dtype) if n else F16,
+                                     arr(*[y.data_ptr() for y in outs]),
+                                     _dtype_code(outs[0].dtype) if n else F32,
+                                     (ctypes.c_int64 * max(n, 1))(*Ms), _stream_ptr(stream)))
+    return outs
 
 
 def qmatmul_host(w: Weight, x: np.ndarray, out: Optional[np.ndarray] = None) -> np.ndarray:
