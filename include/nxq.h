@@ -183,6 +183,22 @@ NXQ_API int nxq_qmatmul_grouped(const nxq_weight_t* w, int count, const void* co
                                 int x_dtype, void* const* y_dev, int y_dtype, const int64_t* M,
                                 void* stream);
 
+/* Fused epilogues (the reference's fused_ffn_int4.metal:120-123 and
+ * activations.metal:51, after its gate/up and projection GEMVs):
+ *   nxq_qmatmul_swiglu:   h_dev[M][N] = silu(x Wg^T) * (x Wu^T), silu(g) = g / (1 + exp(-g)),
+ *                         for gate and up weights of the same shape and type;
+ *                         one decode launch (each CTA takes a tile of both
+ *                         weights) for M <= 32 when the weight has tiles for
+ *                         half the SMs, else gate and up, then one small kernel.
+ *   nxq_qmatmul_residual: y_dev[M][N] = x W^T + res_dev[M][N] (fp32 residual;
+ *                         y_dev may be res_dev), added before the decode
+ *                         kernel's store, else by a small kernel after it.
+ * Results within the matmul tolerance of the unfused computation. */
+NXQ_API int nxq_qmatmul_swiglu(nxq_weight_t w_gate, nxq_weight_t w_up, const void* x_dev, int x_dtype,
+                               void* h_dev, int h_dtype, int64_t M, void* stream);
+NXQ_API int nxq_qmatmul_residual(nxq_weight_t w, const void* x_dev, int x_dtype, const float* res_dev,
+                                 void* y_dev, int y_dtype, int64_t M, void* stream);
+
 /* Host-buffer form, synchronous: the drop-in for ComputeDispatch::gemm_int4
  * (compute_dispatch.h:59-61, .cpp:142-176) - fp32 activations [M][K] in, fp32
  * output [M][N] out, weights resident.  The reference ignores M

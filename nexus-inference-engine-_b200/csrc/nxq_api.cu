@@ -18,6 +18,7 @@
 #include "nxq_internal.h"
 #include "qmm_gemm.h"
 #include "qmm_mma.h"
+#include "stream_scratch.h"
 #include "qmm_tc.h"
 
 namespace nxq {
@@ -498,6 +499,66 @@ NXQ_API int nxq_qmatmul_grouped(const nxq_weight_t* hs, int count, const void* c
     for (int i = 0; i < count; ++i)
         if ((rc = qmatmul_dispatch(ws[i], x_dev[i], x_dtype, y_dev[i], y_dtype, M[i], st))) return rc;
     return NXQ_OK;
+}
+
+NXQ_API int nxq_qmatmul_swiglu(nxq_weight_t hg, nxq_weight_t hu, const void* x_dev, int x_dtype, void* h_dev,
+                               int h_dtype, int64_t M, void* stream) {
+    Weight *wg = nullptr, *wu = nullptr;
+    int rc = check_weight(hg, &wg);
+    if (rc || (rc = check_weight(hu, &wu))) return rc;
+    if (wg->shape.N != wu->shape.N || wg->shape.K != wu->shape.K)
+        return fail(NXQ_ERR_SHAPE, "swiglu: gate [%lld][%lld] and up [%lld][%lld] differ", (long long)wg->shape.N,
+                    (long long)wg->shape.K, (long long)wu->shape.N, (long long)wu->shape.K);
+    if (M < 0) return fail(NXQ_ERR_ARG, "M=%lld", (long long)M);
+    if (M == 0) return NXQ_OK;
+    if (!x_dev || !h_dev) return fail(NXQ_ERR_ARG, "null activation or output");
+    if (!dtype_ok(x_dtype) || !dtype_ok(h_dtype)) return fail(NXQ_ERR_ARG, "bad dtype");
+    if ((rc = check_ready())) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    rc = mma_qmatmul_swiglu(wg, wu, x_dev, x_dtype, h_dev, h_dtype, M, st);
+    if (rc != NXQ_ERR_UNSUPPORTED) return rc;
+    // Gate and up into fp32 intermediates (one grouped launch where it can
+    // be), then h = silu(g) * u.
+    const int64_t mn = M * wg->shape.N;
+    StreamScratch* sc = nullptr;
+    if ((rc = scratch_for(st, 0, 0, 0, &sc, (size_t)(2 * mn)))) return rc;
+    float* gu[2] = {sc->epi, sc->epi + mn};
+    const Weight* ws[2] = {wg, wu};
+    const void* xs[2] = {x_dev, x_dev};
+    const int64_t Ms[2] = {M, M};
+    rc = mma_qmatmul_grouped(ws, 2, xs, x_dtype, reinterpret_cast<void* const*>(gu), NXQ_F32, Ms, st);
+    if (rc == NXQ_ERR_UNSUPPORTED) {
+        if ((rc = qmatmul_dispatch(wg, x_dev, x_dtype, gu[0], NXQ_F32, M, st))) return rc;
+        rc = qmatmul_dispatch(wu, x_dev, x_dtype, gu[1], NXQ_F32, M, st);
+    }
+    if (rc) return rc;
+    cudaError_t e = launch_swiglu(gu[0], gu[1], h_dev, h_dtype, mn, st);
+    return e == cudaSuccess ? NXQ_OK : cuda_fail(e, "swiglu launch");
+}
+
+NXQ_API int nxq_qmatmul_residual(nxq_weight_t h, const void* x_dev, int x_dtype, const float* res_dev, void* y_dev,
+                                 int y_dtype, int64_t M, void* stream) {
+    Weight* w = nullptr;
+    int rc = check_weight(h, &w);
+    if (rc) return rc;
+    if (M < 0) return fail(NXQ_ERR_ARG, "M=%lld", (long long)M);
+    if (M == 0) return NXQ_OK;
+    if (!x_dev || !y_dev || !res_dev) return fail(NXQ_ERR_ARG, "null activation, residual or output");
+    if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return fail(NXQ_ERR_ARG, "bad dtype");
+    if ((rc = check_ready())) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (mma_supported(w->shape, M)) {
+        rc = mma_qmatmul(w, x_dev, x_dtype, y_dev, y_dtype, M, st, res_dev);
+        if (rc != NXQ_ERR_UNSUPPORTED) return rc;
+    }
+    // Other kernels: the product into an fp32 intermediate, then y = it + res
+    // (y may be the residual buffer itself).
+    const int64_t mn = M * w->shape.N;
+    StreamScratch* sc = nullptr;
+    if ((rc = scratch_for(st, 0, 0, 0, &sc, (size_t)mn))) return rc;
+    if ((rc = qmatmul_dispatch(w, x_dev, x_dtype, sc->epi, NXQ_F32, M, st))) return rc;
+    cudaError_t e = launch_add_residual(sc->epi, res_dev, y_dev, y_dtype, mn, st);
+    return e == cudaSuccess ? NXQ_OK : cuda_fail(e, "residual add launch");
 }
 
 NXQ_API int nxq_qmatmul_noalloc(nxq_weight_t h, const void* x_dev, int x_dtype, void* y_dev, int y_dtype,

@@ -256,30 +256,33 @@ constexpr int kMaxCluster = 8;
 constexpr int kMaxItems = 16;
 
 // Shared-memory budget of a variant with `groups` consumer warpgroups.
-template <int TYPE, int MT, int GROUPS, int CMAX>
+template <int TYPE, int MT, int GROUPS, int CMAX, int SETS>
 struct Budget {
     static constexpr int NT = MT / 8;
     static constexpr int WB = Lane<TYPE>::kStage;
     static constexpr int XB = NT * 8 * 32 * 16;
     static constexpr int PB = NT * 8 * TILE_ROWS * 4;
     static constexpr int RECV = (CMAX - 1) * PB;
-    static constexpr int COMB = 2 * (GROUPS - 1) * PB;
+    static constexpr int COMB = 2 * SETS * (GROUPS - 1) * PB;
     static constexpr int S0 = (227 * 1024 - 2048 - RECV - COMB) / (WB + XB);
 };
 
-template <int TYPE, int MT>
+// PAIR: the SwiGLU pairing (each tile twice, gate then up weights, with two
+// result sets handed over; no cluster split).
+template <int TYPE, int MT, bool PAIR = false>
 struct Cfg {
     static constexpr int NT = MT / 8;                   // n8 token tiles
     static constexpr int WB = Lane<TYPE>::kStage;
     static constexpr int XB = NT * 8 * 32 * 16;         // pieces (n8 tile, m, lane) of 16 B
     static constexpr int PB = NT * 8 * TILE_ROWS * 4;   // one tile's fp32 partial, [row][token]
-    static constexpr int CMAX = NT >= 4 ? (WB > 20000 ? 2 : 4) : kMaxCluster;
+    static constexpr int CMAX = PAIR ? 1 : NT >= 4 ? (WB > 20000 ? 2 : 4) : kMaxCluster;
+    static constexpr int SETS = PAIR ? 2 : 1;           // result sets per tile
     // Two consumer warpgroups (measured: a third one, with its tighter
     // register budget, is slower).
     static constexpr int G = 2;
     static constexpr int RECV = (CMAX - 1) * PB;        // cluster leader: the other ranks' partials
-    static constexpr int COMB = 2 * (G - 1) * PB;       // groups 1.. -> group 0 hand-over, two tiles deep
-    static constexpr int S0 = Budget<TYPE, MT, G, CMAX>::S0;
+    static constexpr int COMB = 2 * SETS * (G - 1) * PB;  // groups 1.. -> group 0 hand-over, two tiles deep
+    static constexpr int S0 = Budget<TYPE, MT, G, CMAX, SETS>::S0;
     static constexpr int S = S0 > 8 ? 8 : S0;
     static constexpr int kConsumers = G * kThreads;
     // Producer warps; warp w stages tokens 8w..8w+7 (one is enough up to 8
@@ -307,6 +310,8 @@ struct MmaItem {
     int M;
     int cluster0;      // first cluster of this item
     int tile_base, tile_rem;  // its cluster q owns tile_base + (q < tile_rem) tiles, in order
+    const uint8_t* w_up;  // SwiGLU pairing: the up weight (same shape); y = silu(x W^T) * (x W_up^T)
+    const float* res;     // residual [M][N] fp32 added to the result before the store, or null
 };
 
 struct MmaParams {
@@ -352,9 +357,9 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
 // offsets of the kernel parameters.  Grouped launches need the lookup; single
 // ones use it too up to 16 tokens (measured 1-3 % faster there), but not at
 // 32 tokens, where it is 4 % slower (registers at the 96 cap).
-template <int TYPE, int MT, bool LOOKUP>
-__global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const MmaParams p) {
-    using Cf = Cfg<TYPE, MT>;
+template <int TYPE, int MT, bool LOOKUP, bool PAIR = false>
+__global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(const MmaParams p) {
+    using Cf = Cfg<TYPE, MT, PAIR>;
     constexpr int S = Cf::S, WB = Cf::WB, XB = Cf::XB, NT = Cf::NT, PB = Cf::PB;
     constexpr int kGroups = Cf::G, kConsumers = Cf::kConsumers, kAll = Cf::kAll, kXWarps = Cf::kXWarps;
     constexpr int RS = NT * 8;  // floats per row in a partial
@@ -381,7 +386,8 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
     const int kc0 = rank * Kc / C, kr = (rank + 1) * Kc / C - kc0;
     const int t0 = q * I.tile_base + (q < I.tile_rem ? q : I.tile_rem);
     const int ntiles = I.tile_base + (q < I.tile_rem ? 1 : 0);
-    const int n = ntiles * kr;
+    const int kun = PAIR ? 2 * kr : kr;  // units per tile
+    const int n = ntiles * kun;
     const int64_t K = I.K, N = I.N;
     const int M = I.M;
 
@@ -390,8 +396,13 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
     // units are consecutive tile-chunks from w_base on.
     const uint8_t* const w_base = I.w + ((int64_t)t0 * Kc + kc0) * WB;
     auto w_issue = [&](int u, int stg) {
+        const uint8_t* src = w_base + (int64_t)u * WB;
+        if constexpr (PAIR) {  // unit u = chunk c of tile ti, gate for c < kr, up after
+            const int ti = u / kun, c = u - ti * kun;
+            src = (c < kr ? I.w : I.w_up) + ((int64_t)(t0 + ti) * Kc + kc0 + (c < kr ? c : c - kr)) * WB;
+        }
         ptx::mbar_arrive_expect_tx(&full[stg], WB);
-        ptx::bulk_g2s(wst + stg * WB, w_base + (int64_t)u * WB, WB, &full[stg]);
+        ptx::bulk_g2s(wst + stg * WB, src, WB, &full[stg]);
     };
 
     int w_issued = 0;  // producer lane 0: tile-chunk copies issued
@@ -548,18 +559,24 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
         for (int ti = 0; ti < ntiles; ++ti) {
             // acc[n8 token tile][c0..c3]: c0/c1 = row 16wg+g, tokens 8nt+2t,
             // 8nt+2t+1; c2/c3 = row 16wg+8+g.
+            // PAIR: accu/accu2 hold the up projection's sums.
             float acc[NT][4], acc2[Cf::kAccSets == 2 ? NT : 1][4];
+            float accu[PAIR ? NT : 1][4], accu2[(PAIR && Cf::kAccSets == 2) ? NT : 1][4];
+            auto zero = [](auto& A) {
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
+                for (int i = 0; i < (int)(sizeof(A) / sizeof(A[0])); ++i)
 #pragma unroll
-                for (int e = 0; e < 4; ++e) acc[nt][e] = 0.0f;
-            if constexpr (Cf::kAccSets == 2)
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) acc2[nt][e] = 0.0f;
-            for (int c = gi; c < kr; c += kGroups) {
-                const int u = ti * kr + c, stg = u % S;
+                    for (int e = 0; e < 4; ++e) A[i][e] = 0.0f;
+            };
+            zero(acc);
+            if constexpr (Cf::kAccSets == 2) zero(acc2);
+            if constexpr (PAIR) {
+                zero(accu);
+                if constexpr (Cf::kAccSets == 2) zero(accu2);
+            }
+            // Unit c of this tile into the sums A (A2: the second chain).
+            auto unit = [&](int c, auto& A, auto& A2) {
+                const int u = ti * kun + c, stg = u % S;
                 if (!dead && !ptx::mbar_wait(&full[stg], (uint32_t)(u / S) & 1u, ctl, 31)) dead = true;
                 if (!dead) {
                     Lane<TYPE> LA, LB;
@@ -574,46 +591,70 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
 #pragma unroll
                         for (int nt = 0; nt < NT; ++nt) {
                             const uint4 xv = xs[(nt * 8 + m) * 32];
-                            mma16816(acc[nt], pa[0], pb[0], pa[1], pb[1], xv.x, xv.y);
+                            mma16816(A[nt], pa[0], pb[0], pa[1], pb[1], xv.x, xv.y);
                             if constexpr (Cf::kAccSets == 2)
-                                mma16816(acc2[nt], pa[2], pb[2], pa[3], pb[3], xv.z, xv.w);
+                                mma16816(A2[nt], pa[2], pb[2], pa[3], pb[3], xv.z, xv.w);
                             else
-                                mma16816(acc[nt], pa[2], pb[2], pa[3], pb[3], xv.z, xv.w);
+                                mma16816(A[nt], pa[2], pb[2], pa[3], pb[3], xv.z, xv.w);
                         }
                     }
                 }
                 __syncwarp();
                 if (lane == 0) ptx::mbar_arrive(&empty[stg]);
-            }
-            if constexpr (Cf::kAccSets == 2)
+            };
+            int c = gi;
+            for (; c < kr; c += kGroups) unit(c, acc, acc2);
+            if constexpr (PAIR)
+                for (; c < kun; c += kGroups) unit(c, accu, accu2);
+            auto fold = [](auto& A, auto& A2) {
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) acc[nt][e] += acc2[nt][e];
+                    for (int e = 0; e < 4; ++e) A[nt][e] += A2[nt][e];
+            };
+            if constexpr (Cf::kAccSets == 2) {
+                fold(acc, acc2);
+                if constexpr (PAIR) fold(accu, accu2);
+            }
             // ---- tile end: groups 1.. hand their partials to group 0 ----
             const int r0 = 16 * wg + g;
-            if (gi > 0) {
-                float* cb = comb + ((gi - 1) * 2 + (ti & 1)) * (PB / 4);
+            auto slot = [&](int gg, int set) { return comb + (((gg - 1) * 2 + (ti & 1)) * Cf::SETS + set) * (PB / 4); };
+            auto put = [&](float* cb, auto& A) {
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
-                    *reinterpret_cast<float2*>(cb + r0 * RS + 8 * nt + 2 * tq) = make_float2(acc[nt][0], acc[nt][1]);
-                    *reinterpret_cast<float2*>(cb + (r0 + 8) * RS + 8 * nt + 2 * tq) = make_float2(acc[nt][2], acc[nt][3]);
+                    *reinterpret_cast<float2*>(cb + r0 * RS + 8 * nt + 2 * tq) = make_float2(A[nt][0], A[nt][1]);
+                    *reinterpret_cast<float2*>(cb + (r0 + 8) * RS + 8 * nt + 2 * tq) = make_float2(A[nt][2], A[nt][3]);
                 }
-            }
-            named_sync(1, kConsumers);
-            if (gi > 0) continue;
-            for (int gg = 1; gg < kGroups; ++gg) {
-                const float* cb = comb + ((gg - 1) * 2 + (ti & 1)) * (PB / 4);
+            };
+            auto add = [&](const float* cb, auto& A) {
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     const float2 a = *reinterpret_cast<const float2*>(cb + r0 * RS + 8 * nt + 2 * tq);
                     const float2 b = *reinterpret_cast<const float2*>(cb + (r0 + 8) * RS + 8 * nt + 2 * tq);
-                    acc[nt][0] += a.x;
-                    acc[nt][1] += a.y;
-                    acc[nt][2] += b.x;
-                    acc[nt][3] += b.y;
+                    A[nt][0] += a.x;
+                    A[nt][1] += a.y;
+                    A[nt][2] += b.x;
+                    A[nt][3] += b.y;
                 }
+            };
+            if (gi > 0) {
+                put(slot(gi, 0), acc);
+                if constexpr (PAIR) put(slot(gi, 1), accu);
             }
+            named_sync(1, kConsumers);
+            if (gi > 0) continue;
+            for (int gg = 1; gg < kGroups; ++gg) {
+                add(slot(gg, 0), acc);
+                if constexpr (PAIR) add(slot(gg, 1), accu);
+            }
+            // The value stored for element e: the sum, or silu(gate) * up, plus
+            // the residual.
+            auto result = [&](int nt, int e, int tok, int64_t row) {
+                float v = acc[nt][e];
+                if constexpr (PAIR) v = v / (1.0f + expf(-v)) * accu[nt][e];
+                if (I.res) v += I.res[tok * N + row];
+                return v;
+            };
             const int64_t tile = t0 + ti;
             if (C == 1) {
 #pragma unroll
@@ -622,7 +663,7 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
                     for (int e = 0; e < 4; ++e) {
                         const int tok = 8 * nt + 2 * tq + (e & 1);
                         const int64_t row = tile * TILE_ROWS + r0 + 8 * (e >> 1);
-                        if (tok < M && row < N) store_y(I.y, p.y_dtype, tok * N + row, acc[nt][e]);
+                        if (tok < M && row < N) store_y(I.y, p.y_dtype, tok * N + row, result(nt, e, tok, row));
                     }
             } else if (rank > 0) {
                 // Push this rank's partial to the leader: stage memory is free
@@ -674,7 +715,7 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT>::kAll, 1) mma_gemv_kernel(const 
                         for (int e = 0; e < 4; ++e) {
                             const int tok = 8 * nt + 2 * tq + (e & 1);
                             const int64_t row = tile * TILE_ROWS + r0 + 8 * (e >> 1);
-                            if (tok < M && row < N) store_y(I.y, p.y_dtype, tok * N + row, acc[nt][e]);
+                            if (tok < M && row < N) store_y(I.y, p.y_dtype, tok * N + row, result(nt, e, tok, row));
                         }
                 }
             }
@@ -715,6 +756,9 @@ int set_attr() {
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(mma_gemv_kernel<TYPE, MT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)Cf::smem);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(mma_gemv_kernel<TYPE, MT, false, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg<TYPE, MT, true>::smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute (mma_gemv)");
     int* mq = max_clusters<TYPE, MT>();
     mq[0] = g_sm_count;
@@ -744,6 +788,8 @@ struct HostItem {
     const void* x;
     void* y;
     int64_t M;
+    const Weight* w_up = nullptr;  // SwiGLU pairing (launches of one item)
+    const float* res = nullptr;    // residual added before the store
 };
 
 // Work split of a launch: C CTAs per cluster (K cut C ways, the same C for
@@ -758,7 +804,7 @@ int pick_split(const HostItem* it, int n, const int* maxq, int cmax, MmaParams* 
     int64_t T[kMaxItems], Kc[kMaxItems], q[kMaxItems], sumT = 0, minKc = INT64_MAX;
     for (int i = 0; i < n; ++i) {
         T[i] = it[i].w->shape.tiles;
-        Kc[i] = it[i].w->shape.chunks;
+        Kc[i] = it[i].w->shape.chunks * (it[i].w_up ? 2 : 1);  // a paired tile is two tiles' units
         q[i] = 1;
         sumT += T[i];
         if (Kc[i] < minKc) minKc = Kc[i];
@@ -795,20 +841,22 @@ int pick_split(const HostItem* it, int n, const int* maxq, int cmax, MmaParams* 
         m.y = it[i].y;
         m.N = it[i].w->shape.N;
         m.K = it[i].w->shape.K;
-        m.chunks = (int)Kc[i];
+        m.chunks = (int)it[i].w->shape.chunks;
         m.M = (int)it[i].M;
         m.cluster0 = cl;
         m.tile_base = (int)(T[i] / qi);
         m.tile_rem = (int)(T[i] % qi);
+        m.w_up = it[i].w_up ? it[i].w_up->dev : nullptr;
+        m.res = it[i].res;
         cl += (int)qi;
     }
     for (int i = n; i < kMaxItems; ++i) p->it[i] = MmaItem{};
     return cl;
 }
 
-template <int TYPE, int MT>
+template <int TYPE, int MT, bool PAIR = false>
 int launch(const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st) {
-    using Cf = Cfg<TYPE, MT>;
+    using Cf = Cfg<TYPE, MT, PAIR>;
     MmaParams p;
     for (int i = 0; i < n; ++i)
         if (it[i].w->shape.tile_chunk_bytes != Cf::WB)
@@ -834,8 +882,9 @@ int launch(const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st)
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = p.C > 1 ? 2 : 1;
-    cudaError_t e = (n == 1 && MT == 32) ? cudaLaunchKernelEx(&cfg, mma_gemv_kernel<TYPE, MT, false>, p)
-                                         : cudaLaunchKernelEx(&cfg, mma_gemv_kernel<TYPE, MT, true>, p);
+    cudaError_t e = PAIR                    ? cudaLaunchKernelEx(&cfg, mma_gemv_kernel<TYPE, MT, false, true>, p)
+                    : (n == 1 && MT == 32) ? cudaLaunchKernelEx(&cfg, mma_gemv_kernel<TYPE, MT, false>, p)
+                                           : cudaLaunchKernelEx(&cfg, mma_gemv_kernel<TYPE, MT, true>, p);
     note_launches(1);
     if (e != cudaSuccess) return cuda_fail(e, "mma_gemv launch");
     return NXQ_OK;
@@ -844,10 +893,15 @@ int launch(const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st)
 bool type_ok(int type) { return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || type == T_Q3_K; }
 
 int launch_items(int type, int mt, const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st) {
-#define NXQ_CASE(T)                                                               \
-    case T:                                                                       \
-        return mt == 8    ? launch<T, 8>(it, n, x_dtype, y_dtype, st)             \
-               : mt == 16 ? launch<T, 16>(it, n, x_dtype, y_dtype, st)            \
+    const bool pair = n == 1 && it[0].w_up;
+#define NXQ_CASE(T)                                                                                   \
+    case T:                                                                                           \
+        if (pair)                                                                                     \
+            return mt == 8    ? launch<T, 8, true>(it, n, x_dtype, y_dtype, st)                       \
+                   : mt == 16 ? launch<T, 16, true>(it, n, x_dtype, y_dtype, st)                      \
+                              : launch<T, 32, true>(it, n, x_dtype, y_dtype, st);                     \
+        return mt == 8    ? launch<T, 8>(it, n, x_dtype, y_dtype, st)                                 \
+               : mt == 16 ? launch<T, 16>(it, n, x_dtype, y_dtype, st)                                \
                           : launch<T, 32>(it, n, x_dtype, y_dtype, st);
     switch (type) {
         NXQ_CASE(T_Q4_K)
@@ -887,7 +941,8 @@ void mma_kernel_name(const TiledShape& s, int64_t M, char* buf, size_t n) {
     snprintf(buf, n, "mma_gemv<%s,m%d>", type_name(s.type), M <= 8 ? 8 : M <= 16 ? 16 : 32);
 }
 
-int mma_qmatmul(const Weight* w, const void* x, int x_dtype, void* y, int y_dtype, int64_t M, cudaStream_t st) {
+int mma_qmatmul(const Weight* w, const void* x, int x_dtype, void* y, int y_dtype, int64_t M, cudaStream_t st,
+                const float* res) {
     const TiledShape& s = w->shape;
     if (!mma_supported(s, M)) return NXQ_ERR_UNSUPPORTED;
     const int mt = M <= 8 ? 8 : M <= 16 ? 16 : 32;
@@ -906,8 +961,26 @@ int mma_qmatmul(const Weight* w, const void* x, int x_dtype, void* y, int y_dtyp
         xh = sc->xh;
         xdt = NXQ_F16;
     }
-    const HostItem item{w, xh, y, M};
+    HostItem item{w, xh, y, M};
+    item.res = res;
     return launch_items(s.type, mt, &item, 1, xdt, y_dtype, st);
+}
+
+int mma_qmatmul_swiglu(const Weight* wg, const Weight* wu, const void* x, int x_dtype, void* h, int h_dtype,
+                       int64_t M, cudaStream_t st) {
+    const TiledShape& s = wg->shape;
+    const TiledShape& su = wu->shape;
+    const bool aligned = ((uintptr_t)x % 16) == 0;
+    const bool direct = aligned && (x_dtype == NXQ_F16 || (M <= 2 && (x_dtype == NXQ_F32 || x_dtype == NXQ_BF16)));
+    // Pairing keeps one CTA per tile pair (no K split): worth it only when the
+    // weight has tiles for at least half the SMs.
+    if (!mma_supported(s, M) || !direct || su.type != s.type || su.N != s.N || su.K != s.K ||
+        s.tiles * 2 < g_sm_count)
+        return NXQ_ERR_UNSUPPORTED;
+    const int mt = M <= 8 ? 8 : M <= 16 ? 16 : 32;
+    HostItem item{wg, x, h, M};
+    item.w_up = wu;
+    return launch_items(s.type, mt, &item, 1, x_dtype, h_dtype, st);
 }
 
 int mma_qmatmul_grouped(const Weight* const* w, int n, const void* const* x, int x_dtype, void* const* y,

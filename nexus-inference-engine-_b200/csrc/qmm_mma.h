@@ -12,8 +12,14 @@ DeviceStatus* context_status();
 int mma_init(int device);
 bool mma_supported(const TiledShape& s, int64_t M);
 void mma_kernel_name(const TiledShape& s, int64_t M, char* buf, size_t n);
-// y = x W^T; NXQ_ERR_UNSUPPORTED to decline.
-int mma_qmatmul(const Weight* w, const void* x, int x_dtype, void* y, int y_dtype, int64_t M, cudaStream_t st);
+// y = x W^T (+ res, fp32 [M][N], if given); NXQ_ERR_UNSUPPORTED to decline.
+int mma_qmatmul(const Weight* w, const void* x, int x_dtype, void* y, int y_dtype, int64_t M, cudaStream_t st,
+                const float* res = nullptr);
+// h = silu(x Wg^T) * (x Wu^T) in one launch (each CTA takes a tile of both
+// weights); NXQ_ERR_UNSUPPORTED (nothing launched) unless the weights match,
+// M <= 32, x is read as it is and the weight has tiles for half the SMs.
+int mma_qmatmul_swiglu(const Weight* wg, const Weight* wu, const void* x, int x_dtype, void* h, int h_dtype,
+                       int64_t M, cudaStream_t st);
 // y_i = x_i W_i^T for n weights of one block type in as few launches as
 // possible (16 weights each); items with M_i = 0 are skipped.
 // NXQ_ERR_UNSUPPORTED (nothing launched) unless every item has 1 <= M_i <= 32

@@ -29,7 +29,8 @@ std::list<StreamScratch> g_scratch;
 
 }  // namespace
 
-int scratch_for(cudaStream_t st, size_t ws_floats, size_t n_counters, size_t xh_elems, StreamScratch** out) {
+int scratch_for(cudaStream_t st, size_t ws_floats, size_t n_counters, size_t xh_elems, StreamScratch** out,
+                size_t epi_floats) {
     std::lock_guard<std::mutex> lk(g_scratch_mu);
     StreamScratch* sc = nullptr;
     for (auto& e : g_scratch)
@@ -39,7 +40,8 @@ int scratch_for(cudaStream_t st, size_t ws_floats, size_t n_counters, size_t xh_
         sc = &g_scratch.back();
         sc->st = st;
     }
-    const bool grow = sc->ws_floats < ws_floats || sc->n_counters < n_counters || sc->xh_elems < xh_elems;
+    const bool grow = sc->ws_floats < ws_floats || sc->n_counters < n_counters || sc->xh_elems < xh_elems ||
+                      sc->epi_floats < epi_floats;
     if (grow) {
         cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
         if (cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
@@ -75,11 +77,62 @@ int scratch_for(cudaStream_t st, size_t ws_floats, size_t n_counters, size_t xh_
                 return cuda_fail(e, "cudaMalloc (f16 activations)");
             sc->xh_elems = xh_elems;
         }
+        if (sc->epi_floats < epi_floats) {
+            cudaFree(sc->epi);
+            sc->epi = nullptr;
+            sc->epi_floats = 0;
+            if ((e = cudaMalloc(&sc->epi, epi_floats * sizeof(float))) != cudaSuccess)
+                return cuda_fail(e, "cudaMalloc (epilogue intermediates)");
+            sc->epi_floats = epi_floats;
+        }
     }
     *out = sc;
     return NXQ_OK;
 }
 
+
+namespace {
+
+__device__ __forceinline__ void store_as(void* p, int dt, int64_t i, float v) {
+    if (dt == NXQ_F32)
+        reinterpret_cast<float*>(p)[i] = v;
+    else if (dt == NXQ_F16)
+        reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
+    else
+        reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+}
+
+__global__ void swiglu_kernel(const float* __restrict__ g, const float* __restrict__ u, void* __restrict__ h, int dt,
+                              int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float a = g[i];
+        store_as(h, dt, i, a / (1.0f + expf(-a)) * u[i]);
+    }
+}
+
+__global__ void add_residual_kernel(const float* __restrict__ a, const float* res, void* y, int dt, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        store_as(y, dt, i, a[i] + res[i]);
+}
+
+unsigned elementwise_grid(int64_t n) {
+    int64_t g = (n + 255) / 256;
+    return (unsigned)(g > 4096 ? 4096 : g < 1 ? 1 : g);
+}
+
+}  // namespace
+
+cudaError_t launch_swiglu(const float* g, const float* u, void* h, int h_dtype, int64_t n, cudaStream_t st) {
+    swiglu_kernel<<<elementwise_grid(n), 256, 0, st>>>(g, u, h, h_dtype, n);
+    note_launches(1);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_add_residual(const float* a, const float* res, void* y, int y_dtype, int64_t n, cudaStream_t st) {
+    add_residual_kernel<<<elementwise_grid(n), 256, 0, st>>>(a, res, y, y_dtype, n);
+    note_launches(1);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_to_half(const void* x, int dtype, __half* out, int64_t n, cudaStream_t st) {
     int64_t g = (n + 255) / 256;

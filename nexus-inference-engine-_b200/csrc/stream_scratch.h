@@ -19,13 +19,22 @@ struct StreamScratch {
     size_t n_counters = 0;
     __half* xh = nullptr;
     size_t xh_elems = 0;
+    float* epi = nullptr;  // fp32 intermediates of epilogues that run as their own kernel
+    size_t epi_floats = 0;
 };
 
 // Scratch of `st`, grown to at least the given sizes.  Growing synchronizes the
 // stream and is refused while the stream is being captured into a graph.
-int scratch_for(cudaStream_t st, size_t ws_floats, size_t n_counters, size_t xh_elems, StreamScratch** out);
+int scratch_for(cudaStream_t st, size_t ws_floats, size_t n_counters, size_t xh_elems, StreamScratch** out,
+                size_t epi_floats = 0);
 
 // out[i] = (half)x[i] for an f32/bf16/f16 array of n elements.
 cudaError_t launch_to_half(const void* x, int dtype, __half* out, int64_t n, cudaStream_t st);
+
+// h[i] = silu(g[i]) * u[i] = g[i] / (1 + exp(-g[i])) * u[i] in fp32, stored as h_dtype.
+cudaError_t launch_swiglu(const float* g, const float* u, void* h, int h_dtype, int64_t n, cudaStream_t st);
+
+// y[i] = a[i] + res[i] in fp32, stored as y_dtype (y may be res).
+cudaError_t launch_add_residual(const float* a, const float* res, void* y, int y_dtype, int64_t n, cudaStream_t st);
 
 }  // namespace nxq

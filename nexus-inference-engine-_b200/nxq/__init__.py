@@ -21,7 +21,7 @@ __all__ = [
     "NxqError", "lib", "init", "shutdown", "Weight", "qmatmul", "qmatmul_host", "stream_sync",
     "kernel_name", "launch_count",
     "TYPES", "GEOMETRY", "F32", "F16", "BF16", "SPLIT_COL", "SPLIT_ROW", "declared_symbols",
-    "tp_unique_id", "tp_init", "tp_shutdown", "tp_qmatmul", "tp_allreduce_f32", "GGUF", "qmatmul_grouped",
+    "tp_unique_id", "tp_init", "tp_shutdown", "tp_qmatmul", "tp_allreduce_f32", "GGUF", "qmatmul_grouped", "qmatmul_swiglu", "qmatmul_residual",
 ]
 
 LIB_PATH = Path(__file__).with_name("libnxq.so")
@@ -73,6 +73,10 @@ _SIGS = {
     "nxq_qmatmul_host": [_c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int64],
     "nxq_qmatmul_grouped": [_c.POINTER(_c.c_void_p), _c.c_int, _c.POINTER(_c.c_void_p), _c.c_int,
                             _c.POINTER(_c.c_void_p), _c.c_int, _c.POINTER(_c.c_int64), _c.c_void_p],
+    "nxq_qmatmul_swiglu": [_c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int, _c.c_void_p, _c.c_int, _c.c_int64,
+                           _c.c_void_p],
+    "nxq_qmatmul_residual": [_c.c_void_p, _c.c_void_p, _c.c_int, _c.c_void_p, _c.c_void_p, _c.c_int, _c.c_int64,
+                             _c.c_void_p],
     "nxq_qmatmul_noalloc": [_c.c_void_p, _c.c_void_p, _c.c_int, _c.c_void_p, _c.c_int, _c.c_int64,
                             _c.c_void_p],
     "nxq_stream_sync": [_c.c_void_p],
@@ -276,6 +280,33 @@ def qmatmul_grouped(ws, xs, outs=None, out_dtype=None, stream=None):
                                      _dtype_code(outs[0].dtype) if n else F32,
                                      (ctypes.c_int64 * max(n, 1))(*Ms), _stream_ptr(stream)))
     return outs
+
+
+def qmatmul_swiglu(w_gate: Weight, w_up: Weight, x, out=None, out_dtype=None, stream=None):
+    """h = silu(x Wg^T) * (x Wu^T), silu(g) = g / (1 + exp(-g))."""
+    import torch
+
+    assert x.is_cuda and x.is_contiguous() and x.shape[-1] == w_gate.K
+    M = x.numel() // w_gate.K
+    if out is None:
+        out = torch.empty((M, w_gate.N), dtype=out_dtype or torch.float32, device=x.device)
+    _check(lib().nxq_qmatmul_swiglu(w_gate.handle, w_up.handle, x.data_ptr(), _dtype_code(x.dtype), out.data_ptr(),
+                                    _dtype_code(out.dtype), M, _stream_ptr(stream)))
+    return out
+
+
+def qmatmul_residual(w: Weight, x, res, out=None, out_dtype=None, stream=None):
+    """y = x W^T + res (res fp32 [M][N]; out may be res)."""
+    import torch
+
+    assert x.is_cuda and x.is_contiguous() and x.shape[-1] == w.K
+    M = x.numel() // w.K
+    assert res.dtype == torch.float32 and res.is_contiguous() and res.numel() == M * w.N
+    if out is None:
+        out = torch.empty((M, w.N), dtype=out_dtype or torch.float32, device=x.device)
+    _check(lib().nxq_qmatmul_residual(w.handle, x.data_ptr(), _dtype_code(x.dtype), res.data_ptr(), out.data_ptr(),
+                                      _dtype_code(out.dtype), M, _stream_ptr(stream)))
+    return out
 
 
 def qmatmul_host(w: Weight, x: np.ndarray, out: Optional[np.ndarray] = None) -> np.ndarray:

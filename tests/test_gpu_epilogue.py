@@ -1,0 +1,122 @@
+"""GPU: the fused epilogues against the oracle.
+
+nxq_qmatmul_swiglu: h = silu(x Wg^T) * (x Wu^T), silu(g) = g / (1 + exp(-g)),
+with the oracle's fp32 products combined in float64; one launch when the weight
+has tiles for half the SMs (each CTA takes a tile of gate and up), otherwise
+gate/up then a small kernel (few tiles, prefill batch sizes).
+nxq_qmatmul_residual: y = x W^T + res, fused into the decode kernel's store,
+after the product otherwise; in place (y is the residual buffer) and not.
+Tolerance: rel-L2 <= 1e-3 (the parity bar) for fp32 outputs.  A bf16 output
+is compared with the unrounded oracle under rel-L2 <= 1e-3 + 2^-8: storing in
+bf16 alone adds up to half an ulp (2^-9 relative) per value, and comparing two
+bf16 roundings instead would count whole-ulp flips of values the matmul moved
+by less than 1e-3 (SwiGLU multiplies two such values)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import NAMES
+from oracle import loader
+from nxq import synth
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
+TOL_BF16 = 1e-3 + 2.0 ** -8
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def _silu_mul(g, u):
+    g = g.astype(np.float64)
+    return g / (1.0 + np.exp(-g)) * u.astype(np.float64)
+
+
+def _pair(gpu, t, N, K, seed):
+    bg = synth.make_blocks(t, N, K, seed=seed)
+    bu = synth.make_blocks(t, N, K, seed=seed + 1)
+    return bg, bu, gpu.Weight.register(bg, t, N, K), gpu.Weight.register(bu, t, N, K)
+
+
+@pytest.mark.parametrize("t", [12, 11, 8], ids=lambda t: NAMES[t])
+@pytest.mark.parametrize("M", [1, 4, 16, 32])
+def test_swiglu_fused_one_launch(gpu, t, M):
+    torch = _torch()
+    N, K = 9728, 512  # 76 tiles: the paired path
+    bg, bu, wg, wu = _pair(gpu, t, N, K, seed=40 + M)
+    try:
+        x = torch.from_numpy(synth.make_activations(M, K, seed=M)).cuda()
+        gpu.qmatmul_swiglu(wg, wu, x)  # warm-up
+        torch.cuda.synchronize()
+        n0 = gpu.launch_count()
+        h = gpu.qmatmul_swiglu(wg, wu, x)
+        n1 = gpu.launch_count()
+        torch.cuda.synchronize()
+        assert n1 - n0 == 1
+        xf = x.float().cpu().numpy()
+        want = _silu_mul(loader.qmatmul(t, bg, N, K, xf), loader.qmatmul(t, bu, N, K, xf))
+        assert synth.rel_l2(h.cpu().numpy(), want) < TOL
+    finally:
+        wg.release()
+        wu.release()
+
+
+@pytest.mark.parametrize("N,K,M,out", [(512, 1024, 3, "f32"), (512, 1024, 40, "f32"), (9728, 512, 2, "bf16"),
+                                       (1024, 256, 1, "bf16")])
+def test_swiglu_other_paths(gpu, N, K, M, out):
+    torch = _torch()
+    t = 12
+    bg, bu, wg, wu = _pair(gpu, t, N, K, seed=60)
+    try:
+        x = torch.from_numpy(synth.make_activations(M, K, seed=7)).cuda()
+        dt = torch.float32 if out == "f32" else torch.bfloat16
+        h = gpu.qmatmul_swiglu(wg, wu, x, out_dtype=dt)
+        torch.cuda.synchronize()
+        xf = x.float().cpu().numpy()
+        want = _silu_mul(loader.qmatmul(t, bg, N, K, xf), loader.qmatmul(t, bu, N, K, xf))
+        assert synth.rel_l2(h.float().cpu().numpy(), want) < (TOL if out == "f32" else TOL_BF16)
+    finally:
+        wg.release()
+        wu.release()
+
+
+@pytest.mark.parametrize("t", [12, 11, 8, 2], ids=lambda t: NAMES[t])
+@pytest.mark.parametrize("M", [1, 8, 32, 40])
+@pytest.mark.parametrize("inplace", [False, True])
+def test_residual(gpu, t, M, inplace):
+    torch = _torch()
+    N, K = 1024, 1024
+    b = synth.make_blocks(t, N, K, seed=90 + M)
+    w = gpu.Weight.register(b, t, N, K)
+    try:
+        x = torch.from_numpy(synth.make_activations(M, K, seed=M)).cuda()
+        res = torch.from_numpy(synth.make_activations(M, N, seed=500 + M).astype(np.float32)).cuda()
+        res0 = res.cpu().numpy().astype(np.float64)
+        y = gpu.qmatmul_residual(w, x, res, out=res if inplace else None)
+        torch.cuda.synchronize()
+        want = loader.qmatmul(t, b, N, K, x.float().cpu().numpy()).astype(np.float64) + res0
+        assert synth.rel_l2(y.cpu().numpy(), want) < TOL
+    finally:
+        w.release()
+
+
+def test_epilogue_errors(gpu):
+    torch = _torch()
+    t = 12
+    wa = gpu.Weight.register(synth.make_blocks(t, 256, 512, seed=1), t, 256, 512)
+    wb = gpu.Weight.register(synth.make_blocks(t, 512, 512, seed=2), t, 512, 512)
+    try:
+        x = torch.zeros(1, 512, dtype=torch.float16, device="cuda")
+        h = torch.empty(1, 256, device="cuda")
+        L = gpu.lib()
+        assert L.nxq_qmatmul_swiglu(wa.handle, wb.handle, x.data_ptr(), 1, h.data_ptr(), 0, 1, None) == -3
+        assert L.nxq_qmatmul_residual(wa.handle, x.data_ptr(), 1, None, h.data_ptr(), 0, 1, None) == -1
+        assert L.nxq_qmatmul_swiglu(wa.handle, wa.handle, x.data_ptr(), 1, h.data_ptr(), 0, 0, None) == 0
+    finally:
+        wa.release()
+        wb.release()
