@@ -199,6 +199,15 @@ NXQ_API int nxq_qmatmul_swiglu(nxq_weight_t w_gate, nxq_weight_t w_up, const voi
 NXQ_API int nxq_qmatmul_residual(nxq_weight_t w, const void* x_dev, int x_dtype, const float* res_dev,
                                  void* y_dev, int y_dtype, int64_t M, void* stream);
 
+/* Fused RMSNorm prologue (fused_qkv_int4.metal:50-71): every token row of x_dev
+ * [M][K] is normalized once, xn = x * r * norm_dev with r = 1/sqrt(sum(x^2)/K +
+ * eps) (fp32, rounded to f16), and y_dev[i] = xn W_i^T for the `count` weights
+ * that take it (q/k/v: count 3; all of equal K), as one normalization kernel
+ * and one grouped decode launch (M <= 32; nxq_qmatmul calls beyond). */
+NXQ_API int nxq_rmsnorm_qmatmul(const nxq_weight_t* w, int count, const void* x_dev, int x_dtype,
+                                const float* norm_dev, float eps, void* const* y_dev, int y_dtype,
+                                int64_t M, void* stream);
+
 /* Host-buffer form, synchronous: the drop-in for ComputeDispatch::gemm_int4
  * (compute_dispatch.h:59-61, .cpp:142-176) - fp32 activations [M][K] in, fp32
  * output [M][N] out, weights resident.  The reference ignores M

@@ -536,6 +536,39 @@ NXQ_API int nxq_qmatmul_swiglu(nxq_weight_t hg, nxq_weight_t hu, const void* x_d
     return e == cudaSuccess ? NXQ_OK : cuda_fail(e, "swiglu launch");
 }
 
+NXQ_API int nxq_rmsnorm_qmatmul(const nxq_weight_t* hs, int count, const void* x_dev, int x_dtype,
+                                const float* norm_dev, float eps, void* const* y_dev, int y_dtype, int64_t M,
+                                void* stream) {
+    if (count < 1 || !hs || !y_dev) return fail(NXQ_ERR_ARG, "rmsnorm_qmatmul: bad arrays");
+    if (M < 0 || !(eps >= 0.0f)) return fail(NXQ_ERR_ARG, "rmsnorm_qmatmul: M=%lld eps=%g", (long long)M, (double)eps);
+    if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return fail(NXQ_ERR_ARG, "bad dtype");
+    std::vector<Weight*> ws((size_t)count);
+    for (int i = 0; i < count; ++i) {
+        if (int rc = check_weight(hs[i], &ws[i])) return rc;
+        if (ws[i]->shape.K != ws[0]->shape.K)
+            return fail(NXQ_ERR_SHAPE, "rmsnorm_qmatmul: weight %d has K=%lld, weight 0 K=%lld", i,
+                        (long long)ws[i]->shape.K, (long long)ws[0]->shape.K);
+        if (M > 0 && !y_dev[i]) return fail(NXQ_ERR_ARG, "rmsnorm_qmatmul: null output %d", i);
+    }
+    if (M == 0) return NXQ_OK;
+    if (!x_dev || !norm_dev) return fail(NXQ_ERR_ARG, "rmsnorm_qmatmul: null activation or norm weight");
+    if (int rc = check_ready()) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int64_t K = ws[0]->shape.K;
+    StreamScratch* sc = nullptr;
+    int rc = scratch_for(st, 0, 0, (size_t)(M * K), &sc);
+    if (rc) return rc;
+    cudaError_t e = launch_rmsnorm_to_half(x_dev, x_dtype, norm_dev, eps, sc->xh, M, K, st);
+    if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
+    std::vector<const void*> xs((size_t)count, sc->xh);
+    std::vector<int64_t> Ms((size_t)count, M);
+    rc = mma_qmatmul_grouped(ws.data(), count, xs.data(), NXQ_F16, y_dev, y_dtype, Ms.data(), st);
+    if (rc != NXQ_ERR_UNSUPPORTED) return rc;
+    for (int i = 0; i < count; ++i)
+        if ((rc = qmatmul_dispatch(ws[i], sc->xh, NXQ_F16, y_dev[i], y_dtype, M, st))) return rc;
+    return NXQ_OK;
+}
+
 NXQ_API int nxq_qmatmul_residual(nxq_weight_t h, const void* x_dev, int x_dtype, const float* res_dev, void* y_dev,
                                  int y_dtype, int64_t M, void* stream) {
     Weight* w = nullptr;

@@ -115,6 +115,43 @@ __global__ void add_residual_kernel(const float* __restrict__ a, const float* re
         store_as(y, dt, i, a[i] + res[i]);
 }
 
+__device__ __forceinline__ float load_as(const void* p, int dt, int64_t i) {
+    if (dt == NXQ_F32) return reinterpret_cast<const float*>(p)[i];
+    if (dt == NXQ_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+}
+
+constexpr int kNormThreads = 512;
+
+// One CTA per row: sum of squares (per-thread partials, then warps, then the
+// CTA), r = rsqrtf(sum / K + eps), then the scaled row.
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_to_half_kernel(const void* __restrict__ x, int dt,
+                                                                     const float* __restrict__ w, float eps,
+                                                                     __half* __restrict__ out, int64_t K) {
+    __shared__ float part[kNormThreads / 32];
+    __shared__ float r_s;
+    const int64_t row = blockIdx.x;
+    float ss = 0.0f;
+    for (int64_t i = threadIdx.x; i < K; i += kNormThreads) {
+        const float v = load_as(x, dt, row * K + i);
+        ss = fmaf(v, v, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float t = threadIdx.x < kNormThreads / 32 ? part[threadIdx.x] : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xFFFFFFFFu, t, o);
+        if (threadIdx.x == 0) r_s = rsqrtf(t / (float)K + eps);
+    }
+    __syncthreads();
+    const float r = r_s;
+    for (int64_t i = threadIdx.x; i < K; i += kNormThreads)
+        out[row * K + i] = __float2half_rn(load_as(x, dt, row * K + i) * r * w[i]);
+}
+
 unsigned elementwise_grid(int64_t n) {
     int64_t g = (n + 255) / 256;
     return (unsigned)(g > 4096 ? 4096 : g < 1 ? 1 : g);
@@ -124,6 +161,13 @@ unsigned elementwise_grid(int64_t n) {
 
 cudaError_t launch_swiglu(const float* g, const float* u, void* h, int h_dtype, int64_t n, cudaStream_t st) {
     swiglu_kernel<<<elementwise_grid(n), 256, 0, st>>>(g, u, h, h_dtype, n);
+    note_launches(1);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm_to_half(const void* x, int x_dtype, const float* w, float eps, __half* out, int64_t M,
+                                   int64_t K, cudaStream_t st) {
+    rmsnorm_to_half_kernel<<<(unsigned)M, kNormThreads, 0, st>>>(x, x_dtype, w, eps, out, K);
     note_launches(1);
     return cudaGetLastError();
 }

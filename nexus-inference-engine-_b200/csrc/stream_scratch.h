@@ -34,6 +34,11 @@ cudaError_t launch_to_half(const void* x, int dtype, __half* out, int64_t n, cud
 // h[i] = silu(g[i]) * u[i] = g[i] / (1 + exp(-g[i])) * u[i] in fp32, stored as h_dtype.
 cudaError_t launch_swiglu(const float* g, const float* u, void* h, int h_dtype, int64_t n, cudaStream_t st);
 
+// RMSNorm of each of the M rows of x [M][K] (f32/bf16/f16): out = f16(x * r * w)
+// with r = 1 / sqrt(sum(x^2) / K + eps), all in fp32; one CTA per row.
+cudaError_t launch_rmsnorm_to_half(const void* x, int x_dtype, const float* w, float eps, __half* out, int64_t M,
+                                   int64_t K, cudaStream_t st);
+
 // y[i] = a[i] + res[i] in fp32, stored as y_dtype (y may be res).
 cudaError_t launch_add_residual(const float* a, const float* res, void* y, int y_dtype, int64_t n, cudaStream_t st);
 

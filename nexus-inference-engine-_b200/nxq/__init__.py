@@ -21,7 +21,7 @@ __all__ = [
     "NxqError", "lib", "init", "shutdown", "Weight", "qmatmul", "qmatmul_host", "stream_sync",
     "kernel_name", "launch_count",
     "TYPES", "GEOMETRY", "F32", "F16", "BF16", "SPLIT_COL", "SPLIT_ROW", "declared_symbols",
-    "tp_unique_id", "tp_init", "tp_shutdown", "tp_qmatmul", "tp_allreduce_f32", "GGUF", "qmatmul_grouped", "qmatmul_swiglu", "qmatmul_residual",
+    "tp_unique_id", "tp_init", "tp_shutdown", "tp_qmatmul", "tp_allreduce_f32", "GGUF", "qmatmul_grouped", "qmatmul_swiglu", "qmatmul_residual", "rmsnorm_qmatmul",
 ]
 
 LIB_PATH = Path(__file__).with_name("libnxq.so")
@@ -77,6 +77,8 @@ _SIGS = {
                            _c.c_void_p],
     "nxq_qmatmul_residual": [_c.c_void_p, _c.c_void_p, _c.c_int, _c.c_void_p, _c.c_void_p, _c.c_int, _c.c_int64,
                              _c.c_void_p],
+    "nxq_rmsnorm_qmatmul": [_c.POINTER(_c.c_void_p), _c.c_int, _c.c_void_p, _c.c_int, _c.c_void_p, _c.c_float,
+                            _c.POINTER(_c.c_void_p), _c.c_int, _c.c_int64, _c.c_void_p],
     "nxq_qmatmul_noalloc": [_c.c_void_p, _c.c_void_p, _c.c_int, _c.c_void_p, _c.c_int, _c.c_int64,
                             _c.c_void_p],
     "nxq_stream_sync": [_c.c_void_p],
@@ -307,6 +309,26 @@ def qmatmul_residual(w: Weight, x, res, out=None, out_dtype=None, stream=None):
     _check(lib().nxq_qmatmul_residual(w.handle, x.data_ptr(), _dtype_code(x.dtype), res.data_ptr(), out.data_ptr(),
                                       _dtype_code(out.dtype), M, _stream_ptr(stream)))
     return out
+
+
+def rmsnorm_qmatmul(ws, x, norm, eps: float, outs=None, out_dtype=None, stream=None):
+    """y_i = (x * r * norm) W_i^T, r = 1 / sqrt(mean(x^2) + eps) per token row;
+    norm is an fp32 CUDA tensor [K]; all weights share K."""
+    import torch
+
+    ws = list(ws)
+    K = ws[0].K
+    assert x.is_cuda and x.is_contiguous() and x.shape[-1] == K
+    assert norm.dtype == torch.float32 and norm.is_contiguous() and norm.numel() == K
+    M = x.numel() // K
+    if outs is None:
+        outs = [torch.empty((M, w.N), dtype=out_dtype or torch.float32, device=x.device) for w in ws]
+    n = len(ws)
+    arr = ctypes.c_void_p * n
+    _check(lib().nxq_rmsnorm_qmatmul(arr(*[w.handle.value for w in ws]), n, x.data_ptr(), _dtype_code(x.dtype),
+                                     norm.data_ptr(), eps, arr(*[y.data_ptr() for y in outs]),
+                                     _dtype_code(outs[0].dtype), M, _stream_ptr(stream)))
+    return outs
 
 
 def qmatmul_host(w: Weight, x: np.ndarray, out: Optional[np.ndarray] = None) -> np.ndarray:

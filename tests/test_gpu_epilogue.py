@@ -120,3 +120,39 @@ def test_epilogue_errors(gpu):
     finally:
         wa.release()
         wb.release()
+
+
+@pytest.mark.parametrize("M", [1, 4, 32, 40])
+@pytest.mark.parametrize("xdt", ["f32", "bf16", "f16"])
+def test_rmsnorm_prologue(gpu, M, xdt):
+    """nxq_rmsnorm_qmatmul: y_i = (x * r * g) W_i^T, r = 1/sqrt(mean(x^2) + eps),
+    against the normalization in float64 and the oracle matmul; two launches
+    (normalization + one grouped GEMV) for decode batch sizes."""
+    torch = _torch()
+    t, K, eps = 11, 2048, 1e-6
+    shapes = [(512, K), (128, K), (128, K)]
+    blocks = [synth.make_blocks(t, N, K, seed=120 + i) for i, (N, _) in enumerate(shapes)]
+    ws = [gpu.Weight.register(b, t, N, K) for b, (N, _) in zip(blocks, shapes)]
+    try:
+        rng = np.random.default_rng(M)
+        x32 = (rng.standard_normal((M, K)) * 3.0 + 0.5).astype(np.float32)
+        g32 = rng.uniform(0.5, 1.5, K).astype(np.float32)
+        dt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[xdt]
+        x = torch.from_numpy(x32).to(dt).cuda()
+        g = torch.from_numpy(g32).cuda()
+        gpu.rmsnorm_qmatmul(ws, x, g, eps)  # warm-up (scratch)
+        torch.cuda.synchronize()
+        n0 = gpu.launch_count()
+        ys = gpu.rmsnorm_qmatmul(ws, x, g, eps)
+        n1 = gpu.launch_count()
+        torch.cuda.synchronize()
+        if M <= 32:
+            assert n1 - n0 == 2
+        xin = x.float().cpu().numpy().astype(np.float64)
+        xn = xin / np.sqrt((xin * xin).mean(axis=1, keepdims=True) + eps) * g32.astype(np.float64)
+        for (N, _), b, y in zip(shapes, blocks, ys):
+            want = loader.qmatmul(t, b, N, K, xn.astype(np.float32))
+            assert synth.rel_l2(y.cpu().numpy(), want) < TOL
+    finally:
+        for w in ws:
+            w.release()
