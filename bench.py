@@ -415,6 +415,27 @@ def bench_config3(dev, stream, pk) -> dict:
         issue_grouped()
     stream.synchronize()
     ms_g = graph_time_ms(issue_grouped, stream) / L
+
+    # The layer with every fused prologue/epilogue: RMSNorm + q/k/v (one
+    # normalization kernel + one grouped launch), o with the residual add,
+    # gate/up with SwiGLU (one paired launch), down with the residual add:
+    # 5 launches doing strictly more than the 7 plain GEMVs above.
+    resid = torch.randn(1, 4096, generator=torch.Generator().manual_seed(7), dtype=torch.float32).to(dev)
+    normw = torch.rand(4096, generator=torch.Generator().manual_seed(8), dtype=torch.float32).add_(0.5).to(dev)
+    hbuf = torch.empty(1, 14336, dtype=torch.float16, device=dev)
+
+    def issue_fused():
+        for r in range(L):
+            nxq.rmsnorm_qmatmul([layer[n][r] for n in ("q", "k", "v")], resid, normw, 1e-5,
+                                outs=[yg[n] for n in ("q", "k", "v")], stream=stream)
+            nxq.qmatmul_residual(layer["o"][r], xs[4096], resid, out=resid, stream=stream)
+            nxq.qmatmul_swiglu(layer["gate"][r], layer["up"][r], xs[4096], out=hbuf, stream=stream)
+            nxq.qmatmul_residual(layer["down"][r], hbuf, resid, out=resid, stream=stream)
+
+    with torch.cuda.stream(stream):
+        issue_fused()
+    stream.synchronize()
+    ms_f = graph_time_ms(issue_fused, stream) / L
     out = {"workload": "BASELINE config 3: Q8_0 GEMV M=1, the 7 projections of a Llama-3-8B layer "
                        "(q/o 4096x4096, k/v 4096->1024, gate/up 4096->14336, down 14336->4096), f16 x, fp32 y",
            "kernel": nxq.kernel_name(layer["q"][0], 1), "per_projection": per,
@@ -422,11 +443,63 @@ def bench_config3(dev, stream, pk) -> dict:
            "layer_frac_of_hbm": nb / (ms / 1e3) / 1e9 / pk["hbm_gbs"], "layer_replicas": L,
            "layer_grouped": {"us": ms_g * 1e3, "GB/s": nb / (ms_g / 1e3) / 1e9,
                              "frac_of_hbm": nb / (ms_g / 1e3) / 1e9 / pk["hbm_gbs"], "launches": 4,
-                             "how": "q/k/v and gate/up each one nxq_qmatmul_grouped launch"}}
+                             "how": "q/k/v and gate/up each one nxq_qmatmul_grouped launch"},
+           "layer_fused": {"us": ms_f * 1e3, "GB/s": nb / (ms_f / 1e3) / 1e9,
+                           "frac_of_hbm": nb / (ms_f / 1e3) / 1e9 / pk["hbm_gbs"], "launches": 5,
+                           "how": "RMSNorm + q/k/v (nxq_rmsnorm_qmatmul), o + residual, gate/up + SwiGLU "
+                                  "(nxq_qmatmul_swiglu), down + residual (nxq_qmatmul_residual)"}}
     for ws in layer.values():
         for w in ws:
             w.release()
     return out
+
+
+def bench_swiglu(dev, stream, pk) -> dict:
+    """Config-2 gate/up pair (Q4_K, K=4096, N=14336) with the SwiGLU epilogue:
+    nxq_qmatmul_swiglu (one launch over both weights) against two plain calls
+    (which leave the activation still to do), M in {1, 8, 32}."""
+    import torch
+
+    import nxq
+    from nxq import synth
+
+    K, N = 4096, 14336
+    wb = weight_bytes(K, N)
+    R = replicas_for(2 * wb)
+    bg = synth.make_blocks(Q4_K, N, K, seed=4100)
+    bu = synth.make_blocks(Q4_K, N, K, seed=4101)
+    gs = [nxq.Weight.register(bg, Q4_K, N, K) for _ in range(R)]
+    us = [nxq.Weight.register(bu, Q4_K, N, K) for _ in range(R)]
+    del bg, bu
+    cases = {}
+    for M in (1, 8, 32):
+        x = torch.randn(M, K, generator=torch.Generator().manual_seed(M), dtype=torch.float32).to(torch.float16).to(dev)
+        h = torch.empty(M, N, dtype=torch.float16, device=dev)
+        yg = torch.empty(M, N, dtype=torch.float32, device=dev)
+        yu = torch.empty(M, N, dtype=torch.float32, device=dev)
+
+        def fused(M=M, x=x, h=h):
+            for r in range(R):
+                nxq.qmatmul_swiglu(gs[r], us[r], x, out=h, stream=stream)
+
+        def plain(x=x, yg=yg, yu=yu):
+            for r in range(R):
+                nxq.qmatmul(gs[r], x, out=yg, stream=stream)
+                nxq.qmatmul(us[r], x, out=yu, stream=stream)
+
+        res = {}
+        for name, fn in (("fused", fused), ("two_calls", plain)):
+            with torch.cuda.stream(stream):
+                fn()
+            stream.synchronize()
+            ms = graph_time_ms(fn, stream) / R
+            res[name] = {"us": round(ms * 1e3, 2), "GB/s": round(2 * wb / (ms / 1e3) / 1e9, 1)}
+        cases[f"M{M}"] = res
+    for w in gs + us:
+        w.release()
+    return {"workload": "config-2 gate/up pair, Q4_K K=4096 N=14336, f16 x; fused: h = silu(x Wg^T) * (x Wu^T) "
+                        "stored as f16 in one launch; two_calls: the two products only",
+            "cases": cases, "replicas": R}
 
 
 def bench_tp_layer(dev, stream, pk, rank: int, world: int) -> dict:
@@ -713,6 +786,7 @@ def run_gpu_arm(args, rank, world, local):
         if world == 1:
             extra["config1"] = bench_config1(dev, stream, pk)
             extra["config3"] = bench_config3(dev, stream, pk)
+            extra["swiglu_gate_up"] = bench_swiglu(dev, stream, pk)
         extra["tp_config5"] = bench_tp_layer(dev, stream, pk, rank, world)
         torch.cuda.empty_cache()
 
