@@ -55,7 +55,11 @@ typedef enum {
     NXQ_ERR_FORMAT = -10      /* a file that is not GGUF v2/v3 or is truncated */
 } nxq_status;
 
-/* Block types: the GGUF type ids of nexus/src/import/gguf_importer.h:28-57. */
+/* Block types: the GGUF type ids of nexus/src/import/gguf_importer.h:28-57,
+ * and the NXF INT4 group format (quant/gptq.cpp:9-70: w = (q - zero) * scale,
+ * one fp32 scale and zero per group of gs elements along K) as blocks of one
+ * group, [scale f32][zero f32][gs/2 code bytes: element 2i in the low, 2i+1
+ * in the high nibble of byte i], ids 100 + gs/32 (outside the GGUF range). */
 typedef enum {
     NXQ_TYPE_Q4_0 = 2,
     NXQ_TYPE_Q4_1 = 3,
@@ -64,7 +68,11 @@ typedef enum {
     NXQ_TYPE_Q3_K = 11,
     NXQ_TYPE_Q4_K = 12,
     NXQ_TYPE_Q5_K = 13,
-    NXQ_TYPE_Q6_K = 14
+    NXQ_TYPE_Q6_K = 14,
+    NXQ_TYPE_I4G32 = 101,
+    NXQ_TYPE_I4G64 = 102,
+    NXQ_TYPE_I4G128 = 104,
+    NXQ_TYPE_I4G256 = 108
 } nxq_type;
 
 /* Activation / output element types: nexus::DType F32=0, F16=1, BF16=2
@@ -133,6 +141,27 @@ NXQ_API int nxq_weight_register_shard(const void* host_blocks, size_t bytes, int
 NXQ_API int nxq_shard_extract(const void* host_blocks, size_t bytes, int type, int64_t N,
                               int64_t K, int split, int rank, int world, void* out,
                               size_t out_bytes);
+
+/* NXF INT4 group weights from their separate arrays (the operands of
+ * ComputeDispatch::gemv_int4, compute_dispatch.h:47-49): packed 4-bit codes,
+ * fp32 scales and zeros (zeros may be NULL: zero 0) for groups of group_size
+ * (32, 64, 128 or 256; a divisor of K) elements along K.  `layout` says how the
+ * arrays are ordered:
+ *   NXQ_INT4_ROWS   quant/gptq.cpp's flat order over W[N][K]: element (n, k) is
+ *                   nibble (n*K + k) of codes (low nibble first), group
+ *                   (n*K + k) / group_size of scales and zeros;
+ *   NXQ_INT4_KMAJOR gemv_dequant_int4's order (gemm_dequant.metal:29-70): codes
+ *                   [K/2][N], byte (k/2)*N + n holding k (low) and k+1 (high);
+ *                   scales, zeros [K/group_size][N].
+ * nxq_int4_pack (host only, no GPU) writes the NXQ_TYPE_I4G<gs> blocks [N][K/gs]
+ * into out (out_bytes = N * (K/gs) * (8 + gs/2)); nxq_weight_register_int4 packs
+ * and registers them. */
+typedef enum { NXQ_INT4_ROWS = 0, NXQ_INT4_KMAJOR = 1 } nxq_int4_layout;
+NXQ_API int nxq_int4_pack(const uint8_t* codes, const float* scales, const float* zeros, int64_t N,
+                          int64_t K, int group_size, int layout, void* out, size_t out_bytes);
+NXQ_API int nxq_weight_register_int4(const uint8_t* codes, const float* scales, const float* zeros,
+                                     int64_t N, int64_t K, int group_size, int layout,
+                                     nxq_weight_t* out);
 
 /* Free the HBM copy (ComputeDispatch::clear_buffer_cache, compute_dispatch.cpp:853-860). */
 NXQ_API int nxq_weight_release(nxq_weight_t w);

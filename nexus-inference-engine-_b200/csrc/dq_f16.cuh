@@ -65,6 +65,26 @@ struct Group<T_Q4_K> {
     }
 };
 
+// NXF INT4 groups of 128 (quant/gptq.cpp:9-27): record = [(scale, zero) x2 :
+// 16 B][codes x8 of 16 B]; 32-element group G lies in block G / 4.  The weight
+// is fl16(q * fl16(scale) + fl16(-(zero * scale))).
+template <>
+struct Group<T_I4G128> {
+    static constexpr int kStage = TILE_ROWS * 144;
+    template <int G>
+    __device__ __forceinline__ static void decode(const uint8_t* stage, int r, uint32_t (&o)[16]) {
+        const uint8_t* rec = stage + r * 144;
+        const float2 sz = *reinterpret_cast<const float2*>(rec + 8 * (G / 4));
+        const __half2 s2 = __float2half2_rn(sz.x);
+        const __half2 o2 = __float2half2_rn(-(sz.y * sz.x));
+        const uint4 q = *reinterpret_cast<const uint4*>(rec + 16 + 16 * G);
+        q4_word_pairs(q.x, s2, o2, &o[0]);
+        q4_word_pairs(q.y, s2, o2, &o[4]);
+        q4_word_pairs(q.z, s2, o2, &o[8]);
+        q4_word_pairs(q.w, s2, o2, &o[12]);
+    }
+};
+
 // Q4_0 (gguf_importer.cpp:679-695): record = [d x8][codes x8 of 16 B]; group G
 // = block G.
 template <>

@@ -33,8 +33,21 @@ constexpr int CHUNK_K = 256;
 
 enum BlockType : int {
     T_Q4_0 = 2, T_Q4_1 = 3, T_Q8_0 = 8, T_Q2_K = 10, T_Q3_K = 11,
-    T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14
+    T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14,
+    // NXF INT4 with one fp32 scale and zero per group of gs elements along K
+    // (quant/gptq.cpp:9-27: w = (q - zero) * scale), as blocks of one group:
+    // [scale f32][zero f32][gs/2 code bytes, element 2i low / 2i+1 high nibble
+    // of byte i].  Ids outside the GGUF range: 100 + gs / 32.
+    T_I4G32 = 101, T_I4G64 = 102, T_I4G128 = 104, T_I4G256 = 108
 };
+
+__host__ __device__ constexpr bool is_i4g(int type) {
+    return type == T_I4G32 || type == T_I4G64 || type == T_I4G128 || type == T_I4G256;
+}
+// Group size of an I4G type; the header of its tiled row record (one 8-byte
+// scale/zero pair per block of the chunk, padded to 16 bytes).
+__host__ __device__ constexpr int i4g_gs(int type) { return 32 * (type - 100); }
+__host__ __device__ constexpr int i4g_hdr(int type) { return ((8 * (CHUNK_K / i4g_gs(type))) + 15) & ~15; }
 
 struct Geometry {
     int qk;    // elements per block
@@ -53,11 +66,15 @@ __host__ __device__ inline bool geometry_of(int type, Geometry* g) {
         case T_Q4_K: qk = 256; bb = 144; break;
         case T_Q5_K: qk = 256; bb = 176; break;
         case T_Q6_K: qk = 256; bb = 210; break;
+        case T_I4G32: case T_I4G64: case T_I4G128: case T_I4G256:
+            qk = i4g_gs(type);
+            bb = 8 + qk / 2;
+            break;
         default: return false;
     }
     g->qk = qk;
     g->bb = bb;
-    g->crb = (CHUNK_K / qk) * bb;
+    g->crb = is_i4g(type) ? i4g_hdr(type) + CHUNK_K / 2 : (CHUNK_K / qk) * bb;
     return true;
 }
 
@@ -105,6 +122,8 @@ inline bool make_tiled_shape(int type, int64_t N, int64_t K, TiledShape* s) {
 //         q3_lo_pos); plane B 128 x 14 B (scales[12], d)
 //   Q2_K  plane A 128 x 80 B (scales[16], qs[64]); plane B 128 x 4 B (dmin, d)
 //   Q6_K  plane A 128 x 192 B (ql, qh); plane B 128 x 16 B (scales); plane C 128 x 2 B (d)
+//   I4G   record H + 128 B: [(scale, zero) x 256/gs, padded to H = 16..64 B]
+//         [codes: 8 groups of 32 elements x 16 B, tiled code order]
 // ---------------------------------------------------------------------------
 struct Segment {
     int src, len;
@@ -145,6 +164,12 @@ __host__ __device__ inline int block_segments(int type, int r, int j, Segment* s
             s[1] = {192, 16, (int64_t)R * 192 + r * 16};
             s[2] = {208, 2, (int64_t)R * 208 + r * 2};
             return 3;
+        case T_I4G32: case T_I4G64: case T_I4G128: case T_I4G256: {
+            const int gs = i4g_gs(type), crb = i4g_hdr(type) + CHUNK_K / 2;
+            s[0] = {0, 8, (int64_t)r * crb + 8 * j};
+            s[1] = {8, gs / 2, (int64_t)r * crb + i4g_hdr(type) + (gs / 2) * j};
+            return 2;
+        }
         default:
             return 0;
     }
@@ -160,6 +185,7 @@ __host__ __device__ inline int block_segments(int type, int r, int j, Segment* s
 // Where the GGUF block holds element e of a group:
 //   Q4_0  byte e % 16, high nibble iff e >= 16   (gguf_importer.cpp:687-690)
 //   Q4_K  byte e / 2,  high nibble iff e is odd  (gguf_importer.cpp:864-868)
+//   I4G   byte e / 2,  high nibble iff e is odd  (quant/gptq.cpp:11-24)
 // ---------------------------------------------------------------------------
 __host__ __device__ inline void q4_code_pos(int e, int* byte, int* shift) {
     const int i = e & 7;
@@ -366,6 +392,18 @@ __device__ inline void decode8(int type, const uint8_t* chunk, int r, int e0, fl
                 int q = ((e & 1) ? (c >> 4) : (c & 15)) | (((rec[16 + (e >> 3)] >> (e & 7)) & 1) << 4);
                 out[i] = __fsub_rn(__fmul_rn(ds, (float)q), dm);
             }
+            break;
+        }
+        case T_I4G32: case T_I4G64: case T_I4G128: case T_I4G256: {  // quant/gptq.cpp:9-27
+            const uint8_t* rec = chunk + (int64_t)r * (i4g_hdr(type) + CHUNK_K / 2);
+            const int j = e0 / i4g_gs(type);
+            const float scale = __uint_as_float((uint32_t)rec[8 * j] | ((uint32_t)rec[8 * j + 1] << 8) |
+                                                ((uint32_t)rec[8 * j + 2] << 16) | ((uint32_t)rec[8 * j + 3] << 24));
+            const float zero = __uint_as_float((uint32_t)rec[8 * j + 4] | ((uint32_t)rec[8 * j + 5] << 8) |
+                                               ((uint32_t)rec[8 * j + 6] << 16) | ((uint32_t)rec[8 * j + 7] << 24));
+            const uint8_t* q = rec + i4g_hdr(type) + 16 * (e0 >> 5);
+            for (int i = 0; i < 8; ++i)
+                out[i] = __fmul_rn(__fsub_rn((float)q4_tiled_code(q, (e0 & 31) + i), zero), scale);
             break;
         }
         case T_Q6_K: {  // :924-954

@@ -30,8 +30,8 @@ __global__ void repack_kernel(const uint8_t* __restrict__ src, uint8_t* __restri
         const int ns = block_segments(s.type, (int)r, (int)j, seg);
         // Bytes [c0, c1) of the block are 4-bit codes stored in the tiled order;
         // Q3_K's first 96 bytes (hmask, qs) are regrouped (q3_tiled_byte).
-        const int c0 = s.type == T_Q4_0 ? 2 : s.type == T_Q4_K ? 16 : s.g.bb;
-        const int c1 = s.type == T_Q4_0 ? 18 : s.type == T_Q4_K ? 144 : s.g.bb;
+        const int c0 = s.type == T_Q4_0 ? 2 : s.type == T_Q4_K ? 16 : is_i4g(s.type) ? 8 : s.g.bb;
+        const int c1 = s.type == T_Q4_0 ? 18 : s.type == T_Q4_K ? 144 : is_i4g(s.type) ? s.g.bb : s.g.bb;
         for (int q = 0; q < ns; ++q)
             for (int t = lane; t < seg[q].len; t += 32) {
                 const int sb = seg[q].src + t;

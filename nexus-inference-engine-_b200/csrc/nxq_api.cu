@@ -198,6 +198,10 @@ const char* type_name(int type) {
         case T_Q4_K: return "Q4_K";
         case T_Q5_K: return "Q5_K";
         case T_Q6_K: return "Q6_K";
+        case T_I4G32: return "I4G32";
+        case T_I4G64: return "I4G64";
+        case T_I4G128: return "I4G128";
+        case T_I4G256: return "I4G256";
         default: return "?";
     }
 }

@@ -127,6 +127,27 @@ struct Lane<T_Q4_K> {
     }
 };
 
+// NXF INT4 groups of 128 (quant/gptq.cpp:9-27): record = [(scale, zero) x2 :
+// 16 B][codes x8 of 16 B]; the slice (elements 64t .. 64t+63) lies in block
+// t / 2.  Weights fl16(q * fl16(scale) + fl16(-(zero * scale))).
+template <>
+struct Lane<T_I4G128> {
+    static constexpr int kStage = TILE_ROWS * 144;
+    uint4 q0, q1;
+    __half2 s2[2], o2[2];
+    __device__ __forceinline__ void load(const uint8_t* st, int row, int t) {
+        const uint8_t* rec = st + row * 144;
+        const float2 sz = *reinterpret_cast<const float2*>(rec + 8 * (t >> 1));
+        q0 = *reinterpret_cast<const uint4*>(rec + 16 + 32 * t);
+        q1 = *reinterpret_cast<const uint4*>(rec + 32 + 32 * t);
+        s2[0] = s2[1] = __float2half2_rn(sz.x);
+        o2[0] = o2[1] = __float2half2_rn(-(sz.y * sz.x));
+    }
+    __device__ __forceinline__ void pairs(int m, uint32_t (&p)[4]) const {
+        dq::q4_word_pairs(word_of(m < 4 ? q0 : q1, m & 3), s2[m >> 2], o2[m >> 2], p);
+    }
+};
+
 // Q4_0 (gguf_importer.cpp:679-695): record = [d x8][codes x8 of 16 B]; the
 // slice is blocks 2t, 2t+1.
 template <>
@@ -890,7 +911,9 @@ int launch(const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st)
     return NXQ_OK;
 }
 
-bool type_ok(int type) { return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || type == T_Q3_K; }
+bool type_ok(int type) {
+    return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || type == T_Q3_K || type == T_I4G128;
+}
 
 int launch_items(int type, int mt, const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st) {
     const bool pair = n == 1 && it[0].w_up;
@@ -908,6 +931,7 @@ int launch_items(int type, int mt, const HostItem* it, int n, int x_dtype, int y
         NXQ_CASE(T_Q4_0)
         NXQ_CASE(T_Q8_0)
         NXQ_CASE(T_Q3_K)
+        NXQ_CASE(T_I4G128)
         default:
             return NXQ_ERR_UNSUPPORTED;
     }
@@ -929,6 +953,7 @@ int mma_init(int) {
     NXQ_ATTR(T_Q4_0)
     NXQ_ATTR(T_Q8_0)
     NXQ_ATTR(T_Q3_K)
+    NXQ_ATTR(T_I4G128)
 #undef NXQ_ATTR
     return NXQ_OK;
 }

@@ -21,7 +21,7 @@ __all__ = [
     "NxqError", "lib", "init", "shutdown", "Weight", "qmatmul", "qmatmul_host", "stream_sync",
     "kernel_name", "launch_count",
     "TYPES", "GEOMETRY", "F32", "F16", "BF16", "SPLIT_COL", "SPLIT_ROW", "declared_symbols",
-    "tp_unique_id", "tp_init", "tp_shutdown", "tp_qmatmul", "tp_allreduce_f32", "GGUF", "qmatmul_grouped", "qmatmul_swiglu", "qmatmul_residual", "rmsnorm_qmatmul",
+    "tp_unique_id", "tp_init", "tp_shutdown", "tp_qmatmul", "tp_allreduce_f32", "GGUF", "qmatmul_grouped", "qmatmul_swiglu", "qmatmul_residual", "rmsnorm_qmatmul", "int4_pack", "INT4_ROWS", "INT4_KMAJOR",
 ]
 
 LIB_PATH = Path(__file__).with_name("libnxq.so")
@@ -29,9 +29,12 @@ HEADER = Path(__file__).resolve().parents[2] / "include" / "nxq.h"
 
 # GGUF type ids (nexus/src/import/gguf_importer.h:28-57) and block geometry
 # (elements per block, bytes per block; gguf_importer.cpp:679-954).
-TYPES = {"Q4_0": 2, "Q4_1": 3, "Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14}
+TYPES = {"Q4_0": 2, "Q4_1": 3, "Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14,
+         "I4G32": 101, "I4G64": 102, "I4G128": 104, "I4G256": 108}
 GEOMETRY = {2: (32, 18), 3: (32, 20), 8: (32, 34), 10: (256, 84), 11: (256, 110), 12: (256, 144),
-            13: (256, 176), 14: (256, 210)}
+            13: (256, 176), 14: (256, 210), 101: (32, 24), 102: (64, 40), 104: (128, 72), 108: (256, 136)}
+# NXF INT4 group weights: array orders accepted by register_int4 / int4_pack.
+INT4_ROWS, INT4_KMAJOR = 0, 1
 F32, F16, BF16 = 0, 1, 2
 SPLIT_COL, SPLIT_ROW = 0, 1
 
@@ -65,6 +68,10 @@ _SIGS = {
     "nxq_shard_extract": [_c.c_void_p, _c.c_size_t, _c.c_int, _c.c_int64, _c.c_int64, _c.c_int,
                           _c.c_int, _c.c_int, _c.c_void_p, _c.c_size_t],
     "nxq_weight_release": [_c.c_void_p],
+    "nxq_int4_pack": [_c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_int64, _c.c_int, _c.c_int,
+                      _c.c_void_p, _c.c_size_t],
+    "nxq_weight_register_int4": [_c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_int64, _c.c_int, _c.c_int,
+                                 _c.POINTER(_c.c_void_p)],
     "nxq_weight_info": [_c.c_void_p, _c.POINTER(_c.c_int), _c.POINTER(_c.c_int64),
                         _c.POINTER(_c.c_int64), _c.POINTER(_c.c_size_t), _c.POINTER(_c.c_size_t)],
     "nxq_dequant": [_c.c_void_p, _c.c_void_p, _c.c_void_p],
@@ -203,6 +210,19 @@ class Weight:
         return cls(h.value, t, N, K)
 
     @classmethod
+    def register_int4(cls, codes: np.ndarray, scales: np.ndarray, zeros, N: int, K: int, group_size: int,
+                      layout: int = INT4_ROWS) -> "Weight":
+        """NXF INT4 group weights from their arrays (nxq_weight_register_int4)."""
+        codes = np.ascontiguousarray(codes, dtype=np.uint8)
+        scales = np.ascontiguousarray(scales, dtype=np.float32)
+        zp = None if zeros is None else np.ascontiguousarray(zeros, dtype=np.float32)
+        h = ctypes.c_void_p()
+        _check(lib().nxq_weight_register_int4(codes.ctypes.data, scales.ctypes.data,
+                                              None if zp is None else zp.ctypes.data, N, K, group_size, layout,
+                                              ctypes.byref(h)))
+        return cls(h.value, 100 + group_size // 32, N, K)
+
+    @classmethod
     def register_shard(cls, blocks, type_, N: int, K: int, split: int, rank: int, world: int) -> "Weight":
         t = cls._type_id(type_)
         buf = np.ascontiguousarray(np.frombuffer(memoryview(blocks).cast("B"), dtype=np.uint8))
@@ -255,6 +275,18 @@ def qmatmul(w: Weight, x, out=None, out_dtype=None, stream=None):
         out = torch.empty((M, w.N), dtype=out_dtype or torch.float32, device=x.device)
     _check(lib().nxq_qmatmul(w.handle, x.data_ptr(), _dtype_code(x.dtype), out.data_ptr(),
                              _dtype_code(out.dtype), M, _stream_ptr(stream)))
+    return out
+
+
+def int4_pack(codes: np.ndarray, scales: np.ndarray, zeros, N: int, K: int, group_size: int,
+              layout: int = INT4_ROWS) -> np.ndarray:
+    """NXF INT4 group arrays -> I4G blocks [N][K/gs] (host only, no GPU)."""
+    codes = np.ascontiguousarray(codes, dtype=np.uint8)
+    scales = np.ascontiguousarray(scales, dtype=np.float32)
+    zp = None if zeros is None else np.ascontiguousarray(zeros, dtype=np.float32)
+    out = np.zeros(N * (K // group_size) * (8 + group_size // 2), dtype=np.uint8)
+    _check(lib().nxq_int4_pack(codes.ctypes.data, scales.ctypes.data, None if zp is None else zp.ctypes.data, N, K,
+                               group_size, layout, out.ctypes.data, out.nbytes))
     return out
 
 

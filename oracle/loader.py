@@ -54,6 +54,9 @@ def port() -> ctypes.CDLL:
         L.nxqo_gemm_transb.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                        ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int]
         L.nxqo_gemm_transb.restype = None
+        L.nxqo_dequant_int4.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                        ctypes.c_int64, ctypes.c_int]
+        L.nxqo_dequant_int4.restype = None
         _port = L
     return _port
 
@@ -67,6 +70,9 @@ def ref() -> Optional[ctypes.CDLL]:
         L.ref_dequant.restype = ctypes.c_int
         L.ref_fp16_to_fp32.argtypes = [ctypes.c_uint16]
         L.ref_fp16_to_fp32.restype = ctypes.c_float
+        L.ref_dequant_int4.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                       ctypes.c_int, ctypes.c_int]
+        L.ref_dequant_int4.restype = None
         _ref = L
     return _ref
 
@@ -105,6 +111,26 @@ def qmatmul(type_id: int, blocks: np.ndarray, N: int, K: int, x: np.ndarray, whi
     if rc != 0:
         raise ValueError("oracle qmatmul failed")
     return y
+
+
+def dequant_int4(codes: np.ndarray, scales: np.ndarray, zeros, n: int, group_size: int,
+                 which: str = "port") -> np.ndarray:
+    """quant/gptq.cpp:9-27 over flat arrays: the oracle's restatement ("port")
+    or the reference's own compiled function ("ref")."""
+    codes = np.ascontiguousarray(codes, dtype=np.uint8)
+    scales = np.ascontiguousarray(scales, dtype=np.float32)
+    zp = None if zeros is None else np.ascontiguousarray(zeros, dtype=np.float32)
+    out = np.zeros(n, dtype=np.float32)
+    if which == "ref":
+        L = ref()
+        if L is None:
+            raise FileNotFoundError(REF_SO)
+        L.ref_dequant_int4(out.ctypes.data, codes.ctypes.data, scales.ctypes.data,
+                           None if zp is None else zp.ctypes.data, n, group_size)
+    else:
+        port().nxqo_dequant_int4(out.ctypes.data, codes.ctypes.data, scales.ctypes.data,
+                                 None if zp is None else zp.ctypes.data, ctypes.c_int64(n), group_size)
+    return out
 
 
 def same_bits(a: np.ndarray, b: np.ndarray) -> bool:

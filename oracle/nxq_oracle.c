@@ -47,6 +47,10 @@ int nxqo_block_shape(int type, int* elems, int* bytes) {
         case NXQO_Q2_K: e = 256; b = 84; break;
         case NXQO_Q3_K: e = 256; b = 110; break;
         case NXQO_Q4_K: e = 256; b = 144; break;
+        case NXQO_I4G32: case NXQO_I4G64: case NXQO_I4G128: case NXQO_I4G256:
+            e = 32 * (type - 100);
+            b = 8 + e / 2;
+            break;
         case NXQO_Q5_K: e = 256; b = 176; break;
         case NXQO_Q6_K: e = 256; b = 210; break;
         default: return 0;
@@ -187,6 +191,30 @@ static void blk_q6_k(const uint8_t* b, float* y) {
     }
 }
 
+/* quant/gptq.cpp:9-27: out[i] = ((float)q_i - zero) * scale, q_i nibble i of
+ * data (low nibble first), scale/zero of group i / group_size. */
+void nxqo_dequant_int4(float* out, const uint8_t* data, const float* scales, const float* zeros,
+                       int64_t n, int group_size) {
+    for (int64_t i = 0; i < n; ++i) {
+        const int64_t g = i / group_size;
+        const int q = (i & 1) ? (data[i >> 1] >> 4) & 15 : data[i >> 1] & 15;
+        const float zero = zeros ? zeros[g] : 0.0f;
+        out[i] = ((float)q - zero) * scales[g];
+    }
+}
+
+/* One NXF INT4 group block: [scale f32][zero f32][gs/2 code bytes]. */
+static void blk_i4g(const uint8_t* b, float* y, int gs) {
+    float scale, zero;
+    memcpy(&scale, b, 4);
+    memcpy(&zero, b + 4, 4);
+    nxqo_dequant_int4(y, b + 8, &scale, &zero, gs, gs);
+}
+static void blk_i4g32(const uint8_t* b, float* y) { blk_i4g(b, y, 32); }
+static void blk_i4g64(const uint8_t* b, float* y) { blk_i4g(b, y, 64); }
+static void blk_i4g128(const uint8_t* b, float* y) { blk_i4g(b, y, 128); }
+static void blk_i4g256(const uint8_t* b, float* y) { blk_i4g(b, y, 256); }
+
 typedef void (*blk_fn)(const uint8_t*, float*);
 
 static blk_fn block_decoder(int type) {
@@ -199,6 +227,10 @@ static blk_fn block_decoder(int type) {
         case NXQO_Q4_K: return blk_q4_k;
         case NXQO_Q5_K: return blk_q5_k;
         case NXQO_Q6_K: return blk_q6_k;
+        case NXQO_I4G32: return blk_i4g32;
+        case NXQO_I4G64: return blk_i4g64;
+        case NXQO_I4G128: return blk_i4g128;
+        case NXQO_I4G256: return blk_i4g256;
         default: return NULL;
     }
 }

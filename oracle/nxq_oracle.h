@@ -30,8 +30,17 @@ extern "C" {
 enum {
     NXQO_F32 = 0, NXQO_F16 = 1, NXQO_Q4_0 = 2, NXQO_Q4_1 = 3, NXQO_Q8_0 = 8,
     NXQO_Q2_K = 10, NXQO_Q3_K = 11, NXQO_Q4_K = 12, NXQO_Q5_K = 13,
-    NXQO_Q6_K = 14, NXQO_BF16 = 30
+    NXQO_Q6_K = 14, NXQO_BF16 = 30,
+    /* NXF INT4 groups of 32/64/128/256 as blocks [scale f32][zero f32][codes]
+     * (the library's NXQ_TYPE_I4G*; quant/gptq.cpp:9-27 per group) */
+    NXQO_I4G32 = 101, NXQO_I4G64 = 102, NXQO_I4G128 = 104, NXQO_I4G256 = 108
 };
+
+/* quant/gptq.cpp:9-27, dequant_int4, over flat arrays: element i is nibble i of
+ * data (low nibble first), out[i] = ((float)q - zero[g]) * scale[g] with
+ * g = i / group_size (zeros NULL: 0). */
+void nxqo_dequant_int4(float* out, const uint8_t* data, const float* scales, const float* zeros,
+                       int64_t n, int group_size);
 
 /* Elements per block and bytes per block for `type`; returns 0 if unknown. */
 int nxqo_block_shape(int type, int* elems, int* bytes);

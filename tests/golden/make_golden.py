@@ -20,6 +20,13 @@ Per block type golden_<TYPE>.npz holds
                                  in the benchmark distribution, x ~ N(0,1)
                                  rounded to fp16, and the reference CPU path's y;
                                  mat_w_sha256 hashes the decoded weight bytes.
+
+golden_I4G.npz (NXF INT4 groups, quant/gptq.cpp:9-27) holds, per group size
+gs in {32, 64, 128, 256}, flat known-answer arrays g<gs>_codes / _scales /
+_zeros (zero, negative, fp32-subnormal, huge, Inf and NaN scales; codes 0 and
+15; one set with zeros omitted, g<gs>_nozero_out) and the reference's
+nexus::quant::dequant_int4 output g<gs>_out, plus a ragged matrix in the
+I4G block form (g<gs>_mat_*) with the reference CPU path's y.
 """
 from __future__ import annotations
 
@@ -70,11 +77,49 @@ def kat_blocks(t: int, seed: int) -> np.ndarray:
     return np.concatenate(blocks)
 
 
+def make_i4g() -> None:
+    out = {}
+    for gs in (32, 64, 128, 256):
+        g = synth.rng(7100 + gs)
+        groups = 24
+        n = groups * gs
+        codes = g.integers(0, 256, n // 2, dtype=np.uint8)
+        codes[: gs // 2] = 0x00           # group 0: codes 0
+        codes[gs // 2: gs] = 0xFF         # group 1: codes 15
+        scales = g.uniform(-4.0, 4.0, groups).astype(np.float32)
+        zeros = g.uniform(-2.0, 17.0, groups).astype(np.float32)
+        special = np.array([0.0, -0.0, 1e-40, -3.0e38, 3.4e38, np.inf, -np.inf, np.nan, 1.0, -1.0],
+                           dtype=np.float32)
+        scales[2:2 + special.size] = special
+        zeros[12] = np.inf
+        zeros[13] = np.nan
+        zeros[14] = 0.0
+        out[f"g{gs}_codes"] = codes
+        out[f"g{gs}_scales"] = scales
+        out[f"g{gs}_zeros"] = zeros
+        out[f"g{gs}_out"] = loader.dequant_int4(codes, scales, zeros, n, gs, which="ref")
+        out[f"g{gs}_nozero_out"] = loader.dequant_int4(codes, scales, None, n, gs, which="ref")
+        t = 100 + gs // 32
+        N, K = 96, (768 if gs < 256 else 512)
+        mb = synth.make_blocks(t, N, K, seed=8100 + gs)
+        x = synth.make_activations(4, K, seed=9100 + gs, dtype=np.float16).astype(np.float32)
+        out[f"g{gs}_mat_blocks"] = mb
+        out[f"g{gs}_mat_N"] = np.int64(N)
+        out[f"g{gs}_mat_K"] = np.int64(K)
+        out[f"g{gs}_mat_x"] = x
+        out[f"g{gs}_mat_y"] = loader.qmatmul(t, mb, N, K, x, which="ref", nthreads=4)
+        print(f"I4G{gs}: kat {groups} groups; mat {N} x {K}")
+    np.savez_compressed(OUT / "golden_I4G.npz", **out)
+
+
 def main() -> int:
     loader.build(ref=True)
     if loader.ref() is None:
         print("reference decoders not built (oracle/_ref missing)", file=sys.stderr)
         return 2
+    if len(sys.argv) > 1 and sys.argv[1] == "i4g":
+        make_i4g()
+        return 0
     for t, name in NAMES.items():
         qk, bb = synth.GEOMETRY[t]
         kb = kat_blocks(t, 7000 + t)
@@ -93,6 +138,7 @@ def main() -> int:
             mat_w_sha256=np.array(hashlib.sha256(w.tobytes()).hexdigest()),
         )
         print(name, "kat", kb.size // bb, "blocks; mat", N, "x", K)
+    make_i4g()
     return 0
 
 
