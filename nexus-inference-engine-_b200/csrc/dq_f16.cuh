@@ -188,5 +188,55 @@ struct Group<T_Q3_K> {
     }
 };
 
+// Pair K (0..3) of a Q6_K L word (formats.cuh, q6_lo_bit / q6_hi_bit): for
+// K = 0, 1 the low nibbles sit at bits 4K (+16) of `l` and the high bits two
+// above them in `h` (= H rotated by 2 (w % 2)); K = 2, 3 use l >> 8 and H
+// rotated by 8 + 2 (w % 2).  The 6-bit code lands in the mantissa of 1024
+// (K even) or 64 (K odd); subtracting magic + 32 leaves q - 32 exactly; times
+// s = fl16(d * sc).
+template <int K>
+__device__ __forceinline__ uint32_t q6_pair(uint32_t l, uint32_t h, __half2 s2) {
+    constexpr int KK = K & 1;
+    constexpr uint32_t MG = KK ? 0x54005400u : 0x64006400u;  // 64, 1024
+    constexpr uint32_t BI = KK ? 0x56005600u : 0x64206420u;  // 96, 1056
+    const uint32_t v = or_and(and_or(l, 0x000F000Fu << (4 * KK), MG), h, 0x00300030u << (4 * KK));
+    return h2u(__hmul2(__hsub2(u2h(v), u2h(BI)), s2));
+}
+
+// The four pairs of L word `l` (elements 8w .. 8w+7 of its group) whose high
+// bits are in `h`, with o = 2 (w % 2).
+template <int O>
+__device__ __forceinline__ void q6_word_pairs(uint32_t l, uint32_t h, __half2 s2, uint32_t* o) {
+    const uint32_t h0 = O ? __funnelshift_r(h, h, O) : h;
+    const uint32_t h1 = __funnelshift_r(h, h, 8 + O);
+    const uint32_t l8 = l >> 8;
+    o[0] = q6_pair<0>(l, h0, s2);
+    o[1] = q6_pair<1>(l, h0, s2);
+    o[2] = q6_pair<2>(l8, h1, s2);
+    o[3] = q6_pair<3>(l8, h1, s2);
+}
+
+// Q6_K (gguf_importer.cpp:924-954): plane A = 8 x [L0 L1 L2 L3 H0 H1] (tiled
+// code order) at r*192, plane B = 16 int8 scales at 128*192 + r*16, plane C =
+// d at 128*208 + r*2; group G = elements 32G..32G+31, scales 2G and 2G+1.
+template <>
+struct Group<T_Q6_K> {
+    static constexpr int kStage = TILE_ROWS * 210;
+    template <int G>
+    __device__ __forceinline__ static void decode(const uint8_t* stage, int r, uint32_t (&o)[16]) {
+        const uint8_t* rec = stage + r * 192 + 24 * G;
+        const int8_t* sc = reinterpret_cast<const int8_t*>(stage + TILE_ROWS * 192 + r * 16 + 2 * G);
+        const float d = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(stage + TILE_ROWS * 208 + r * 2)));
+        const __half2 sa = __float2half2_rn(d * (float)sc[0]), sb = __float2half2_rn(d * (float)sc[1]);
+        const uint2 a = *reinterpret_cast<const uint2*>(rec);
+        const uint2 b = *reinterpret_cast<const uint2*>(rec + 8);
+        const uint2 c = *reinterpret_cast<const uint2*>(rec + 16);
+        q6_word_pairs<0>(a.x, c.x, sa, &o[0]);
+        q6_word_pairs<2>(a.y, c.x, sa, &o[4]);
+        q6_word_pairs<0>(b.x, c.y, sb, &o[8]);
+        q6_word_pairs<2>(b.y, c.y, sb, &o[12]);
+    }
+};
+
 }  // namespace dq
 }  // namespace nxq

@@ -121,7 +121,8 @@ inline bool make_tiled_shape(int type, int64_t N, int64_t K, TiledShape* s) {
 //   Q3_K  plane A 128 x 96 B (hmask + qs regrouped: 8 x [L0 L1 H], see
 //         q3_lo_pos); plane B 128 x 14 B (scales[12], d)
 //   Q2_K  plane A 128 x 80 B (scales[16], qs[64]); plane B 128 x 4 B (dmin, d)
-//   Q6_K  plane A 128 x 192 B (ql, qh); plane B 128 x 16 B (scales); plane C 128 x 2 B (d)
+//   Q6_K  plane A 128 x 192 B (ql, qh regrouped: 8 x [L0 L1 L2 L3 H0 H1], see
+//         q6_lo_bit); plane B 128 x 16 B (scales); plane C 128 x 2 B (d)
 //   I4G   record H + 128 B: [(scale, zero) x 256/gs, padded to H = 16..64 B]
 //         [codes: 8 groups of 32 elements x 16 B, tiled code order]
 // ---------------------------------------------------------------------------
@@ -261,6 +262,59 @@ __device__ __forceinline__ int q3_tiled_code(const uint8_t* rec, int e) {
     const uint32_t lo = (w[e32 >> 4] >> q3_lo_pos(e32 & 15)) & 3u;
     const uint32_t hb = (w[2] >> q3_hi_pos(e32)) & 1u;
     return (int)(lo | (hb << 2));
+}
+
+// ---------------------------------------------------------------------------
+// Q6_K code order in the tiled copy.  Each 32-element group becomes six 32-bit
+// words [L0 L1 L2 L3][H0 H1], the 24 bytes the block spends on it (16 of ql,
+// 8 of qh).  L_w holds the low 4 bits of elements 8w..8w+7 in the 4-bit order
+// of Q4_0 / Q4_K: element 8w+i at bit 4k + 16s (k = i/2, s = i%2).  H_{w/2}
+// holds their high 2 bits at bit ((4 + 4k + 16s) mod 32) + 2 (w % 2): right
+// above the low nibble of pairs k = 0, 1 (after a rotate by 2 (w % 2)) and of
+// pairs k = 2, 3 of L_w >> 8 (after a rotate by 8 + 2 (w % 2)).  So a pair is
+// (L & mask | magic) | (H' & mask') with magic 1024 (k even) or 64 (k odd).
+// Where the block holds element j (NEXUS Q6_K, gguf_importer.cpp:924-954):
+//   low 4 bits  (ql[j/2] >> 4(j%2)) & 15     (ql at block offset 0)
+//   high 2 bits (qh[j/4] >> 2(j%4)) & 3      (qh at block offset 128)
+// ---------------------------------------------------------------------------
+__host__ __device__ inline int q6_lo_bit(int e32) {
+    const int i = e32 & 7;
+    return 4 * (i >> 1) + 16 * (i & 1);
+}
+__host__ __device__ inline int q6_hi_bit(int e32) {
+    const int i = e32 & 7;
+    return ((4 + 4 * (i >> 1) + 16 * (i & 1)) & 31) + 2 * ((e32 >> 3) & 1);
+}
+
+// Byte `ob` (0..191) of the tiled Q6_K plane-A record of one block.
+__host__ __device__ inline uint8_t q6_tiled_byte(const uint8_t* blk, int ob) {
+    const int G = ob / 24, wb = ob % 24, word = wb >> 2;
+    uint32_t v = 0;
+    for (int bit = 0; bit < 8; ++bit) {
+        const int p = 8 * (wb & 3) + bit;
+        uint32_t b;
+        if (word < 4) {  // p = 4k + 16s + f: bit f of the low nibble of element 8 word + 2k + s
+            const int s = p >> 4, k = (p & 15) >> 2, f = p & 3;
+            const int j = 32 * G + 8 * word + 2 * k + s;
+            b = (blk[j >> 1] >> (4 * (j & 1) + f)) & 1u;
+        } else {  // p = ((4 + 4k + 16s) mod 32) + 2h + f: bit f of the high bits of L word 2 (word - 4) + h
+            const int f = p & 1, h = (p >> 1) & 1;
+            const int u = (p - 2 * h - f - 4) & 31;
+            const int k = (u >> 2) & 3, s = u >> 4;
+            const int j = 32 * G + 8 * (2 * (word - 4) + h) + 2 * k + s;
+            b = (blk[128 + (j >> 2)] >> (2 * (j & 3) + f)) & 1u;
+        }
+        v |= b << bit;
+    }
+    return (uint8_t)v;
+}
+
+__device__ __forceinline__ int q6_tiled_code(const uint8_t* rec, int e) {
+    const int G = e >> 5, e32 = e & 31;
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(rec + 24 * G);
+    const uint32_t lo = (w[e32 >> 3] >> q6_lo_bit(e32)) & 15u;
+    const uint32_t hi = (w[4 + (e32 >> 4)] >> q6_hi_bit(e32)) & 3u;
+    return (int)(lo | (hi << 4));
 }
 
 __device__ __forceinline__ int q4_tiled_code(const uint8_t* g, int e) {
@@ -411,12 +465,7 @@ __device__ inline void decode8(int type, const uint8_t* chunk, int r, int e0, fl
             const int8_t* scl = (const int8_t*)(chunk + (int64_t)R * 192 + r * 16);
             float d = half_bits_to_float(rd16(chunk + (int64_t)R * 208 + r * 2));
             float ds = __fmul_rn(d, (float)scl[e0 >> 4]);
-            for (int i = 0; i < 8; ++i) {
-                int e = e0 + i;
-                int lo = (e & 1) ? (rec[e >> 1] >> 4) : (rec[e >> 1] & 15);
-                int hi = (rec[128 + (e >> 2)] >> (2 * (e & 3))) & 3;
-                out[i] = __fmul_rn(ds, __fsub_rn((float)(lo | (hi << 4)), 32.0f));
-            }
+            for (int i = 0; i < 8; ++i) out[i] = __fmul_rn(ds, __fsub_rn((float)q6_tiled_code(rec, e0 + i), 32.0f));
             break;
         }
         default:

@@ -127,6 +127,37 @@ struct Lane<T_Q4_K> {
     }
 };
 
+// Q6_K (gguf_importer.cpp:924-954): plane A = 8 x [L0 L1 L2 L3 H0 H1] per row
+// (formats.cuh, q6_lo_bit); the slice (elements 64t .. 64t+63) is groups 2t,
+// 2t+1 = 48 bytes at r*192 + 48t, with scales 4t .. 4t+3 (16 elements each)
+// and d.  Weights fl16((q - 32) * fl16(d * sc)).
+template <>
+struct Lane<T_Q6_K> {
+    static constexpr int kStage = TILE_ROWS * 210;
+    uint32_t L[8], H[4];
+    __half2 s2[4];
+    __device__ __forceinline__ void load(const uint8_t* st, int row, int t) {
+        const uint4* rec = reinterpret_cast<const uint4*>(st + row * 192 + 48 * t);
+        const uint4 a = rec[0], b = rec[1], c = rec[2];
+        L[0] = a.x; L[1] = a.y; L[2] = a.z; L[3] = a.w;
+        H[0] = b.x; H[1] = b.y;
+        L[4] = b.z; L[5] = b.w; L[6] = c.x; L[7] = c.y;
+        H[2] = c.z; H[3] = c.w;
+        const uint32_t sc = *reinterpret_cast<const uint32_t*>(st + TILE_ROWS * 192 + row * 16 + 4 * t);
+        const float d = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(st + TILE_ROWS * 208 + row * 2)));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s2[i] = __float2half2_rn(d * (float)(int8_t)(sc >> (8 * i)));
+    }
+    // Elements 8m .. 8m+7 of the slice: group m >> 2, L word m & 3, scale m >> 1.
+    __device__ __forceinline__ void pairs(int m, uint32_t (&p)[4]) const {
+        const int g = m >> 2, wl = m & 3;
+        if (wl & 1)
+            dq::q6_word_pairs<2>(L[4 * g + wl], H[2 * g + (wl >> 1)], s2[m >> 1], p);
+        else
+            dq::q6_word_pairs<0>(L[4 * g + wl], H[2 * g + (wl >> 1)], s2[m >> 1], p);
+    }
+};
+
 // NXF INT4 groups of 128 (quant/gptq.cpp:9-27): record = [(scale, zero) x2 :
 // 16 B][codes x8 of 16 B]; the slice (elements 64t .. 64t+63) lies in block
 // t / 2.  Weights fl16(q * fl16(scale) + fl16(-(zero * scale))).
@@ -912,7 +943,7 @@ int launch(const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st)
 }
 
 bool type_ok(int type) {
-    return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || type == T_Q3_K || type == T_I4G128;
+    return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || type == T_Q3_K || type == T_I4G128 || type == T_Q6_K;
 }
 
 int launch_items(int type, int mt, const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st) {
@@ -932,6 +963,7 @@ int launch_items(int type, int mt, const HostItem* it, int n, int x_dtype, int y
         NXQ_CASE(T_Q8_0)
         NXQ_CASE(T_Q3_K)
         NXQ_CASE(T_I4G128)
+        NXQ_CASE(T_Q6_K)
         default:
             return NXQ_ERR_UNSUPPORTED;
     }
@@ -954,6 +986,7 @@ int mma_init(int) {
     NXQ_ATTR(T_Q8_0)
     NXQ_ATTR(T_Q3_K)
     NXQ_ATTR(T_I4G128)
+    NXQ_ATTR(T_Q6_K)
 #undef NXQ_ATTR
     return NXQ_OK;
 }

@@ -275,3 +275,17 @@ def test_qmm_small_batch_fp32_bf16_activations(gpu, t, x_dt):
         assert synth.rel_l2(y3.cpu().numpy(), want) < TOL
     finally:
         w.release()
+
+
+def test_q6k_runs_on_the_tensor_core_kernels(gpu):
+    """Q6_K (the high-precision tensors of Q4_K_M / Q5_K_M files) decodes on the
+    mma.sync GEMV and multiplies on the tcgen05 GEMM, like the config types."""
+    t = 14
+    blocks = synth.make_blocks(t, 256, 1024, seed=3)
+    w = gpu.Weight.register(blocks, t, 256, 1024)
+    try:
+        for M, name in ((1, "mma_gemv<Q6_K,m8>"), (16, "mma_gemv<Q6_K,m16>"), (32, "mma_gemv<Q6_K,m32>"),
+                        (33, "tc_gemm<Q6_K,n256>")):
+            assert gpu.kernel_name(w, M) == name
+    finally:
+        w.release()
