@@ -216,6 +216,56 @@ __device__ __forceinline__ void q6_word_pairs(uint32_t l, uint32_t h, __half2 s2
     o[3] = q6_pair<3>(l8, h1, s2);
 }
 
+// Pair K (0..3) of a Q5_K L word (formats.cuh, q5_hi_bit): as q6_pair with one
+// high bit (mask 0x10 << 4(K&1)); the 5-bit code q lands in the mantissa of
+// 1024 or 64, and fl16(q * s + o) follows as for Q4_K.
+template <int K>
+__device__ __forceinline__ uint32_t q5_pair(uint32_t l, uint32_t h, __half2 s2, __half2 o2) {
+    constexpr int KK = K & 1;
+    constexpr uint32_t MG = KK ? 0x54005400u : 0x64006400u;  // 64, 1024
+    const uint32_t v = or_and(and_or(l, 0x000F000Fu << (4 * KK), MG), h, 0x00100010u << (4 * KK));
+    return h2u(__hfma2(__hsub2(u2h(v), u2h(MG)), s2, o2));
+}
+
+// The four pairs of L word w (elements 8w .. 8w+7 of its group); h is the
+// group's high-bit word.
+template <int W>
+__device__ __forceinline__ void q5_word_pairs(uint32_t l, uint32_t h, __half2 s2, __half2 o2, uint32_t* o) {
+    const uint32_t h0 = W ? __funnelshift_r(h, h, W) : h;
+    const uint32_t h1 = __funnelshift_r(h, h, 8 + W);
+    const uint32_t l8 = l >> 8;
+    o[0] = q5_pair<0>(l, h0, s2, o2);
+    o[1] = q5_pair<1>(l, h0, s2, o2);
+    o[2] = q5_pair<2>(l8, h1, s2, o2);
+    o[3] = q5_pair<3>(l8, h1, s2, o2);
+}
+
+// Q5_K (gguf_importer.cpp:878-915): record = [d, dmin, scales[12]][L words of 8
+// groups][H word of 8 groups] (tiled code order); group G = sub-block G.
+template <>
+struct Group<T_Q5_K> {
+    static constexpr int kStage = TILE_ROWS * 176;
+    template <int G>
+    __device__ __forceinline__ static void decode(const uint8_t* stage, int r, uint32_t (&o)[16]) {
+        const uint8_t* rec = stage + r * 176;
+        const uint4 hd = *reinterpret_cast<const uint4*>(rec);
+        const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFFu)));
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
+        const uint32_t sb = ((G < 4 ? hd.y : hd.z) >> (8 * (G & 3))) & 0xFFu;
+        const uint32_t eb = (hd.w >> (8 * (G & 3))) & 0xFFu;
+        const int S = (int)(sb & 63u);
+        const int Mn = (int)((sb >> 6) | ((G < 4 ? (eb & 15u) : (eb >> 4)) << 2));
+        const __half2 s2 = __float2half2_rn(d * (float)S);
+        const __half2 o2 = __float2half2_rn(-(dmin * (float)Mn));
+        const uint4 q = *reinterpret_cast<const uint4*>(rec + 16 + 16 * G);
+        const uint32_t h = *reinterpret_cast<const uint32_t*>(rec + 144 + 4 * G);
+        q5_word_pairs<0>(q.x, h, s2, o2, &o[0]);
+        q5_word_pairs<1>(q.y, h, s2, o2, &o[4]);
+        q5_word_pairs<2>(q.z, h, s2, o2, &o[8]);
+        q5_word_pairs<3>(q.w, h, s2, o2, &o[12]);
+    }
+};
+
 // Q6_K (gguf_importer.cpp:924-954): plane A = 8 x [L0 L1 L2 L3 H0 H1] (tiled
 // code order) at r*192, plane B = 16 int8 scales at 128*192 + r*16, plane C =
 // d at 128*208 + r*2; group G = elements 32G..32G+31, scales 2G and 2G+1.

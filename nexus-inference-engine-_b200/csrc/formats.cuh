@@ -117,7 +117,8 @@ inline bool make_tiled_shape(int type, int64_t N, int64_t K, TiledShape* s) {
 //   Q8_0  record 272 B: [d x8 : 16 B][codes x8 : 8 x 32 B]
 //   Q4_K  record 144 B: the block itself (d, dmin, scales[12], qs[128]), qs in
 //         tiled code order
-//   Q5_K  record 176 B: the block itself
+//   Q5_K  record 176 B: [d, dmin, scales[12]][low nibbles: 8 groups x 16 B,
+//         tiled code order][high bits: 8 groups x 4 B, see q5_hi_bit]
 //   Q3_K  plane A 128 x 96 B (hmask + qs regrouped: 8 x [L0 L1 H], see
 //         q3_lo_pos); plane B 128 x 14 B (scales[12], d)
 //   Q2_K  plane A 128 x 80 B (scales[16], qs[64]); plane B 128 x 4 B (dmin, d)
@@ -309,6 +310,51 @@ __host__ __device__ inline uint8_t q6_tiled_byte(const uint8_t* blk, int ob) {
     return (uint8_t)v;
 }
 
+// ---------------------------------------------------------------------------
+// Q5_K code order in the tiled copy.  After the 16-byte header, group G keeps
+// its low nibbles as four 32-bit words L_w at 16 + 16G (the 4-bit order,
+// element 8w+i at bit 4k + 16s) and its 32 high bits as one word H at 144 +
+// 4G, element 8w+i at bit ((4 + 4k + 16s) mod 32) + w: rotated by w (pairs
+// k = 0, 1 of L_w) or 8 + w (pairs 2, 3 of L_w >> 8) each high bit sits right
+// above its nibble, so a pair is (L & mask | magic) | (H' & mask').
+// Where the block holds element j (gguf_importer.cpp:878-915):
+//   low 4 bits  (qs[j/2] >> 4(j%2)) & 15     (qs at block offset 48)
+//   high bit    (qh[j/8] >> (j%8)) & 1       (qh at block offset 16)
+// ---------------------------------------------------------------------------
+__host__ __device__ inline int q5_hi_bit(int e32) {
+    const int i = e32 & 7;
+    return ((4 + 4 * (i >> 1) + 16 * (i & 1)) & 31) + (e32 >> 3);
+}
+
+// Byte `ob` (0..159) of the tiled Q5_K code planes (record offset 16 + ob).
+__host__ __device__ inline uint8_t q5_tiled_byte(const uint8_t* blk, int ob) {
+    uint32_t v = 0;
+    if (ob < 128) {  // low nibbles: bit p = 4k + 16s + f of word (ob % 16) / 4 of group ob / 16
+        const int G = ob >> 4, wb = ob & 15, word = wb >> 2;
+        for (int bit = 0; bit < 8; ++bit) {
+            const int p = 8 * (wb & 3) + bit, s = p >> 4, k = (p & 15) >> 2, f = p & 3;
+            const int j = 32 * G + 8 * word + 2 * k + s;
+            v |= (uint32_t)((blk[48 + (j >> 1)] >> (4 * (j & 1) + f)) & 1) << bit;
+        }
+    } else {  // high bits: bit p = ((4 + 4k + 16s) mod 32) + w of group (ob - 128) / 4
+        const int G = (ob - 128) >> 2, wb = (ob - 128) & 3;
+        for (int bit = 0; bit < 8; ++bit) {
+            const int p = 8 * wb + bit, w = p & 3, u = (p - w - 4) & 31;
+            const int j = 32 * G + 8 * w + 2 * ((u >> 2) & 3) + (u >> 4);
+            v |= (uint32_t)((blk[16 + (j >> 3)] >> (j & 7)) & 1) << bit;
+        }
+    }
+    return (uint8_t)v;
+}
+
+// Code of element e (0..255) of a tiled Q5_K record.
+__device__ __forceinline__ int q5_tiled_code(const uint8_t* rec, int e) {
+    const int G = e >> 5, e32 = e & 31;
+    const uint32_t l = *reinterpret_cast<const uint32_t*>(rec + 16 + 16 * G + 4 * (e32 >> 3));
+    const uint32_t h = *reinterpret_cast<const uint32_t*>(rec + 144 + 4 * G);
+    return (int)(((l >> q6_lo_bit(e32)) & 15u) | (((h >> q5_hi_bit(e32)) & 1u) << 4));
+}
+
 __device__ __forceinline__ int q6_tiled_code(const uint8_t* rec, int e) {
     const int G = e >> 5, e32 = e & 31;
     const uint32_t* w = reinterpret_cast<const uint32_t*>(rec + 24 * G);
@@ -440,12 +486,7 @@ __device__ inline void decode8(int type, const uint8_t* chunk, int r, int e0, fl
             kquant_scale_min(rec + 4, e0 >> 5, &s, &m);
             float ds = __fmul_rn(d, (float)s);
             float dm = __fmul_rn(dmin, (float)m);
-            for (int i = 0; i < 8; ++i) {
-                int e = e0 + i;
-                int c = rec[48 + (e >> 1)];
-                int q = ((e & 1) ? (c >> 4) : (c & 15)) | (((rec[16 + (e >> 3)] >> (e & 7)) & 1) << 4);
-                out[i] = __fsub_rn(__fmul_rn(ds, (float)q), dm);
-            }
+            for (int i = 0; i < 8; ++i) out[i] = __fsub_rn(__fmul_rn(ds, (float)q5_tiled_code(rec, e0 + i)), dm);
             break;
         }
         case T_I4G32: case T_I4G64: case T_I4G128: case T_I4G256: {  // quant/gptq.cpp:9-27

@@ -371,7 +371,8 @@ int launch(const Weight* w, const CUtensorMap& tmap, void* y, int y_dtype, int64
 }
 
 bool type_ok(int type) {
-    return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || type == T_Q3_K || type == T_I4G128 || type == T_Q6_K;
+    return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || type == T_Q3_K || type == T_I4G128 || type == T_Q6_K ||
+           type == T_Q5_K;
 }
 
 }  // namespace
@@ -389,7 +390,8 @@ int gemm_init(int) {
     g_encode = reinterpret_cast<EncodeTiledFn>(fn);
     int rc;
     if ((rc = set_attr<T_Q4_K>()) || (rc = set_attr<T_Q4_0>()) || (rc = set_attr<T_Q8_0>()) ||
-        (rc = set_attr<T_Q3_K>()) || (rc = set_attr<T_I4G128>()) || (rc = set_attr<T_Q6_K>()))
+        (rc = set_attr<T_Q3_K>()) || (rc = set_attr<T_I4G128>()) || (rc = set_attr<T_Q6_K>()) ||
+        (rc = set_attr<T_Q5_K>()))
         return rc;
     return NXQ_OK;
 }
@@ -431,6 +433,7 @@ int gemm_qmatmul(const Weight* w, const void* x, int x_dtype, void* y, int y_dty
         case T_Q3_K: return launch<T_Q3_K>(w, tmap, y, y_dtype, M, st);
         case T_I4G128: return launch<T_I4G128>(w, tmap, y, y_dtype, M, st);
         case T_Q6_K: return launch<T_Q6_K>(w, tmap, y, y_dtype, M, st);
+        case T_Q5_K: return launch<T_Q5_K>(w, tmap, y, y_dtype, M, st);
         default: return NXQ_ERR_UNSUPPORTED;
     }
 }

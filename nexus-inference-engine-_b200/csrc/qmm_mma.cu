@@ -93,6 +93,26 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
 template <int TYPE>
 struct Lane;
 
+// Q4_K / Q5_K header hd = (d, dmin, scales[12]): the f16 scale and offset
+// pairs of sub-blocks 2t, 2t+1.  Scale bytes 2t, 2t+1 hold the 6-bit scale
+// and the low 2 bits of the min, nibbles of bytes 8 + 2(t&1) + {0,1} the high
+// 4 bits of the min.  (scale, min) pairs become exact f16 integers by the
+// magic number; one f16 multiply by (d, d) / (-dmin, -dmin) then rounds d*sc
+// and -dmin*m once each, as fp32 math followed by one rounding would.
+__device__ __forceinline__ void kquant_lane_scales(const uint4& hd, int t, __half2 (&s2)[2], __half2 (&o2)[2]) {
+    const uint32_t v = __byte_perm(((t < 2 ? hd.y : hd.z) >> (16 * (t & 1))), 0u, 0x4140u);
+    const uint32_t e = __byte_perm(((hd.w >> (16 * (t & 1))) >> (4 * (t >> 1))), 0u, 0x4140u);
+    const __half2 magic = u2h(0x64006400u);
+    const __half2 sc = __hsub2(u2h((v & 0x003F003Fu) | 0x64006400u), magic);
+    const __half2 mn = __hsub2(u2h(((v >> 6) & 0x00030003u) | ((e & 0x000F000Fu) << 2) | 0x64006400u), magic);
+    const uint32_t sp = h2u(__hmul2(sc, u2h(__byte_perm(hd.x, 0u, 0x1010u))));
+    const uint32_t op = h2u(__hmul2(mn, u2h(__byte_perm(hd.x, 0u, 0x3232u) ^ 0x80008000u)));
+    s2[0] = u2h(__byte_perm(sp, 0u, 0x1010u));
+    s2[1] = u2h(__byte_perm(sp, 0u, 0x3232u));
+    o2[0] = u2h(__byte_perm(op, 0u, 0x1010u));
+    o2[1] = u2h(__byte_perm(op, 0u, 0x3232u));
+}
+
 // Q4_K (gguf_importer.cpp:838-873): record = block (d, dmin, scales[12], qs[128]);
 // the slice is sub-blocks 2t, 2t+1 = code bytes 32t .. 32t+31.
 template <>
@@ -105,25 +125,38 @@ struct Lane<T_Q4_K> {
         const uint4 hd = *reinterpret_cast<const uint4*>(rec);
         q0 = *reinterpret_cast<const uint4*>(rec + 16 + 32 * t);
         q1 = *reinterpret_cast<const uint4*>(rec + 32 + 32 * t);
-        // Sub-blocks 2t, 2t+1: scale bytes 2t, 2t+1 (6-bit scale, low 2 bits of
-        // the min) and nibbles of bytes 8 + 2(t&1) + {0,1} (high 4 bits of the
-        // min).  (scale, min) pairs become exact f16 integers by the magic
-        // number; one f16 multiply by (d, d) / (-dmin, -dmin) then rounds
-        // d*sc and -dmin*m once each, as fp32 math followed by one rounding would.
-        const uint32_t v = __byte_perm(((t < 2 ? hd.y : hd.z) >> (16 * (t & 1))), 0u, 0x4140u);
-        const uint32_t e = __byte_perm(((hd.w >> (16 * (t & 1))) >> (4 * (t >> 1))), 0u, 0x4140u);
-        const __half2 magic = u2h(0x64006400u);
-        const __half2 sc = __hsub2(u2h((v & 0x003F003Fu) | 0x64006400u), magic);
-        const __half2 mn = __hsub2(u2h(((v >> 6) & 0x00030003u) | ((e & 0x000F000Fu) << 2) | 0x64006400u), magic);
-        const uint32_t sp = h2u(__hmul2(sc, u2h(__byte_perm(hd.x, 0u, 0x1010u))));
-        const uint32_t op = h2u(__hmul2(mn, u2h(__byte_perm(hd.x, 0u, 0x3232u) ^ 0x80008000u)));
-        s2[0] = u2h(__byte_perm(sp, 0u, 0x1010u));
-        s2[1] = u2h(__byte_perm(sp, 0u, 0x3232u));
-        o2[0] = u2h(__byte_perm(op, 0u, 0x1010u));
-        o2[1] = u2h(__byte_perm(op, 0u, 0x3232u));
+        kquant_lane_scales(hd, t, s2, o2);
     }
     __device__ __forceinline__ void pairs(int m, uint32_t (&p)[4]) const {
         dq::q4_word_pairs(word_of(m < 4 ? q0 : q1, m & 3), s2[m >> 2], o2[m >> 2], p);
+    }
+};
+
+// Q5_K (gguf_importer.cpp:878-915): record = [d, dmin, scales[12]][L words of
+// 8 groups][H words] (formats.cuh, q5_hi_bit); the slice is sub-blocks 2t,
+// 2t+1: L words at 16 + 32t, H words at 144 + 8t.
+template <>
+struct Lane<T_Q5_K> {
+    static constexpr int kStage = TILE_ROWS * 176;
+    uint4 q0, q1;
+    uint2 hh;
+    __half2 s2[2], o2[2];
+    __device__ __forceinline__ void load(const uint8_t* st, int row, int t) {
+        const uint8_t* rec = st + row * 176;
+        const uint4 hd = *reinterpret_cast<const uint4*>(rec);
+        q0 = *reinterpret_cast<const uint4*>(rec + 16 + 32 * t);
+        q1 = *reinterpret_cast<const uint4*>(rec + 32 + 32 * t);
+        hh = *reinterpret_cast<const uint2*>(rec + 144 + 8 * t);
+        kquant_lane_scales(hd, t, s2, o2);
+    }
+    __device__ __forceinline__ void pairs(int m, uint32_t (&p)[4]) const {
+        const uint32_t l = word_of(m < 4 ? q0 : q1, m & 3), h = m < 4 ? hh.x : hh.y;
+        switch (m & 3) {
+            case 0: dq::q5_word_pairs<0>(l, h, s2[m >> 2], o2[m >> 2], p); break;
+            case 1: dq::q5_word_pairs<1>(l, h, s2[m >> 2], o2[m >> 2], p); break;
+            case 2: dq::q5_word_pairs<2>(l, h, s2[m >> 2], o2[m >> 2], p); break;
+            default: dq::q5_word_pairs<3>(l, h, s2[m >> 2], o2[m >> 2], p); break;
+        }
     }
 };
 
@@ -943,7 +976,8 @@ int launch(const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st)
 }
 
 bool type_ok(int type) {
-    return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || type == T_Q3_K || type == T_I4G128 || type == T_Q6_K;
+    return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || type == T_Q3_K || type == T_I4G128 || type == T_Q6_K ||
+           type == T_Q5_K;
 }
 
 int launch_items(int type, int mt, const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st) {
@@ -964,6 +998,7 @@ int launch_items(int type, int mt, const HostItem* it, int n, int x_dtype, int y
         NXQ_CASE(T_Q3_K)
         NXQ_CASE(T_I4G128)
         NXQ_CASE(T_Q6_K)
+        NXQ_CASE(T_Q5_K)
         default:
             return NXQ_ERR_UNSUPPORTED;
     }
@@ -987,6 +1022,7 @@ int mma_init(int) {
     NXQ_ATTR(T_Q3_K)
     NXQ_ATTR(T_I4G128)
     NXQ_ATTR(T_Q6_K)
+    NXQ_ATTR(T_Q5_K)
 #undef NXQ_ATTR
     return NXQ_OK;
 }

@@ -277,15 +277,17 @@ def test_qmm_small_batch_fp32_bf16_activations(gpu, t, x_dt):
         w.release()
 
 
-def test_q6k_runs_on_the_tensor_core_kernels(gpu):
-    """Q6_K (the high-precision tensors of Q4_K_M / Q5_K_M files) decodes on the
-    mma.sync GEMV and multiplies on the tcgen05 GEMM, like the config types."""
-    t = 14
+@pytest.mark.parametrize("t", [13, 14], ids=lambda t: NAMES[t])
+def test_q5k_q6k_run_on_the_tensor_core_kernels(gpu, t):
+    """Q5_K and Q6_K (the tensors of Q5_K_M files, and the high-precision ones of
+    Q4_K_M) decode on the mma.sync GEMV and multiply on the tcgen05 GEMM, like
+    the config types."""
     blocks = synth.make_blocks(t, 256, 1024, seed=3)
     w = gpu.Weight.register(blocks, t, 256, 1024)
+    n = NAMES[t]
     try:
-        for M, name in ((1, "mma_gemv<Q6_K,m8>"), (16, "mma_gemv<Q6_K,m16>"), (32, "mma_gemv<Q6_K,m32>"),
-                        (33, "tc_gemm<Q6_K,n256>")):
+        for M, name in ((1, f"mma_gemv<{n},m8>"), (16, f"mma_gemv<{n},m16>"), (32, f"mma_gemv<{n},m32>"),
+                        (33, f"tc_gemm<{n},n256>")):
             assert gpu.kernel_name(w, M) == name
     finally:
         w.release()
