@@ -360,7 +360,9 @@ struct Cfg {
     static constexpr int WB = Lane<TYPE>::kStage;
     static constexpr int XB = NT * 8 * 32 * 16;         // pieces (n8 tile, m, lane) of 16 B
     static constexpr int PB = NT * 8 * TILE_ROWS * 4;   // one tile's fp32 partial, [row][token]
-    static constexpr int CMAX = PAIR ? 1 : NT >= 4 ? (WB > 20000 ? 2 : 4) : kMaxCluster;
+    // Up to 8 CTAs per cluster; with 32 tokens the partial sums are large, so
+    // 4 where three stages still fit beside them, else 2.
+    static constexpr int CMAX = PAIR ? 1 : NT >= 4 ? (Budget<TYPE, MT, 2, 4, 1>::S0 >= 3 ? 4 : 2) : kMaxCluster;
     static constexpr int SETS = PAIR ? 2 : 1;           // result sets per tile
     // Two consumer warpgroups (measured: a third one, with its tighter
     // register budget, is slower).
