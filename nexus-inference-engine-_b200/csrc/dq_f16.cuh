@@ -85,6 +85,25 @@ struct Group<T_I4G128> {
     }
 };
 
+// Q4_1 (gguf_importer.cpp:699-717): record = [(d, m) x8][codes x8 of 16 B];
+// group G = block G; weights fl16(q * d + m).
+template <>
+struct Group<T_Q4_1> {
+    static constexpr int kStage = TILE_ROWS * 160;
+    template <int G>
+    __device__ __forceinline__ static void decode(const uint8_t* stage, int r, uint32_t (&o)[16]) {
+        const uint8_t* rec = stage + r * 160;
+        const uint32_t dm = *reinterpret_cast<const uint32_t*>(rec + 4 * G);
+        const __half2 s2 = u2h((dm & 0xFFFFu) | (dm << 16));
+        const __half2 o2 = u2h((dm >> 16) | (dm & 0xFFFF0000u));
+        const uint4 q = *reinterpret_cast<const uint4*>(rec + 32 + 16 * G);
+        q4_word_pairs(q.x, s2, o2, &o[0]);
+        q4_word_pairs(q.y, s2, o2, &o[4]);
+        q4_word_pairs(q.z, s2, o2, &o[8]);
+        q4_word_pairs(q.w, s2, o2, &o[12]);
+    }
+};
+
 // Q4_0 (gguf_importer.cpp:679-695): record = [d x8][codes x8 of 16 B]; group G
 // = block G.
 template <>

@@ -113,7 +113,7 @@ inline bool make_tiled_shape(int type, int64_t N, int64_t K, TiledShape* s) {
 //   the kernels read them with vector loads.
 //
 //   Q4_0  record 144 B: [d x8 : 16 B][codes x8 : 8 x 16 B, tiled code order]
-//   Q4_1  record 160 B: [(d,m) x8 : 32 B][codes x8 : 8 x 16 B]
+//   Q4_1  record 160 B: [(d,m) x8 : 32 B][codes x8 : 8 x 16 B, tiled code order]
 //   Q8_0  record 272 B: [d x8 : 16 B][codes x8 : 8 x 32 B]
 //   Q4_K  record 144 B: the block itself (d, dmin, scales[12], qs[128]), qs in
 //         tiled code order
@@ -186,6 +186,7 @@ __host__ __device__ inline int block_segments(int type, int r, int j, Segment* s
 // two pairs in the same places of w >> 8.
 // Where the GGUF block holds element e of a group:
 //   Q4_0  byte e % 16, high nibble iff e >= 16   (gguf_importer.cpp:687-690)
+//   Q4_1  the same                                (gguf_importer.cpp:707-712)
 //   Q4_K  byte e / 2,  high nibble iff e is odd  (gguf_importer.cpp:864-868)
 //   I4G   byte e / 2,  high nibble iff e is odd  (quant/gptq.cpp:11-24)
 // ---------------------------------------------------------------------------
@@ -196,7 +197,7 @@ __host__ __device__ inline void q4_code_pos(int e, int* byte, int* shift) {
 }
 
 __host__ __device__ inline int q4_gguf_code(int type, const uint8_t* g, int e) {
-    if (type == T_Q4_0) return e < 16 ? (g[e] & 15) : (g[e - 16] >> 4);
+    if (type == T_Q4_0 || type == T_Q4_1) return e < 16 ? (g[e] & 15) : (g[e - 16] >> 4);
     return (e & 1) ? (g[e >> 1] >> 4) : (g[e >> 1] & 15);
 }
 
@@ -421,11 +422,7 @@ __device__ inline void decode8(int type, const uint8_t* chunk, int r, int e0, fl
             float d = half_bits_to_float(rd16(rec + 4 * j));
             float m = half_bits_to_float(rd16(rec + 4 * j + 2));
             const uint8_t* q = rec + 32 + 16 * j;
-            for (int i = 0; i < 8; ++i) {
-                int e = w + i;
-                int c = e < 16 ? (q[e] & 15) : (q[e - 16] >> 4);
-                out[i] = __fadd_rn(__fmul_rn((float)c, d), m);
-            }
+            for (int i = 0; i < 8; ++i) out[i] = __fadd_rn(__fmul_rn((float)q4_tiled_code(q, w + i), d), m);
             break;
         }
         case T_Q8_0: {  // :721-733

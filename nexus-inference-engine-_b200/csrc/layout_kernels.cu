@@ -31,8 +31,8 @@ __global__ void repack_kernel(const uint8_t* __restrict__ src, uint8_t* __restri
         // Bytes [c0, c1) of the block are 4-bit codes stored in the tiled order;
         // Q3_K's first 96 bytes (hmask, qs), Q6_K's first 192 (ql, qh) and
         // Q5_K's last 160 (qh, qs) are regrouped (q3/q6/q5_tiled_byte).
-        const int c0 = s.type == T_Q4_0 ? 2 : s.type == T_Q4_K ? 16 : is_i4g(s.type) ? 8 : s.g.bb;
-        const int c1 = s.type == T_Q4_0 ? 18 : s.type == T_Q4_K ? 144 : is_i4g(s.type) ? s.g.bb : s.g.bb;
+        const int c0 = s.type == T_Q4_0 ? 2 : s.type == T_Q4_1 ? 4 : s.type == T_Q4_K ? 16 : is_i4g(s.type) ? 8 : s.g.bb;
+        const int c1 = s.type == T_Q4_0 ? 18 : s.type == T_Q4_1 ? 20 : s.type == T_Q4_K ? 144 : s.g.bb;
         for (int q = 0; q < ns; ++q)
             for (int t = lane; t < seg[q].len; t += 32) {
                 const int sb = seg[q].src + t;

@@ -235,6 +235,28 @@ struct Lane<T_Q4_0> {
     }
 };
 
+// Q4_1 (gguf_importer.cpp:699-717): record = [(d, m) x8][codes x8 of 16 B];
+// the slice is blocks 2t, 2t+1; weights fl16(q * d + m).
+template <>
+struct Lane<T_Q4_1> {
+    static constexpr int kStage = TILE_ROWS * 160;
+    uint4 q0, q1;
+    __half2 s2[2], o2[2];
+    __device__ __forceinline__ void load(const uint8_t* st, int row, int t) {
+        const uint8_t* rec = st + row * 160;
+        const uint2 dm = *reinterpret_cast<const uint2*>(rec + 8 * t);
+        q0 = *reinterpret_cast<const uint4*>(rec + 32 + 32 * t);
+        q1 = *reinterpret_cast<const uint4*>(rec + 48 + 32 * t);
+        s2[0] = u2h((dm.x & 0xFFFFu) | (dm.x << 16));
+        o2[0] = u2h((dm.x >> 16) | (dm.x & 0xFFFF0000u));
+        s2[1] = u2h((dm.y & 0xFFFFu) | (dm.y << 16));
+        o2[1] = u2h((dm.y >> 16) | (dm.y & 0xFFFF0000u));
+    }
+    __device__ __forceinline__ void pairs(int m, uint32_t (&p)[4]) const {
+        dq::q4_word_pairs(word_of(m < 4 ? q0 : q1, m & 3), s2[m >> 2], o2[m >> 2], p);
+    }
+};
+
 // Q8_0 (gguf_importer.cpp:721-733): record = [d x8][codes x8 of 32 B]; the
 // slice is blocks 2t, 2t+1 = code bytes 64t .. 64t+63.
 template <>
@@ -979,7 +1001,7 @@ int launch(const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st)
 
 bool type_ok(int type) {
     return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || type == T_Q3_K || type == T_I4G128 || type == T_Q6_K ||
-           type == T_Q5_K;
+           type == T_Q5_K || type == T_Q4_1;
 }
 
 int launch_items(int type, int mt, const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st) {
@@ -1001,6 +1023,7 @@ int launch_items(int type, int mt, const HostItem* it, int n, int x_dtype, int y
         NXQ_CASE(T_I4G128)
         NXQ_CASE(T_Q6_K)
         NXQ_CASE(T_Q5_K)
+        NXQ_CASE(T_Q4_1)
         default:
             return NXQ_ERR_UNSUPPORTED;
     }
@@ -1025,6 +1048,7 @@ int mma_init(int) {
     NXQ_ATTR(T_I4G128)
     NXQ_ATTR(T_Q6_K)
     NXQ_ATTR(T_Q5_K)
+    NXQ_ATTR(T_Q4_1)
 #undef NXQ_ATTR
     return NXQ_OK;
 }
