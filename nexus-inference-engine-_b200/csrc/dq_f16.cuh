@@ -235,6 +235,49 @@ __device__ __forceinline__ void q6_word_pairs(uint32_t l, uint32_t h, __half2 s2
     o[3] = q6_pair<3>(l8, h1, s2);
 }
 
+// Pair K (0..3) of a Q2_K code word (formats.cuh, q2_tiled_byte): the 2-bit
+// codes at bits {2K, 2K+1} (+16) in the mantissa of a magic number whose unit
+// is bit 2K (1024, 256, 64, 16); fl16(q * s + o) as for Q4_K.
+template <int K>
+__device__ __forceinline__ uint32_t q2_pair(uint32_t ls, __half2 s2, __half2 o2) {
+    constexpr uint32_t MG = K == 0 ? 0x64006400u : K == 1 ? 0x5C005C00u : K == 2 ? 0x54005400u : 0x4C004C00u;
+    const uint32_t v = and_or(ls, 0x00030003u << (2 * K), MG);
+    return h2u(__hfma2(__hsub2(u2h(v), u2h(MG)), s2, o2));
+}
+
+// Pairs (2i, 2i+1), i = 4h .. 4h+3, of the 16 elements of a Q2_K code word.
+__device__ __forceinline__ void q2_half_pairs(uint32_t l, __half2 s2, __half2 o2, uint32_t* o) {
+    o[0] = q2_pair<0>(l, s2, o2);
+    o[1] = q2_pair<1>(l, s2, o2);
+    o[2] = q2_pair<2>(l, s2, o2);
+    o[3] = q2_pair<3>(l, s2, o2);
+}
+
+// Q2_K (gguf_importer.cpp:756-786): plane A = [scales[16]][8 x [L0 L1]] at
+// r*80, plane B = (dmin, d) at 128*80 + r*4; group G = elements 32G..32G+31,
+// scale bytes 2G (L0) and 2G+1 (L1): low nibble scale, high nibble min.
+template <>
+struct Group<T_Q2_K> {
+    static constexpr int kStage = TILE_ROWS * 84;
+    template <int G>
+    __device__ __forceinline__ static void decode(const uint8_t* stage, int r, uint32_t (&o)[16]) {
+        const uint8_t* rec = stage + r * 80;
+        const uint32_t dd = *reinterpret_cast<const uint32_t*>(stage + TILE_ROWS * 80 + r * 4);
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(dd & 0xFFFFu)));
+        const float d = __half2float(__ushort_as_half((unsigned short)(dd >> 16)));
+        const uint2 w = *reinterpret_cast<const uint2*>(rec + 16 + 8 * G);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t sc = rec[2 * G + h];
+            const __half2 s2 = __float2half2_rn(d * (float)(sc & 15u));
+            const __half2 o2 = __float2half2_rn(-(dmin * (float)(sc >> 4)));
+            const uint32_t l = h ? w.y : w.x;
+            q2_half_pairs(l, s2, o2, &o[8 * h]);
+            q2_half_pairs(l >> 8, s2, o2, &o[8 * h + 4]);
+        }
+    }
+};
+
 // Pair K (0..3) of a Q5_K L word (formats.cuh, q5_hi_bit): as q6_pair with one
 // high bit (mask 0x10 << 4(K&1)); the 5-bit code q lands in the mantissa of
 // 1024 or 64, and fl16(q * s + o) follows as for Q4_K.

@@ -121,7 +121,8 @@ inline bool make_tiled_shape(int type, int64_t N, int64_t K, TiledShape* s) {
 //         tiled code order][high bits: 8 groups x 4 B, see q5_hi_bit]
 //   Q3_K  plane A 128 x 96 B (hmask + qs regrouped: 8 x [L0 L1 H], see
 //         q3_lo_pos); plane B 128 x 14 B (scales[12], d)
-//   Q2_K  plane A 128 x 80 B (scales[16], qs[64]); plane B 128 x 4 B (dmin, d)
+//   Q2_K  plane A 128 x 80 B (scales[16], qs regrouped: 8 x [L0 L1], see
+//         q2_tiled_byte); plane B 128 x 4 B (dmin, d)
 //   Q6_K  plane A 128 x 192 B (ql, qh regrouped: 8 x [L0 L1 L2 L3 H0 H1], see
 //         q6_lo_bit); plane B 128 x 16 B (scales); plane C 128 x 2 B (d)
 //   I4G   record H + 128 B: [(scale, zero) x 256/gs, padded to H = 16..64 B]
@@ -256,6 +257,27 @@ __host__ __device__ inline uint8_t q3_tiled_byte(const uint8_t* blk, int ob) {
         v |= b << bit;
     }
     return (uint8_t)v;
+}
+
+// Q2_K code order in the tiled copy: the 2-bit codes (block offset 16, element
+// j at bits 2(j%4) of byte j/4, gguf_importer.cpp:756-786) regrouped per 32
+// elements as Q3_K's low codes: words L0 (elements 0..15) and L1 (16..31),
+// element e at bit q3_lo_pos(e % 16).  Byte `ob` (16..79) of plane A.
+__host__ __device__ inline uint8_t q2_tiled_byte(const uint8_t* blk, int ob) {
+    const int G = (ob - 16) >> 3, wb = (ob - 16) & 7, word = wb >> 2;
+    uint32_t v = 0;
+    for (int bit = 0; bit < 8; ++bit) {
+        const int p = 8 * (wb & 3) + bit, s = p >> 4, i = (p & 15) >> 1, f = p & 1;
+        const int j = 32 * G + 16 * word + 2 * i + s;
+        v |= (uint32_t)((blk[16 + (j >> 2)] >> (2 * (j & 3) + f)) & 1) << bit;
+    }
+    return (uint8_t)v;
+}
+
+__device__ __forceinline__ int q2_tiled_code(const uint8_t* rec, int e) {
+    const int G = e >> 5, e32 = e & 31;
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(rec + 16 + 8 * G + 4 * (e32 >> 4));
+    return (int)((w >> q3_lo_pos(e32 & 15)) & 3u);
 }
 
 __device__ __forceinline__ int q3_tiled_code(const uint8_t* rec, int e) {
@@ -441,11 +463,7 @@ __device__ inline void decode8(int type, const uint8_t* chunk, int r, int e0, fl
             int g = e0 >> 4;
             float s = __fmul_rn(d, (float)(rec[g] & 15));
             float m = __fmul_rn(dmin, (float)(rec[g] >> 4));
-            for (int i = 0; i < 8; ++i) {
-                int e = e0 + i;
-                int q = (rec[16 + (e >> 2)] >> (2 * (e & 3))) & 3;
-                out[i] = __fsub_rn(__fmul_rn(s, (float)q), m);
-            }
+            for (int i = 0; i < 8; ++i) out[i] = __fsub_rn(__fmul_rn(s, (float)q2_tiled_code(rec, e0 + i)), m);
             break;
         }
         case T_Q3_K: {  // :791-833

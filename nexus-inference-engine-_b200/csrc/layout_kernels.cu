@@ -29,8 +29,8 @@ __global__ void repack_kernel(const uint8_t* __restrict__ src, uint8_t* __restri
         Segment seg[3];
         const int ns = block_segments(s.type, (int)r, (int)j, seg);
         // Bytes [c0, c1) of the block are 4-bit codes stored in the tiled order;
-        // Q3_K's first 96 bytes (hmask, qs), Q6_K's first 192 (ql, qh) and
-        // Q5_K's last 160 (qh, qs) are regrouped (q3/q6/q5_tiled_byte).
+        // Q3_K's first 96 bytes (hmask, qs), Q6_K's first 192 (ql, qh), Q5_K's
+        // last 160 (qh, qs) and Q2_K's qs are regrouped (q3/q6/q5/q2_tiled_byte).
         const int c0 = s.type == T_Q4_0 ? 2 : s.type == T_Q4_1 ? 4 : s.type == T_Q4_K ? 16 : is_i4g(s.type) ? 8 : s.g.bb;
         const int c1 = s.type == T_Q4_0 ? 18 : s.type == T_Q4_1 ? 20 : s.type == T_Q4_K ? 144 : s.g.bb;
         for (int q = 0; q < ns; ++q)
@@ -46,6 +46,8 @@ __global__ void repack_kernel(const uint8_t* __restrict__ src, uint8_t* __restri
                     v = q6_tiled_byte(blk, sb);
                 } else if (s.type == T_Q5_K && sb >= 16) {
                     v = q5_tiled_byte(blk, sb - 16);
+                } else if (s.type == T_Q2_K && sb >= 16 && sb < 80) {
+                    v = q2_tiled_byte(blk, sb);
                 } else {
                     v = blk[sb];
                 }

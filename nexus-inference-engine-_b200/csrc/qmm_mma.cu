@@ -257,6 +257,36 @@ struct Lane<T_Q4_1> {
     }
 };
 
+// Q2_K (gguf_importer.cpp:756-786): plane A = [scales[16]][8 x [L0 L1]] per
+// row (formats.cuh, q2_tiled_byte), plane B = (dmin, d); the slice (elements
+// 64t .. 64t+63) is code words 4t .. 4t+3 with scale bytes 4t .. 4t+3.
+template <>
+struct Lane<T_Q2_K> {
+    static constexpr int kStage = TILE_ROWS * 84;
+    uint4 q;
+    __half2 s2[4], o2[4];
+    __device__ __forceinline__ void load(const uint8_t* st, int row, int t) {
+        const uint8_t* rec = st + row * 80;
+        q = *reinterpret_cast<const uint4*>(rec + 16 + 16 * t);
+        const uint32_t sc = *reinterpret_cast<const uint32_t*>(rec + 4 * t);
+        const uint32_t dd = *reinterpret_cast<const uint32_t*>(st + TILE_ROWS * 80 + row * 4);
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(dd & 0xFFFFu)));
+        const float d = __half2float(__ushort_as_half((unsigned short)(dd >> 16)));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t b = (sc >> (8 * i)) & 0xFFu;
+            s2[i] = __float2half2_rn(d * (float)(b & 15u));
+            o2[i] = __float2half2_rn(-(dmin * (float)(b >> 4)));
+        }
+    }
+    // Elements 8m .. 8m+7: code word m >> 1 (low or high byte of each half),
+    // scale group m >> 1.
+    __device__ __forceinline__ void pairs(int m, uint32_t (&p)[4]) const {
+        const uint32_t l = word_of(q, m >> 1);
+        dq::q2_half_pairs((m & 1) ? l >> 8 : l, s2[m >> 1], o2[m >> 1], p);
+    }
+};
+
 // Q8_0 (gguf_importer.cpp:721-733): record = [d x8][codes x8 of 32 B]; the
 // slice is blocks 2t, 2t+1 = code bytes 64t .. 64t+63.
 template <>
@@ -1001,7 +1031,7 @@ int launch(const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st)
 
 bool type_ok(int type) {
     return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || type == T_Q3_K || type == T_I4G128 || type == T_Q6_K ||
-           type == T_Q5_K || type == T_Q4_1;
+           type == T_Q5_K || type == T_Q4_1 || type == T_Q2_K;
 }
 
 int launch_items(int type, int mt, const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st) {
@@ -1024,6 +1054,7 @@ int launch_items(int type, int mt, const HostItem* it, int n, int x_dtype, int y
         NXQ_CASE(T_Q6_K)
         NXQ_CASE(T_Q5_K)
         NXQ_CASE(T_Q4_1)
+        NXQ_CASE(T_Q2_K)
         default:
             return NXQ_ERR_UNSUPPORTED;
     }
@@ -1049,6 +1080,7 @@ int mma_init(int) {
     NXQ_ATTR(T_Q6_K)
     NXQ_ATTR(T_Q5_K)
     NXQ_ATTR(T_Q4_1)
+    NXQ_ATTR(T_Q2_K)
 #undef NXQ_ATTR
     return NXQ_OK;
 }

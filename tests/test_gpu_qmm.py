@@ -277,9 +277,9 @@ def test_qmm_small_batch_fp32_bf16_activations(gpu, t, x_dt):
         w.release()
 
 
-@pytest.mark.parametrize("t", [3, 13, 14], ids=lambda t: NAMES[t])
+@pytest.mark.parametrize("t", [3, 10, 13, 14], ids=lambda t: NAMES[t])
 def test_other_types_run_on_the_tensor_core_kernels(gpu, t):
-    """Q4_1, Q5_K and Q6_K (Q5_K and Q6_K are the tensors of Q5_K_M files and the
+    """Q4_1, Q2_K, Q5_K and Q6_K (Q5_K and Q6_K are the tensors of Q5_K_M files and the
     high-precision ones of Q4_K_M) decode on the mma.sync GEMV and multiply on
     the tcgen05 GEMM, like the config types."""
     blocks = synth.make_blocks(t, 256, 1024, seed=3)
