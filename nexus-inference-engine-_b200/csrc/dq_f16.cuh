@@ -65,25 +65,34 @@ struct Group<T_Q4_K> {
     }
 };
 
-// NXF INT4 groups of 128 (quant/gptq.cpp:9-27): record = [(scale, zero) x2 :
-// 16 B][codes x8 of 16 B]; 32-element group G lies in block G / 4.  The weight
-// is fl16(q * fl16(scale) + fl16(-(zero * scale))).
-template <>
-struct Group<T_I4G128> {
-    static constexpr int kStage = TILE_ROWS * 144;
+// NXF INT4 groups (quant/gptq.cpp:9-27): record = [(scale, zero) per group,
+// padded to H bytes][codes x8 of 16 B]; 32-element group G lies in block
+// 32G / gs.  The weight is fl16(q * fl16(scale) + fl16(-(zero * scale))).
+template <int TYPE>
+struct GroupI4G {
+    static constexpr int GS = i4g_gs(TYPE), H = i4g_hdr(TYPE), REC = H + CHUNK_K / 2;
+    static constexpr int kStage = TILE_ROWS * REC;
     template <int G>
     __device__ __forceinline__ static void decode(const uint8_t* stage, int r, uint32_t (&o)[16]) {
-        const uint8_t* rec = stage + r * 144;
-        const float2 sz = *reinterpret_cast<const float2*>(rec + 8 * (G / 4));
+        const uint8_t* rec = stage + r * REC;
+        const float2 sz = *reinterpret_cast<const float2*>(rec + 8 * (32 * G / GS));
         const __half2 s2 = __float2half2_rn(sz.x);
         const __half2 o2 = __float2half2_rn(-(sz.y * sz.x));
-        const uint4 q = *reinterpret_cast<const uint4*>(rec + 16 + 16 * G);
+        const uint4 q = *reinterpret_cast<const uint4*>(rec + H + 16 * G);
         q4_word_pairs(q.x, s2, o2, &o[0]);
         q4_word_pairs(q.y, s2, o2, &o[4]);
         q4_word_pairs(q.z, s2, o2, &o[8]);
         q4_word_pairs(q.w, s2, o2, &o[12]);
     }
 };
+template <>
+struct Group<T_I4G32> : GroupI4G<T_I4G32> {};
+template <>
+struct Group<T_I4G64> : GroupI4G<T_I4G64> {};
+template <>
+struct Group<T_I4G128> : GroupI4G<T_I4G128> {};
+template <>
+struct Group<T_I4G256> : GroupI4G<T_I4G256> {};
 
 // Q4_1 (gguf_importer.cpp:699-717): record = [(d, m) x8][codes x8 of 16 B];
 // group G = block G; weights fl16(q * d + m).

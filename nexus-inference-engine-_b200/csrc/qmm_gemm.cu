@@ -371,8 +371,8 @@ int launch(const Weight* w, const CUtensorMap& tmap, void* y, int y_dtype, int64
 }
 
 bool type_ok(int type) {
-    return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || type == T_Q3_K || type == T_I4G128 || type == T_Q6_K ||
-           type == T_Q5_K || type == T_Q4_1 || type == T_Q2_K;
+    return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || type == T_Q3_K || type == T_Q6_K ||
+           type == T_Q5_K || type == T_Q4_1 || type == T_Q2_K || is_i4g(type);
 }
 
 }  // namespace
@@ -391,7 +391,8 @@ int gemm_init(int) {
     int rc;
     if ((rc = set_attr<T_Q4_K>()) || (rc = set_attr<T_Q4_0>()) || (rc = set_attr<T_Q8_0>()) ||
         (rc = set_attr<T_Q3_K>()) || (rc = set_attr<T_I4G128>()) || (rc = set_attr<T_Q6_K>()) ||
-        (rc = set_attr<T_Q5_K>()) || (rc = set_attr<T_Q4_1>()) || (rc = set_attr<T_Q2_K>()))
+        (rc = set_attr<T_Q5_K>()) || (rc = set_attr<T_Q4_1>()) || (rc = set_attr<T_Q2_K>()) ||
+        (rc = set_attr<T_I4G32>()) || (rc = set_attr<T_I4G64>()) || (rc = set_attr<T_I4G256>()))
         return rc;
     return NXQ_OK;
 }
@@ -436,6 +437,9 @@ int gemm_qmatmul(const Weight* w, const void* x, int x_dtype, void* y, int y_dty
         case T_Q5_K: return launch<T_Q5_K>(w, tmap, y, y_dtype, M, st);
         case T_Q4_1: return launch<T_Q4_1>(w, tmap, y, y_dtype, M, st);
         case T_Q2_K: return launch<T_Q2_K>(w, tmap, y, y_dtype, M, st);
+        case T_I4G32: return launch<T_I4G32>(w, tmap, y, y_dtype, M, st);
+        case T_I4G64: return launch<T_I4G64>(w, tmap, y, y_dtype, M, st);
+        case T_I4G256: return launch<T_I4G256>(w, tmap, y, y_dtype, M, st);
         default: return NXQ_ERR_UNSUPPORTED;
     }
 }

@@ -191,26 +191,39 @@ struct Lane<T_Q6_K> {
     }
 };
 
-// NXF INT4 groups of 128 (quant/gptq.cpp:9-27): record = [(scale, zero) x2 :
-// 16 B][codes x8 of 16 B]; the slice (elements 64t .. 64t+63) lies in block
-// t / 2.  Weights fl16(q * fl16(scale) + fl16(-(zero * scale))).
-template <>
-struct Lane<T_I4G128> {
-    static constexpr int kStage = TILE_ROWS * 144;
+// NXF INT4 groups (quant/gptq.cpp:9-27): record = [(scale, zero) per group of
+// the chunk, padded to H bytes][codes x8 of 16 B]; sub-blocks 2t, 2t+1 of the
+// slice lie in groups 64t / gs and (64t + 32) / gs.  Weights
+// fl16(q * fl16(scale) + fl16(-(zero * scale))).
+template <int TYPE>
+struct LaneI4G {
+    static constexpr int GS = i4g_gs(TYPE), H = i4g_hdr(TYPE), REC = H + CHUNK_K / 2;
+    static constexpr int kStage = TILE_ROWS * REC;
     uint4 q0, q1;
     __half2 s2[2], o2[2];
     __device__ __forceinline__ void load(const uint8_t* st, int row, int t) {
-        const uint8_t* rec = st + row * 144;
-        const float2 sz = *reinterpret_cast<const float2*>(rec + 8 * (t >> 1));
-        q0 = *reinterpret_cast<const uint4*>(rec + 16 + 32 * t);
-        q1 = *reinterpret_cast<const uint4*>(rec + 32 + 32 * t);
-        s2[0] = s2[1] = __float2half2_rn(sz.x);
-        o2[0] = o2[1] = __float2half2_rn(-(sz.y * sz.x));
+        const uint8_t* rec = st + row * REC;
+        q0 = *reinterpret_cast<const uint4*>(rec + H + 32 * t);
+        q1 = *reinterpret_cast<const uint4*>(rec + H + 16 + 32 * t);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const float2 sz = *reinterpret_cast<const float2*>(rec + 8 * ((64 * t + 32 * h) / GS));
+            s2[h] = __float2half2_rn(sz.x);
+            o2[h] = __float2half2_rn(-(sz.y * sz.x));
+        }
     }
     __device__ __forceinline__ void pairs(int m, uint32_t (&p)[4]) const {
         dq::q4_word_pairs(word_of(m < 4 ? q0 : q1, m & 3), s2[m >> 2], o2[m >> 2], p);
     }
 };
+template <>
+struct Lane<T_I4G32> : LaneI4G<T_I4G32> {};
+template <>
+struct Lane<T_I4G64> : LaneI4G<T_I4G64> {};
+template <>
+struct Lane<T_I4G128> : LaneI4G<T_I4G128> {};
+template <>
+struct Lane<T_I4G256> : LaneI4G<T_I4G256> {};
 
 // Q4_0 (gguf_importer.cpp:679-695): record = [d x8][codes x8 of 16 B]; the
 // slice is blocks 2t, 2t+1.
@@ -1030,8 +1043,8 @@ int launch(const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st)
 }
 
 bool type_ok(int type) {
-    return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || type == T_Q3_K || type == T_I4G128 || type == T_Q6_K ||
-           type == T_Q5_K || type == T_Q4_1 || type == T_Q2_K;
+    return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || type == T_Q3_K || type == T_Q6_K ||
+           type == T_Q5_K || type == T_Q4_1 || type == T_Q2_K || is_i4g(type);
 }
 
 int launch_items(int type, int mt, const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st) {
@@ -1055,6 +1068,9 @@ int launch_items(int type, int mt, const HostItem* it, int n, int x_dtype, int y
         NXQ_CASE(T_Q5_K)
         NXQ_CASE(T_Q4_1)
         NXQ_CASE(T_Q2_K)
+        NXQ_CASE(T_I4G32)
+        NXQ_CASE(T_I4G64)
+        NXQ_CASE(T_I4G256)
         default:
             return NXQ_ERR_UNSUPPORTED;
     }
@@ -1081,6 +1097,9 @@ int mma_init(int) {
     NXQ_ATTR(T_Q5_K)
     NXQ_ATTR(T_Q4_1)
     NXQ_ATTR(T_Q2_K)
+    NXQ_ATTR(T_I4G32)
+    NXQ_ATTR(T_I4G64)
+    NXQ_ATTR(T_I4G256)
 #undef NXQ_ATTR
     return NXQ_OK;
 }

@@ -8,8 +8,8 @@ special scales and zeros, codes 0 and 15, zeros omitted), the block form
 against the flat form, packing from quant/gptq.cpp's flat order and from the
 GEMV shader's K-major order (identical blocks), and packing errors.
 GPU: registration from both orders decodes bit-exactly to the fixtures and
-the reference; matmul within the parity bar on the decode GEMV (groups of
-128), the prefill GEMM (groups of 128) and the CUDA-core path (other groups)."""
+the reference; matmul within the parity bar on the decode GEMV and the
+prefill GEMM for every group size."""
 from __future__ import annotations
 
 from pathlib import Path
@@ -132,7 +132,9 @@ def test_golden_matrix_on_gpu(gpu, gs):
 @pytest.mark.gpu
 @pytest.mark.parametrize("gs,M,kernel", [(128, 1, "mma_gemv<I4G128,m8>"), (128, 8, "mma_gemv<I4G128,m8>"),
                                           (128, 32, "mma_gemv<I4G128,m32>"), (128, 300, "tc_gemm<I4G128,n256>"),
-                                          (64, 4, "simt"), (32, 40, "simt"), (256, 2, "simt")])
+                                          (64, 4, "mma_gemv<I4G64,m8>"), (32, 20, "mma_gemv<I4G32,m32>"),
+                                          (256, 2, "mma_gemv<I4G256,m8>"), (32, 40, "tc_gemm<I4G32,n256>"),
+                                          (64, 100, "tc_gemm<I4G64,n256>"), (256, 64, "tc_gemm<I4G256,n256>")])
 def test_matmul_paths(gpu, gs, M, kernel):
     import torch
 
