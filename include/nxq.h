@@ -216,9 +216,10 @@ NXQ_API int nxq_qmatmul_grouped(const nxq_weight_t* w, int count, const void* co
  * activations.metal:51, after its gate/up and projection GEMVs):
  *   nxq_qmatmul_swiglu:   h_dev[M][N] = silu(x Wg^T) * (x Wu^T), silu(g) = g / (1 + exp(-g)),
  *                         for gate and up weights of the same shape and type;
- *                         one decode launch (each CTA takes a tile of both
- *                         weights) for M <= 32 when the weight has tiles for
- *                         half the SMs, else gate and up, then one small kernel.
+ *                         one decode launch for M <= 32 (a row tile's gate and
+ *                         up tile-chunks are one run of units, a tile shared
+ *                         by several CTAs finished by one of them), else gate
+ *                         and up, then one small kernel.
  *   nxq_qmatmul_residual: y_dev[M][N] = x W^T + res_dev[M][N] (fp32 residual;
  *                         y_dev may be res_dev), added before the decode
  *                         kernel's store, else by a small kernel after it.

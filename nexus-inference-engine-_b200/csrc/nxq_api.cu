@@ -87,6 +87,7 @@ int grow(void** buf, size_t* have, size_t need) {
 int report_status(const DeviceStatus& st) {
     if (st.code) {
         cudaMemset(g_ctx.status, 0, sizeof(DeviceStatus));
+        scratch_reset_counters();
         return fail(NXQ_ERR_TIMEOUT, "device-side bounded wait expired (code %u at %u)", st.code,
                     st.where);
     }

@@ -46,6 +46,7 @@
 
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 
 #include "dq_f16.cuh"
 #include "qmm_mma.h"
@@ -461,7 +462,13 @@ struct MmaItem {
     int chunks;        // K chunks per row
     int M;
     int cluster0;      // first cluster of this item
-    int tile_base, tile_rem;  // its cluster q owns tile_base + (q < tile_rem) tiles, in order
+    // Units: tile t's tile-chunks are units t kun .. t kun + kun - 1 (kun =
+    // chunks; paired: twice that, the gate's then the up weight's).  C = 1:
+    // CTA q of the item takes units [s(q), s(q + 1)), s(q) = gran (q ub +
+    // min(q, ur)): whole tiles (gran = kun) or any run of units (gran = 1; a
+    // tile shared by several CTAs is finished by the last of them).  C > 1:
+    // cluster q owns tile q.
+    int ub, ur, gran;
     const uint8_t* w_up;  // SwiGLU pairing: the up weight (same shape); y = silu(x W^T) * (x W_up^T)
     const float* res;     // residual [M][N] fp32 added to the result before the store, or null
 };
@@ -472,6 +479,8 @@ struct MmaParams {
     int x_dtype, y_dtype;
     int C;  // CTAs per cluster: the reduction is split C ways inside a cluster
     DeviceStatus* status;
+    float* part;    // C = 1, gran = 1: a partial-sum slot per CTA
+    unsigned* cnt;  // ... and a counter per CTA (zero between launches)
 };
 
 __device__ __forceinline__ void store_y(void* y, int dt, int64_t i, float v) {
@@ -497,13 +506,18 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
 // One CTA per SM: warps 0 .. 8G-1 are G consumer groups that take the CTA's
 // units in turn (group = unit index mod G), the warps after them are producers
 // (one for up to 8 tokens, else four; the first also issues the tile-chunk
-// copies).  Cluster q owns a contiguous range of tiles; CTA rank r of the
-// cluster takes chunks [r K/C, (r+1) K/C) of each, so with C = 1 a CTA owns
-// whole tiles and writes y directly; with C > 1 the cluster owns one tile and
-// ranks 1..C-1 push their partial sums into rank 0's shared memory (one bulk
-// copy each, completing on an mbarrier there), which adds them in rank order:
-// no global-memory round trip and a result that does not depend on timing.
-// A CTA's units are consecutive tile-chunks in memory in either case.
+// copies).  A CTA's units are consecutive tile-chunks in memory.  C = 1: the
+// CTA takes a run of units (MmaItem), whole tiles or not; a tile it holds
+// whole is written to y directly, a tile shared with other CTAs (stream-K)
+// through partial sums in global memory: the sharers that hold its later
+// units store their partials and count themselves in, and the one holding its
+// first units (at the end of its run) waits for the counts, adds the partials
+// in CTA order and writes y.  Every CTA of the launch fits on the GPU at once
+// and publishes without waiting, so the wait ends once the later CTAs have
+// run their first tile.  C > 1: the cluster owns one tile, CTA rank r takes chunks
+// [r K/C, (r+1) K/C), and ranks 1..C-1 push their partial sums into rank 0's
+// shared memory (one bulk copy each, completing on an mbarrier there), which
+// adds them in rank order.  Either way the result does not depend on timing.
 // LOOKUP = true: the CTA looks its item up from its cluster index, and the
 // item's fields live in registers; false: a launch of one item, read at fixed
 // offsets of the kernel parameters.  Grouped launches need the lookup; single
@@ -524,6 +538,7 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
     __shared__ uint64_t empty[S];  // the 8 warps of the consuming group are done with the stage
     __shared__ uint64_t recv_full;  // cluster leader: the C-1 partials have landed
     __shared__ int s_abort;
+    __shared__ int s_last;  // stream-K: the counts of the tile this CTA finishes are in
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, tq = lane & 3;
@@ -535,23 +550,22 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
     const MmaItem& I = p.it[LOOKUP ? ii : 0];
     const int q = qg - I.cluster0;
     const int Kc = I.chunks;
-    const int kc0 = rank * Kc / C, kr = (rank + 1) * Kc / C - kc0;
-    const int t0 = q * I.tile_base + (q < I.tile_rem ? q : I.tile_rem);
-    const int ntiles = I.tile_base + (q < I.tile_rem ? 1 : 0);
-    const int kun = PAIR ? 2 * kr : kr;  // units per tile
-    const int n = ntiles * kun;
+    const int kun = PAIR ? 2 * Kc : Kc;  // units per tile
+    // Start of CTA b's run (C = 1).
+    auto run_start = [&](int b) { return I.gran * (b * I.ub + (b < I.ur ? b : I.ur)); };
+    const int g0 = C == 1 ? run_start(q) : q * kun + rank * Kc / C;
+    const int g1 = C == 1 ? run_start(q + 1) : q * kun + (rank + 1) * Kc / C;
+    const int n = g1 - g0;  // this CTA's units: item units g0 .. g1 - 1
     const int64_t K = I.K, N = I.N;
     const int M = I.M;
 
-    // Unit u's tile-chunk: tiles t0 .. t0 + ntiles - 1 hold chunks kc0 ..
-    // kc0 + kr - 1 each, and either ntiles = 1 or kr = all chunks, so the
-    // units are consecutive tile-chunks from w_base on.
-    const uint8_t* const w_base = I.w + ((int64_t)t0 * Kc + kc0) * WB;
+    // Unit u is item unit g0 + u: without pairing, the tile-chunk at w_base + u WB.
+    const uint8_t* const w_base = I.w + (int64_t)g0 * WB;
     auto w_issue = [&](int u, int stg) {
         const uint8_t* src = w_base + (int64_t)u * WB;
-        if constexpr (PAIR) {  // unit u = chunk c of tile ti, gate for c < kr, up after
-            const int ti = u / kun, c = u - ti * kun;
-            src = (c < kr ? I.w : I.w_up) + ((int64_t)(t0 + ti) * Kc + kc0 + (c < kr ? c : c - kr)) * WB;
+        if constexpr (PAIR) {  // chunk c of tile t: the gate's for c < Kc, the up weight's after
+            const int g = g0 + u, t = g / kun, c = g - t * kun;
+            src = (c < Kc ? I.w : I.w_up) + ((int64_t)t * Kc + (c < Kc ? c : c - Kc)) * WB;
         }
         ptx::mbar_arrive_expect_tx(&full[stg], WB);
         ptx::bulk_g2s(wst + stg * WB, src, WB, &full[stg]);
@@ -616,20 +630,18 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
             }
             return ok != 0;
         };
-        auto chunk_k0 = [&](int u) {
-            const int ti = u / kr;
-            return (int64_t)(kc0 + u - ti * kr) * CHUNK_K;
-        };
+        // Unit u reads the activations of chunk (g0 + u) mod Kc (kun is a multiple of Kc).
+        auto chunk_k0 = [&](int u) { return (int64_t)((g0 + u) % Kc) * CHUNK_K; };
         if (p.x_dtype == NXQ_F16) {
             // Lane (t4, m) = ((lane >> 3) & 3, lane & 7) copies piece (token, t4,
             // m) of every token: one source row and one destination step apart.
             const __half* xh = static_cast<const __half*>(I.x);
             const int t4 = (lane >> 3) & 3, m = lane & 7;
             const int tok0 = 8 * pw, tok1 = M < tok0 + 8 ? M : tok0 + 8;
-            for (int u = 0, c = 0; u < n; ++u, c = c + 1 == kr ? 0 : c + 1) {
+            for (int u = 0, c = g0 % Kc; u < n; ++u, c = c + 1 == Kc ? 0 : c + 1) {
                 if (!refill(u)) break;
                 uint4* xd = reinterpret_cast<uint4*>(xst + (u % S) * XB) + m * 32 + t4;
-                const int64_t k = (int64_t)(kc0 + c) * CHUNK_K + 64 * t4 + 8 * m;
+                const int64_t k = (int64_t)c * CHUNK_K + 64 * t4 + 8 * m;
                 const uint32_t bytes = k < K ? 16u : 0u;
                 const __half* src = xh + (k < K ? k : 0) + (int64_t)tok0 * K;
                 for (int tok = tok0; tok < tok1; ++tok, src += K)
@@ -704,11 +716,44 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
             }
         }
     } else {
-        // ---- consumers: group gi takes the units c = gi mod G of each tile ----
+        // ---- consumers: of the units [cs, ce) that this CTA holds of tile t,
+        // group gi takes c = cs + gi, cs + gi + G, ... ----
         asm volatile("griddepcontrol.wait;" ::: "memory");
         const int gi = warp >> 3, wg = warp & 7;
+        const int r0 = 16 * wg + g;  // the fragment rows r0, r0 + 8 of a tile
         bool dead = false;
-        for (int ti = 0; ti < ntiles; ++ti) {
+        // Stores a tile's sums A (PAIR: gate; AU: up): y = A, or silu(A) * AU,
+        // plus the residual.
+        auto store_vals = [&](int t, const auto& A, const auto& AU) {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int tok = 8 * nt + 2 * tq + (e & 1);
+                    const int64_t row = (int64_t)t * TILE_ROWS + r0 + 8 * (e >> 1);
+                    if (tok < M && row < N) {
+                        float v = A[nt][e];
+                        if constexpr (PAIR) v = v / (1.0f + expf(-v)) * AU[nt][e];
+                        if (I.res) v += I.res[tok * N + row];
+                        store_y(I.y, p.y_dtype, tok * N + row, v);
+                    }
+                }
+        };
+        // Stream-K (C = 1, runs that start or end inside a tile): CTAs b0 ..
+        // b1 of the item hold units of tile t.  b0, which holds the tile's
+        // first units, reaches it at the end of its run and finishes it; b0 + 1
+        // .. b1 reach it at the start of their runs (or hold runs inside it)
+        // and publish their partials: each one the partial of the tile its
+        // run starts in (its only one) and a count on b0's counter (no other
+        // shared tile starts inside b0's run).
+        auto cta_of = [&](int gu) {
+            const int big = I.ur * (I.ub + 1);
+            return gu < big ? gu / (I.ub + 1) : I.ur + (gu - big) / I.ub;
+        };
+        auto part_of = [&](int b) { return p.part + (size_t)(I.cluster0 + b) * (Cf::SETS * PB / 4); };
+        for (int t = g0 / kun; t * kun < g1; ++t) {
+            const int cs = g0 > t * kun ? g0 - t * kun : 0;
+            const int ce = g1 < (t + 1) * kun ? g1 - t * kun : kun;
             // acc[n8 token tile][c0..c3]: c0/c1 = row 16wg+g, tokens 8nt+2t,
             // 8nt+2t+1; c2/c3 = row 16wg+8+g.
             // PAIR: accu/accu2 hold the up projection's sums.
@@ -728,7 +773,7 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
             }
             // Unit c of this tile into the sums A (A2: the second chain).
             auto unit = [&](int c, auto& A, auto& A2) {
-                const int u = ti * kun + c, stg = u % S;
+                const int u = t * kun + c - g0, stg = u % S;
                 if (!dead && !ptx::mbar_wait(&full[stg], (uint32_t)(u / S) & 1u, ctl, 31)) dead = true;
                 if (!dead) {
                     Lane<TYPE> LA, LB;
@@ -754,10 +799,10 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
                 __syncwarp();
                 if (lane == 0) ptx::mbar_arrive(&empty[stg]);
             };
-            int c = gi;
-            for (; c < kr; c += kGroups) unit(c, acc, acc2);
+            int c = cs + gi;
+            for (; c < (ce < Kc ? ce : Kc); c += kGroups) unit(c, acc, acc2);
             if constexpr (PAIR)
-                for (; c < kun; c += kGroups) unit(c, accu, accu2);
+                for (; c < ce; c += kGroups) unit(c, accu, accu2);
             auto fold = [](auto& A, auto& A2) {
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
@@ -769,8 +814,7 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
                 if constexpr (PAIR) fold(accu, accu2);
             }
             // ---- tile end: groups 1.. hand their partials to group 0 ----
-            const int r0 = 16 * wg + g;
-            auto slot = [&](int gg, int set) { return comb + (((gg - 1) * 2 + (ti & 1)) * Cf::SETS + set) * (PB / 4); };
+            auto slot = [&](int gg, int set) { return comb + (((gg - 1) * 2 + (t & 1)) * Cf::SETS + set) * (PB / 4); };
             auto put = [&](float* cb, auto& A) {
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
@@ -799,24 +843,63 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
                 add(slot(gg, 0), acc);
                 if constexpr (PAIR) add(slot(gg, 1), accu);
             }
-            // The value stored for element e: the sum, or silu(gate) * up, plus
-            // the residual.
-            auto result = [&](int nt, int e, int tok, int64_t row) {
-                float v = acc[nt][e];
-                if constexpr (PAIR) v = v / (1.0f + expf(-v)) * accu[nt][e];
-                if (I.res) v += I.res[tok * N + row];
-                return v;
-            };
-            const int64_t tile = t0 + ti;
-            if (C == 1) {
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int tok = 8 * nt + 2 * tq + (e & 1);
-                        const int64_t row = tile * TILE_ROWS + r0 + 8 * (e >> 1);
-                        if (tok < M && row < N) store_y(I.y, p.y_dtype, tok * N + row, result(nt, e, tok, row));
+            if (C == 1 && cs == 0 && ce == kun) {
+                store_vals(t, acc, accu);
+            } else if (C == 1) {
+                const int b0 = cta_of(t * kun), b1 = cta_of(t * kun + kun - 1);
+                unsigned* cn = p.cnt + I.cluster0 + b0;
+                if (q != b0) {
+                    float* mine = part_of(q);
+                    put(mine, acc);
+                    if constexpr (PAIR) put(mine + PB / 4, accu);
+                    named_sync(3, kThreads);
+                    if (tid == 0) {
+                        __threadfence();  // the group's partial (ordered by the barrier) before the count
+                        atomicAdd(cn, 1u);
                     }
+                } else {
+                    // Wait (bounded) for the b1 - b0 counts, then add the
+                    // partials in CTA order, this CTA's first: the same sum
+                    // whatever the timing.
+                    if (tid == 0) {
+                        const unsigned need = (unsigned)(b1 - b0);
+                        const long long w0 = clock64();
+                        int ok = 1;
+                        for (;;) {
+                            unsigned v;
+                            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(cn) : "memory");
+                            if (v >= need) break;
+                            if (*ctl.abort || clock64() - w0 > ptx::kWaitCycles) {
+                                if (!*ctl.abort) ptx::raise_timeout(ctl, 34);
+                                ok = 0;
+                                break;
+                            }
+                            __nanosleep(64);
+                        }
+                        if (ok) *cn = 0u;  // every count is in: ready for the next launch
+                        s_last = ok;
+                    }
+                    named_sync(3, kThreads);
+                    if (s_last) {
+                        auto add_l2 = [&](const float* cb, auto& A) {
+#pragma unroll
+                            for (int nt = 0; nt < NT; ++nt) {
+                                const float2 a = __ldcg(reinterpret_cast<const float2*>(cb + r0 * RS + 8 * nt + 2 * tq));
+                                const float2 b = __ldcg(reinterpret_cast<const float2*>(cb + (r0 + 8) * RS + 8 * nt + 2 * tq));
+                                A[nt][0] += a.x;
+                                A[nt][1] += a.y;
+                                A[nt][2] += b.x;
+                                A[nt][3] += b.y;
+                            }
+                        };
+                        for (int b = b0 + 1; b <= b1; ++b) {
+                            const float* pb = part_of(b);
+                            add_l2(pb, acc);
+                            if constexpr (PAIR) add_l2(pb + PB / 4, accu);
+                        }
+                        store_vals(t, acc, accu);
+                    }
+                }
             } else if (rank > 0) {
                 // Push this rank's partial to the leader: stage memory is free
                 // now (every unit has been consumed), so it holds the copy source.
@@ -861,14 +944,7 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
                             acc[nt][3] += b.y;
                         }
                     }
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int tok = 8 * nt + 2 * tq + (e & 1);
-                            const int64_t row = tile * TILE_ROWS + r0 + 8 * (e >> 1);
-                            if (tok < M && row < N) store_y(I.y, p.y_dtype, tok * N + row, result(nt, e, tok, row));
-                        }
+                    store_vals(t, acc, accu);
                 }
             }
         }
@@ -890,6 +966,7 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
 }
 
 bool g_mma_enabled = true;
+bool g_streamk = true;  // NXQ_GEMV_SPLIT=tiles: whole tiles and clusters only
 int g_sm_count = 0;
 
 // How many clusters of 2, 4, 8 CTAs of a variant fit on the GPU at once
@@ -944,20 +1021,27 @@ struct HostItem {
     const float* res = nullptr;    // residual added before the store
 };
 
-// Work split of a launch: C CTAs per cluster (K cut C ways, the same C for
-// every item) and Q_i clusters for item i, at most as many clusters in all as
-// fit on the GPU at once (one wave).  C = 1: every CTA owns ceil or floor of
-// T_i / Q_i whole tiles of one item, and the SMs go one at a time to the item
-// whose CTAs have the most units (so a lone weight gets min(T, SMs) CTAs).
-// C > 1 (only when all items together have few enough tiles): one tile per
-// cluster.  Picks the split with the fewest units on the busiest CTA, the
-// smallest C among equals.  Returns the number of clusters.
-int pick_split(const HostItem* it, int n, const int* maxq, int cmax, MmaParams* p) {
-    int64_t T[kMaxItems], Kc[kMaxItems], q[kMaxItems], sumT = 0, minKc = INT64_MAX;
+// Work split of a launch, one of three kinds, with at most as many clusters
+// in all as fit on the GPU at once (one wave):
+//   whole tiles: C = 1, item i's Q_i CTAs own floor or ceil of T_i / Q_i tiles
+//     each; the SMs go one at a time to the item whose CTAs have the most
+//     units (so a lone weight gets min(T, SMs) CTAs);
+//   clusters: C > 1 CTAs per tile, K cut C ways (the same C for every item;
+//     only when all items together have few enough tiles);
+//   stream-K (when sk_margin >= 0): C = 1, item i's Q_i CTAs take equal runs
+//     of its T_i kun_i units, tiles shared between CTAs finished through
+//     partial sums in global memory; the SMs go to the item with the longest
+//     runs.
+// Picks the fewest units on the busiest CTA, ties to whole tiles, then to the
+// smallest C; stream-K only when its busiest CTA has more than sk_margin units
+// fewer (its shared tiles cost a wait at the end of a run, and no SM is left
+// for the next launch to start on early).  Returns the number of clusters.
+int pick_split(const HostItem* it, int n, const int* maxq, int cmax, int sk_margin, MmaParams* p) {
+    int64_t T[kMaxItems], Kc[kMaxItems], q[kMaxItems], qs[kMaxItems], sumT = 0, minKc = INT64_MAX;
     for (int i = 0; i < n; ++i) {
         T[i] = it[i].w->shape.tiles;
         Kc[i] = it[i].w->shape.chunks * (it[i].w_up ? 2 : 1);  // a paired tile is two tiles' units
-        q[i] = 1;
+        q[i] = qs[i] = 1;
         sumT += T[i];
         if (Kc[i] < minKc) minKc = Kc[i];
     }
@@ -982,11 +1066,28 @@ int pick_split(const HostItem* it, int n, const int* maxq, int cmax, MmaParams* 
             best_c = c;
         }
     }
+    bool sk = false;
+    if (sk_margin >= 0) {
+        auto cost_sk = [&](int i) { return (T[i] * Kc[i] + qs[i] - 1) / qs[i]; };
+        for (int64_t used = n; used < g_sm_count; ++used) {
+            int bi = -1;
+            for (int i = 0; i < n; ++i)
+                if (qs[i] < T[i] * Kc[i] && (bi < 0 || cost_sk(i) > cost_sk(bi))) bi = i;
+            if (bi < 0) break;
+            ++qs[bi];
+        }
+        int64_t cost = 0;
+        for (int i = 0; i < n; ++i) cost = cost_sk(i) > cost ? cost_sk(i) : cost;
+        if (cost + sk_margin < best) {
+            sk = true;
+            best_c = 1;
+        }
+    }
     p->C = best_c;
     p->n_items = n;
     int cl = 0;
     for (int i = 0; i < n; ++i) {
-        const int64_t qi = best_c == 1 ? q[i] : T[i];
+        const int64_t qi = sk ? qs[i] : best_c == 1 ? q[i] : T[i];
         MmaItem& m = p->it[i];
         m.w = it[i].w->dev;
         m.x = it[i].x;
@@ -996,8 +1097,10 @@ int pick_split(const HostItem* it, int n, const int* maxq, int cmax, MmaParams* 
         m.chunks = (int)it[i].w->shape.chunks;
         m.M = (int)it[i].M;
         m.cluster0 = cl;
-        m.tile_base = (int)(T[i] / qi);
-        m.tile_rem = (int)(T[i] % qi);
+        const int64_t units = sk ? T[i] * Kc[i] : T[i];
+        m.gran = sk ? 1 : (int)Kc[i];
+        m.ub = best_c == 1 ? (int)(units / qi) : 0;
+        m.ur = best_c == 1 ? (int)(units % qi) : 0;
         m.w_up = it[i].w_up ? it[i].w_up->dev : nullptr;
         m.res = it[i].res;
         cl += (int)qi;
@@ -1014,7 +1117,21 @@ int launch(const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st)
         if (it[i].w->shape.tile_chunk_bytes != Cf::WB)
             return fail(NXQ_ERR_SHAPE, "mma_gemv: tile-chunk of %lld bytes, kernel stage %d",
                         (long long)it[i].w->shape.tile_chunk_bytes, Cf::WB);
-    const int clusters = pick_split(it, n, max_clusters<TYPE, MT>(), Cf::CMAX, &p);
+    // Stream-K partials: a slot of up to two result sets of 32 tokens per CTA,
+    // one counter per CTA; sized once for every variant.  While the stream
+    // is captured into a graph and its scratch is still too small, the launch
+    // splits by whole tiles or clusters instead.
+    StreamScratch* sc = nullptr;
+    if (g_streamk) {
+        const size_t slots = (size_t)g_sm_count * 2 * kMaxMT * TILE_ROWS;
+        if (int rc = scratch_try(st, slots, (size_t)g_sm_count, &sc)) return rc;
+    }
+    // Measured (Q4_K, Q3_K, 4096 - 16384 rows): stream-K pays when it takes
+    // more than 2 units off the busiest CTA at 8 tokens, 1 at 16, any at 32.
+    const int margin = sc == nullptr ? -1 : MT == 8 ? 2 : MT == 16 ? 1 : 0;
+    const int clusters = pick_split(it, n, max_clusters<TYPE, MT>(), Cf::CMAX, margin, &p);
+    p.part = sc ? sc->ws : nullptr;
+    p.cnt = sc ? sc->counters : nullptr;
     p.x_dtype = x_dtype;
     p.y_dtype = y_dtype;
     p.status = context_status();
@@ -1082,6 +1199,8 @@ int launch_items(int type, int mt, const HostItem* it, int n, int x_dtype, int y
 int mma_init(int) {
     const char* env = getenv("NXQ_DECODE_KERNEL");
     g_mma_enabled = !(env && env[0] && env[0] != 'm');  // "tc" / "simt" select another decode kernel
+    const char* split = getenv("NXQ_GEMV_SPLIT");
+    g_streamk = !(split && strcmp(split, "tiles") == 0);
     g_sm_count = context_sm_count();
     int rc;
 #define NXQ_ATTR(T)                                       \
@@ -1143,10 +1262,10 @@ int mma_qmatmul_swiglu(const Weight* wg, const Weight* wu, const void* x, int x_
     const TiledShape& su = wu->shape;
     const bool aligned = ((uintptr_t)x % 16) == 0;
     const bool direct = aligned && (x_dtype == NXQ_F16 || (M <= 2 && (x_dtype == NXQ_F32 || x_dtype == NXQ_BF16)));
-    // Pairing keeps one CTA per tile pair (no K split): worth it only when the
-    // weight has tiles for at least half the SMs.
+    // Pairing has no cluster split: without stream-K it is worth it only when
+    // the weight has tiles for at least half the SMs.
     if (!mma_supported(s, M) || !direct || su.type != s.type || su.N != s.N || su.K != s.K ||
-        s.tiles * 2 < g_sm_count)
+        (!g_streamk && s.tiles * 2 < g_sm_count))
         return NXQ_ERR_UNSUPPORTED;
     const int mt = M <= 8 ? 8 : M <= 16 ? 16 : 32;
     HostItem item{wg, x, h, M};

@@ -90,6 +90,27 @@ int scratch_for(cudaStream_t st, size_t ws_floats, size_t n_counters, size_t xh_
     return NXQ_OK;
 }
 
+void scratch_reset_counters() {
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    for (auto& e : g_scratch)
+        if (e.counters) cudaMemset(e.counters, 0, e.n_counters * sizeof(unsigned));
+    cudaDeviceSynchronize();
+}
+
+int scratch_try(cudaStream_t st, size_t ws_floats, size_t n_counters, StreamScratch** out) {
+    *out = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_scratch_mu);
+        for (auto& e : g_scratch)
+            if (e.st == st && e.ws_floats >= ws_floats && e.n_counters >= n_counters) {
+                *out = &e;
+                return NXQ_OK;
+            }
+    }
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone) return NXQ_OK;
+    return scratch_for(st, ws_floats, n_counters, 0, out);
+}
 
 namespace {
 

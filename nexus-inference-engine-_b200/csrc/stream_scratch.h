@@ -28,6 +28,14 @@ struct StreamScratch {
 int scratch_for(cudaStream_t st, size_t ws_floats, size_t n_counters, size_t xh_elems, StreamScratch** out,
                 size_t epi_floats = 0);
 
+// Zeroes every stream's tile counters: after a kernel gave up a bounded wait,
+// counts it left behind must not carry into the next launch (device idle).
+void scratch_reset_counters();
+
+// As scratch_for, except that a scratch which would have to grow while `st` is
+// being captured is not an error: *out is then null and nothing is recorded.
+int scratch_try(cudaStream_t st, size_t ws_floats, size_t n_counters, StreamScratch** out);
+
 // out[i] = (half)x[i] for an f32/bf16/f16 array of n elements.
 cudaError_t launch_to_half(const void* x, int dtype, __half* out, int64_t n, cudaStream_t st);
 

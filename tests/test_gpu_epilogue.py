@@ -1,9 +1,10 @@
 """GPU: the fused epilogues against the oracle.
 
 nxq_qmatmul_swiglu: h = silu(x Wg^T) * (x Wu^T), silu(g) = g / (1 + exp(-g)),
-with the oracle's fp32 products combined in float64; one launch when the weight
-has tiles for half the SMs (each CTA takes a tile of gate and up), otherwise
-gate/up then a small kernel (few tiles, prefill batch sizes).
+with the oracle's fp32 products combined in float64; one launch for decode
+batch sizes (a row tile's gate and up units in one run, tiles shared between
+CTAs finished by one of them), otherwise gate/up then a small kernel (prefill
+batch sizes).
 nxq_qmatmul_residual: y = x W^T + res, fused into the decode kernel's store,
 after the product otherwise; in place (y is the residual buffer) and not.
 Tolerance: rel-L2 <= 1e-3 (the parity bar) for fp32 outputs.  A bf16 output
@@ -45,9 +46,9 @@ def _pair(gpu, t, N, K, seed):
 
 @pytest.mark.parametrize("t", [12, 11, 8], ids=lambda t: NAMES[t])
 @pytest.mark.parametrize("M", [1, 4, 16, 32])
-def test_swiglu_fused_one_launch(gpu, t, M):
+@pytest.mark.parametrize("N,K", [(9728, 512), (1024, 2048)])
+def test_swiglu_fused_one_launch(gpu, t, M, N, K):
     torch = _torch()
-    N, K = 9728, 512  # 76 tiles: the paired path
     bg, bu, wg, wu = _pair(gpu, t, N, K, seed=40 + M)
     try:
         x = torch.from_numpy(synth.make_activations(M, K, seed=M)).cuda()
@@ -100,6 +101,25 @@ def test_residual(gpu, t, M, inplace):
         y = gpu.qmatmul_residual(w, x, res, out=res if inplace else None)
         torch.cuda.synchronize()
         want = loader.qmatmul(t, b, N, K, x.float().cpu().numpy()).astype(np.float64) + res0
+        assert synth.rel_l2(y.cpu().numpy(), want) < TOL
+    finally:
+        w.release()
+
+
+@pytest.mark.parametrize("M", [1, 8, 32])
+def test_residual_shared_tiles(gpu, M):
+    """A weight with more row tiles than SMs: tiles shared between CTAs get the
+    residual once, from the CTA that finishes them."""
+    torch = _torch()
+    t, N, K = 12, 14336, 4096
+    b = synth.make_blocks(t, N, K, seed=95)
+    w = gpu.Weight.register(b, t, N, K)
+    try:
+        x = torch.from_numpy(synth.make_activations(M, K, seed=M)).cuda()
+        res = torch.from_numpy(synth.make_activations(M, N, seed=600 + M).astype(np.float32)).cuda()
+        want = loader.qmatmul(t, b, N, K, x.float().cpu().numpy()).astype(np.float64) + res.cpu().numpy()
+        y = gpu.qmatmul_residual(w, x, res)
+        torch.cuda.synchronize()
         assert synth.rel_l2(y.cpu().numpy(), want) < TOL
     finally:
         w.release()

@@ -5,7 +5,10 @@ Cases: projections sharing one input (q/k/v style), many experts with their
 own inputs and batch sizes (more than one launch's 16 weights, an expert with
 M = 0), and the inputs that run item by item instead (mixed block types,
 prefill batch sizes, fp32 activations with M > 2).  Also checks that a group
-of one block type runs as one launch per 16 weights."""
+of one block type runs as one launch per 16 weights, and that weights with
+more tiles than the GPU has SMs (runs of tile-chunks that cross tiles, tiles
+finished by the last of the CTAs that share them) give the same bits on every
+call."""
 from __future__ import annotations
 
 import numpy as np
@@ -48,6 +51,29 @@ def test_shared_input_projections(gpu, t, M):
             want = loader.qmatmul(t, b, N, K, xf)
             assert synth.rel_l2(y.cpu().numpy(), want) < TOL
             assert synth.rel_l2(y.cpu().numpy(), s.cpu().numpy()) < 1e-5
+    finally:
+        for w in ws:
+            w.release()
+
+
+@pytest.mark.parametrize("t", [12, 8], ids=lambda t: NAMES[t])
+@pytest.mark.parametrize("M", [1, 5, 32])
+def test_large_group_shared_tiles(gpu, t, M):
+    torch = _torch()
+    K = 2048
+    shapes = [(9728, K), (9728, K), (1024, K)]  # 160 tiles: no cluster split fits
+    blocks, ws = _weights(gpu, t, shapes, seed=400 + M)
+    try:
+        x = torch.from_numpy(synth.make_activations(M, K, seed=M)).cuda()
+        ys = gpu.qmatmul_grouped(ws, [x] * 3)
+        torch.cuda.synchronize()
+        xf = x.float().cpu().numpy()
+        for (N, _), b, y in zip(shapes, blocks, ys):
+            assert synth.rel_l2(y.cpu().numpy(), loader.qmatmul(t, b, N, K, xf)) < TOL
+        for _ in range(3):
+            again = gpu.qmatmul_grouped(ws, [x] * 3)
+            torch.cuda.synchronize()
+            assert all(torch.equal(a, b) for a, b in zip(ys, again))
     finally:
         for w in ws:
             w.release()
