@@ -29,7 +29,8 @@ _ref: Optional[ctypes.CDLL] = None
 def build(ref: bool = True) -> None:
     """make -C oracle port [ref]; the ref target only where the reference exists."""
     targets = ["port"]
-    if ref and Path(os.environ.get("NXQ_REFERENCE", "/root/reference/nexus"), "src").exists():
+    default_ref = HERE.parent.parent / "reference" / "nexus"  # the checkout beside this repository
+    if ref and Path(os.environ.get("NXQ_REFERENCE", str(default_ref)), "src").exists():
         targets.append("ref")
     env = dict(os.environ)
     if "NXQ_REFERENCE" in os.environ:
