@@ -65,6 +65,31 @@ def test_qmm_golden_matrix(gpu, t):
         w.release()
 
 
+@pytest.mark.parametrize("M", [1, 5, 32, 40])
+def test_host_call_output_buffers(gpu, M):
+    """nxq_qmatmul_host into pageable memory, pinned memory and a view at an
+    offset inside a larger pinned allocation: the same values, within the
+    parity bar, and nothing written outside the view."""
+    torch = _torch()
+    t, N, K = 12, 1536, 2048
+    blocks = synth.make_blocks(t, N, K, seed=70 + M)
+    w = gpu.Weight.register(blocks, t, N, K)
+    try:
+        x = synth.make_activations(M, K, seed=M).astype(np.float32)
+        want = loader.qmatmul(t, blocks, N, K, x)
+        pageable = gpu.qmatmul_host(w, x)
+        pinned = torch.full((M, N), float("nan")).pin_memory().numpy()
+        gpu.qmatmul_host(w, x, out=pinned)
+        big = torch.full((M * N + 96,), float("nan")).pin_memory().numpy()
+        view = big[32:32 + M * N].reshape(M, N)
+        gpu.qmatmul_host(w, x, out=view)
+        assert synth.rel_l2(pageable, want) < TOL
+        assert np.array_equal(pinned, pageable) and np.array_equal(view, pageable)
+        assert np.isnan(big[:32]).all() and np.isnan(big[32 + M * N:]).all()
+    finally:
+        w.release()
+
+
 @pytest.mark.parametrize("t", ALL_TYPES, ids=lambda t: NAMES[t])
 @pytest.mark.parametrize("M", [1, 2, 3, 4, 7, 8, 16, 31, 32])
 def test_qmm_batch_sizes(gpu, t, M):
