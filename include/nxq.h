@@ -180,7 +180,11 @@ NXQ_API int nxq_dequant(nxq_weight_t w, float* y_dev, void* stream);
  * x_dtype, y_dtype in nxq_dtype.  Device-resident form of
  * MetalBackend::gemm_int4_gpu (metal_backend.h:86-87) with M honoured and the
  * block codec taken from the weight.  M >= 1; any M is accepted (decode and
- * prefill shapes share this entry point). */
+ * prefill shapes share this entry point).  The first call on a stream
+ * allocates that stream's scratch (partial sums of row tiles shared between
+ * CTAs, an f16 copy of non-f16 activations); a call captured into a CUDA
+ * graph cannot allocate, so make one call of the largest shape on the stream
+ * before capturing (the decode GEMV then splits without scratch, slower). */
 NXQ_API int nxq_qmatmul(nxq_weight_t w, const void* x_dev, int x_dtype, void* y_dev,
                         int y_dtype, int64_t M, void* stream);
 
