@@ -65,6 +65,37 @@ def test_qmm_golden_matrix(gpu, t):
         w.release()
 
 
+def test_graph_capture_on_a_fresh_stream(gpu):
+    """A decode call captured into a CUDA graph on a stream that has no
+    scratch yet runs with a split that needs none; the same call outside the
+    capture (the stream's scratch allocated, stream-K) agrees."""
+    torch = _torch()
+    t, N, K, M = 12, 9728, 2048, 4  # 76 row tiles x 8 chunks: stream-K when it can
+    blocks = synth.make_blocks(t, N, K, seed=5)
+    w = gpu.Weight.register(blocks, t, N, K)
+    try:
+        x = torch.from_numpy(synth.make_activations(M, K, seed=3)).cuda()
+        y = torch.empty(M, N, device="cuda")
+        s = torch.cuda.Stream()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            gpu.qmatmul(w, x, out=y, stream=s)
+        with torch.cuda.stream(s):
+            g.replay()
+        torch.cuda.synchronize()
+        want = loader.qmatmul(t, blocks, N, K, x.float().cpu().numpy())
+        assert synth.rel_l2(y.cpu().numpy(), want) < TOL
+        y2 = torch.empty(M, N, device="cuda")
+        gpu.qmatmul(w, x, out=y2, stream=s)
+        torch.cuda.synchronize()
+        gpu.stream_sync(s)
+        assert synth.rel_l2(y2.cpu().numpy(), want) < TOL
+        assert synth.rel_l2(y2.cpu().numpy(), y.cpu().numpy()) < 1e-5
+        del g
+    finally:
+        w.release()
+
+
 @pytest.mark.parametrize("M", [1, 5, 32, 40])
 def test_host_call_output_buffers(gpu, M):
     """nxq_qmatmul_host into pageable memory, pinned memory and a view at an
