@@ -2,8 +2,9 @@
 //
 // Replaces the reference's Metal decode GEMV (gemv_int4_nr8.metal:31-87,
 // gemv_q3k.metal:33-98; dispatched by ComputeDispatch::gemm_int4 ->
-// MetalBackend::gemv_int4_nr8, metal_backend.mm:607-642) for Q4_0, Q8_0,
-// Q4_K and Q3_K.
+// MetalBackend::gemv_int4_nr8, metal_backend.mm:607-642) for every GGUF
+// block type of the reference (Q4_0, Q4_1, Q8_0, Q2_K .. Q6_K) and the NXF
+// INT4 group format.
 //
 // Why mma.sync and not tcgen05 here: a tcgen05.mma with M=128, K=16 costs
 // ~60 cycles for any N <= 128 (measured on this B200), so feeding dequantized
@@ -23,11 +24,14 @@
 //
 // Decomposition: the weight is stored tiled (formats.cuh: 128-row tiles x
 // 256-k chunks, each tile-chunk contiguous, a tile's chunks in order).  A
-// unit is one tile-chunk, one bulk copy.  One CTA per SM; cluster q of Q owns
-// a contiguous range of tiles, and the C CTAs of a cluster split K, their
-// partial sums meeting in the leader's shared memory.  (Measured: cutting the
-// rows finer than tiles, so that every SM gets the same share, was slower -
-// a unit that straddles two tiles costs more than the balance gains.)
+// unit is one tile-chunk, one bulk copy.  One CTA per SM, each taking a run
+// of consecutive units: whole tiles, a run that crosses tile boundaries
+// (stream-K; a tile shared by several CTAs is finished by the one holding its
+// first units, from the others' partial sums in global memory), or, in a
+// cluster of C CTAs, 1/C of one tile's chunks (partial sums meeting in the
+// leader's shared memory).  (Measured: cutting the rows finer than tiles, so
+// that every SM gets the same share, was slower - a unit that straddles two
+// tiles costs more than the balance gains.)
 //
 // Per consumer group, 8 warps; warp w owns rows 16w..16w+15 of the tile.  Lane
 // (g, t) (g = lane/4, t = lane%4) holds rows 16w+g and 16w+8+g, and the mma's
