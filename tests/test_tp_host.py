@@ -1,4 +1,4 @@
-"""CPU, world_size 2 over gloo: the tensor-parallel decomposition.
+"""CPU, world_size 2 and 4 over gloo: the tensor-parallel decomposition.
 
 Each rank slices its shard with the library's host-only nxq_shard_extract,
 computes its partial output with the CPU oracle, and the ranks combine them
@@ -73,11 +73,12 @@ def _worker(rank, world, port, t, N, K, M, q):
 
 
 @pytest.mark.parametrize("t", [11, 12])
-def test_tp_decomposition_matches_full(t):
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_decomposition_matches_full(t, world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    world, N, K, M = 2, 256, 2048, 3
+    N, K, M = 128 * world, 2048, 3
     procs = [ctx.Process(target=_worker, args=(r, world, port, t, N, K, M, q)) for r in range(world)]
     for p in procs:
         p.start()
