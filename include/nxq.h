@@ -52,7 +52,7 @@ typedef enum {
     NXQ_ERR_STATE = -7,       /* not initialised / wrong device / TP not set up */
     NXQ_ERR_NCCL = -8,        /* NCCL unavailable or a collective failed       */
     NXQ_ERR_UNSUPPORTED = -9, /* no GPU of the required architecture           */
-    NXQ_ERR_FORMAT = -10      /* a file that is not GGUF v2/v3 or is truncated */
+    NXQ_ERR_FORMAT = -10      /* a GGUF / NXF file that is malformed or truncated */
 } nxq_status;
 
 /* Block types: the GGUF type ids of nexus/src/import/gguf_importer.h:28-57,
@@ -347,6 +347,64 @@ NXQ_API int nxq_gguf_register(nxq_gguf_t g, int64_t i, int64_t slice, nxq_weight
  * (nxq_weight_register_shard rules). */
 NXQ_API int nxq_gguf_register_shard(nxq_gguf_t g, int64_t i, int64_t slice, int split, int rank,
                                     int world, nxq_weight_t* out);
+
+/* ---- residency loader: NXF files ------------------------------------------
+ * Replaces the reference's NXF read path (NXFReader::open / get_tensor /
+ * map_chunk, format/nxf_reader.cpp:166-258 and 295-409; layouts in
+ * format/nxf.h:27-51), which maps chunks for the engine to stream at every
+ * call: a 64-byte header (magic "NXF1", version 1, manifest and tensor-index
+ * offsets and sizes, total file size), a flat JSON manifest, and a tensor
+ * index of name, shape (shape[0] fastest, as GGUF dims), dtype and 24-byte
+ * chunk descriptors (file offset, stored and decoded size, xxHash32 of the
+ * stored bytes, codec, group size).  The file is mapped read-only and every
+ * field is bounds-checked; registration checks each chunk's xxHash32 (the
+ * reference stores it but never checks it) and builds the tiled HBM copy.
+ * Registered codecs (Codec, core/config.h:21-36): INT4 = 4 - a chunk is
+ * [4-bit codes in NXQ_INT4_ROWS order][fp32 scales][fp32 zeros] per group of
+ * the descriptor's group size (32, 64, 128), as GGUFImporter writes it
+ * (import/gguf_importer.cpp:1144-1170) - and the GGUF-block passthroughs
+ * Q3K = 11, Q4K = 12, Q2K = 13.  Parsing needs no GPU; registration needs
+ * nxq_init.  A malformed or truncated file, or a checksum mismatch, is
+ * NXQ_ERR_FORMAT; another codec is NXQ_ERR_CODEC. */
+typedef struct nxq_nxf_s* nxq_nxf_t;
+
+NXQ_API int nxq_nxf_open(const char* path, nxq_nxf_t* out);
+NXQ_API int nxq_nxf_close(nxq_nxf_t f);
+NXQ_API int nxq_nxf_tensor_count(nxq_nxf_t f, int64_t* n);
+
+/* Tensor i, in file order: name (NUL-terminated, truncated to name_len),
+ * dtype, dims (up to 4, unused ones 1), chunk count, the first chunk's codec
+ * and group size, and the stored bytes of all chunks. */
+NXQ_API int nxq_nxf_tensor_info(nxq_nxf_t f, int64_t i, char* name, size_t name_len, int* dtype,
+                                int* n_dims, int64_t dims[4], int64_t* n_chunks, int* codec,
+                                int* group_size, uint64_t* bytes);
+NXQ_API int nxq_nxf_chunk_info(nxq_nxf_t f, int64_t i, int64_t c, uint64_t* offset,
+                               uint32_t* stored, uint32_t* decoded, uint32_t* checksum,
+                               int* codec, int* group_size);
+
+/* Index of the tensor called `name`; NXQ_ERR_ARG if there is none. */
+NXQ_API int nxq_nxf_find(nxq_nxf_t f, const char* name, int64_t* index);
+
+/* Checks tensor i's chunks (one codec and group size, no entropy coding,
+ * xxHash32 as stored) without registering it. */
+NXQ_API int nxq_nxf_verify(nxq_nxf_t f, int64_t i);
+
+/* xxHash32 (seed 0) of n bytes, the checksum NXF chunk descriptors carry. */
+NXQ_API int nxq_nxf_xxh32(const void* data, size_t n, uint32_t* out);
+
+/* The manifest's JSON text (NUL-terminated, truncated to n; *size = its
+ * length), and the value of a key as a number or a string. */
+NXQ_API int nxq_nxf_manifest(nxq_nxf_t f, char* buf, size_t n, uint64_t* size);
+NXQ_API int nxq_nxf_manifest_number(nxq_nxf_t f, const char* key, double* v);
+NXQ_API int nxq_nxf_manifest_string(nxq_nxf_t f, const char* key, char* buf, size_t n);
+
+/* Register tensor i as a weight [N][K]: K = dims[0], N = dims[1]; for a
+ * 3-D tensor [E][N][K] (stacked experts) `slice` picks one, else pass 0.  The
+ * _shard form registers this rank's tensor-parallel shard
+ * (nxq_weight_register_shard rules; block passthrough codecs only). */
+NXQ_API int nxq_nxf_register(nxq_nxf_t f, int64_t i, int64_t slice, nxq_weight_t* out);
+NXQ_API int nxq_nxf_register_shard(nxq_nxf_t f, int64_t i, int64_t slice, int split, int rank,
+                                   int world, nxq_weight_t* out);
 
 #ifdef __cplusplus
 }

@@ -21,7 +21,7 @@ __all__ = [
     "NxqError", "lib", "init", "shutdown", "Weight", "qmatmul", "qmatmul_host", "stream_sync",
     "kernel_name", "launch_count",
     "TYPES", "GEOMETRY", "F32", "F16", "BF16", "SPLIT_COL", "SPLIT_ROW", "declared_symbols",
-    "tp_unique_id", "tp_init", "tp_shutdown", "tp_qmatmul", "tp_allreduce_f32", "GGUF", "qmatmul_grouped", "qmatmul_swiglu", "qmatmul_residual", "rmsnorm_qmatmul", "int4_pack", "INT4_ROWS", "INT4_KMAJOR",
+    "tp_unique_id", "tp_init", "tp_shutdown", "tp_qmatmul", "tp_allreduce_f32", "GGUF", "NXF", "xxh32", "qmatmul_grouped", "qmatmul_swiglu", "qmatmul_residual", "rmsnorm_qmatmul", "int4_pack", "INT4_ROWS", "INT4_KMAJOR",
 ]
 
 LIB_PATH = Path(__file__).with_name("libnxq.so")
@@ -117,6 +117,24 @@ _SIGS = {
     "nxq_gguf_register": [_c.c_void_p, _c.c_int64, _c.c_int64, _c.POINTER(_c.c_void_p)],
     "nxq_gguf_register_shard": [_c.c_void_p, _c.c_int64, _c.c_int64, _c.c_int, _c.c_int, _c.c_int,
                                 _c.POINTER(_c.c_void_p)],
+    "nxq_nxf_open": [_c.c_char_p, _c.POINTER(_c.c_void_p)],
+    "nxq_nxf_close": [_c.c_void_p],
+    "nxq_nxf_tensor_count": [_c.c_void_p, _c.POINTER(_c.c_int64)],
+    "nxq_nxf_tensor_info": [_c.c_void_p, _c.c_int64, _c.c_char_p, _c.c_size_t, _c.POINTER(_c.c_int),
+                            _c.POINTER(_c.c_int), _c.POINTER(_c.c_int64), _c.POINTER(_c.c_int64),
+                            _c.POINTER(_c.c_int), _c.POINTER(_c.c_int), _c.POINTER(_c.c_uint64)],
+    "nxq_nxf_chunk_info": [_c.c_void_p, _c.c_int64, _c.c_int64, _c.POINTER(_c.c_uint64), _c.POINTER(_c.c_uint32),
+                           _c.POINTER(_c.c_uint32), _c.POINTER(_c.c_uint32), _c.POINTER(_c.c_int),
+                           _c.POINTER(_c.c_int)],
+    "nxq_nxf_find": [_c.c_void_p, _c.c_char_p, _c.POINTER(_c.c_int64)],
+    "nxq_nxf_verify": [_c.c_void_p, _c.c_int64],
+    "nxq_nxf_xxh32": [_c.c_void_p, _c.c_size_t, _c.POINTER(_c.c_uint32)],
+    "nxq_nxf_manifest": [_c.c_void_p, _c.c_char_p, _c.c_size_t, _c.POINTER(_c.c_uint64)],
+    "nxq_nxf_manifest_number": [_c.c_void_p, _c.c_char_p, _c.POINTER(_c.c_double)],
+    "nxq_nxf_manifest_string": [_c.c_void_p, _c.c_char_p, _c.c_char_p, _c.c_size_t],
+    "nxq_nxf_register": [_c.c_void_p, _c.c_int64, _c.c_int64, _c.POINTER(_c.c_void_p)],
+    "nxq_nxf_register_shard": [_c.c_void_p, _c.c_int64, _c.c_int64, _c.c_int, _c.c_int, _c.c_int,
+                               _c.POINTER(_c.c_void_p)],
 }
 
 
@@ -502,6 +520,123 @@ class GGUF:
         _check(lib().nxq_gguf_register_shard(self.handle, i, slice_, split, rank, world, ctypes.byref(h)))
         N, K = info["dims"][1], info["dims"][0]
         return Weight(h.value, info["type"], N // world if split == SPLIT_COL else N,
+                      K // world if split == SPLIT_ROW else K)
+
+
+# ---- residency loader: NXF files ----------------------------------------------
+
+# NXF chunk codecs (Codec, core/config.h) that register as weights, and the
+# block type each becomes (INT4: the NXF INT4 group type of the chunk's group size).
+NXF_CODEC_INT4, NXF_CODEC_Q3K, NXF_CODEC_Q4K, NXF_CODEC_Q2K = 4, 11, 12, 13
+
+
+def xxh32(data) -> int:
+    """xxHash32 (seed 0) of a bytes-like object: the NXF chunk checksum."""
+    buf = np.ascontiguousarray(np.frombuffer(bytes(data), dtype=np.uint8))
+    v = ctypes.c_uint32()
+    _check(lib().nxq_nxf_xxh32(buf.ctypes.data if buf.size else None, buf.size, ctypes.byref(v)))
+    return v.value
+
+
+class NXF:
+    """An NXF file opened by the library's loader (mapped read-only; header,
+    manifest and tensor index parsed and bounds-checked on the host, no GPU
+    needed).  Use as a context manager or call close()."""
+
+    def __init__(self, path):
+        h = ctypes.c_void_p()
+        _check(lib().nxq_nxf_open(str(path).encode(), ctypes.byref(h)))
+        self._h = h
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        if self._h is None:
+            raise NxqError(-1, "NXF file already closed")
+        return self._h
+
+    def close(self) -> None:
+        if self._h is not None:
+            _check(lib().nxq_nxf_close(self._h))
+            self._h = None
+
+    def __enter__(self) -> "NXF":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
+    def tensors(self) -> list[dict]:
+        n = ctypes.c_int64()
+        _check(lib().nxq_nxf_tensor_count(self.handle, ctypes.byref(n)))
+        return [self.tensor_info(i) for i in range(n.value)]
+
+    def tensor_info(self, i: int) -> dict:
+        name = ctypes.create_string_buffer(512)
+        dt, nd, codec, gs = ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        dims = (ctypes.c_int64 * 4)()
+        nc, nb = ctypes.c_int64(), ctypes.c_uint64()
+        _check(lib().nxq_nxf_tensor_info(self.handle, i, name, 512, ctypes.byref(dt), ctypes.byref(nd), dims,
+                                         ctypes.byref(nc), ctypes.byref(codec), ctypes.byref(gs), ctypes.byref(nb)))
+        return {"name": name.value.decode(), "dtype": dt.value, "dims": list(dims)[:nd.value],
+                "chunks": nc.value, "codec": codec.value, "group_size": gs.value, "bytes": nb.value}
+
+    def chunk_info(self, i: int, c: int) -> dict:
+        off, st, de, cs = ctypes.c_uint64(), ctypes.c_uint32(), ctypes.c_uint32(), ctypes.c_uint32()
+        codec, gs = ctypes.c_int(), ctypes.c_int()
+        _check(lib().nxq_nxf_chunk_info(self.handle, i, c, ctypes.byref(off), ctypes.byref(st), ctypes.byref(de),
+                                        ctypes.byref(cs), ctypes.byref(codec), ctypes.byref(gs)))
+        return {"offset": off.value, "stored": st.value, "decoded": de.value, "checksum": cs.value,
+                "codec": codec.value, "group_size": gs.value}
+
+    def find(self, name: str) -> int:
+        i = ctypes.c_int64()
+        _check(lib().nxq_nxf_find(self.handle, name.encode(), ctypes.byref(i)))
+        return i.value
+
+    def verify(self, name_or_index) -> None:
+        i = self.find(name_or_index) if isinstance(name_or_index, str) else int(name_or_index)
+        _check(lib().nxq_nxf_verify(self.handle, i))
+
+    def manifest(self) -> str:
+        n = ctypes.c_uint64()
+        _check(lib().nxq_nxf_manifest(self.handle, None, 0, ctypes.byref(n)))
+        buf = ctypes.create_string_buffer(n.value + 1)
+        _check(lib().nxq_nxf_manifest(self.handle, buf, n.value + 1, None))
+        return buf.value.decode()
+
+    def manifest_number(self, key: str) -> float:
+        v = ctypes.c_double()
+        _check(lib().nxq_nxf_manifest_number(self.handle, key.encode(), ctypes.byref(v)))
+        return v.value
+
+    def manifest_string(self, key: str, n: int = 4096) -> str:
+        buf = ctypes.create_string_buffer(n)
+        _check(lib().nxq_nxf_manifest_string(self.handle, key.encode(), buf, n))
+        return buf.value.decode()
+
+    @staticmethod
+    def _type(info: dict) -> int:
+        c = info["codec"]
+        if c == NXF_CODEC_INT4:
+            return 100 + info["group_size"] // 32
+        return {NXF_CODEC_Q3K: TYPES["Q3_K"], NXF_CODEC_Q4K: TYPES["Q4_K"], NXF_CODEC_Q2K: TYPES["Q2_K"]}.get(c, -1)
+
+    def register(self, name_or_index, slice_: int = 0) -> "Weight":
+        """Upload tensor [N][K] (slice `slice_` of a 3-D tensor) as a weight,
+        after checking every chunk's xxHash32."""
+        i = self.find(name_or_index) if isinstance(name_or_index, str) else int(name_or_index)
+        info = self.tensor_info(i)
+        h = ctypes.c_void_p()
+        _check(lib().nxq_nxf_register(self.handle, i, slice_, ctypes.byref(h)))
+        return Weight(h.value, self._type(info), info["dims"][1], info["dims"][0])
+
+    def register_shard(self, name_or_index, split: int, rank: int, world: int, slice_: int = 0) -> "Weight":
+        i = self.find(name_or_index) if isinstance(name_or_index, str) else int(name_or_index)
+        info = self.tensor_info(i)
+        h = ctypes.c_void_p()
+        _check(lib().nxq_nxf_register_shard(self.handle, i, slice_, split, rank, world, ctypes.byref(h)))
+        N, K = info["dims"][1], info["dims"][0]
+        return Weight(h.value, self._type(info), N // world if split == SPLIT_COL else N,
                       K // world if split == SPLIT_ROW else K)
 
 

@@ -48,4 +48,42 @@ void ref_dequant_int4(float* out, const uint8_t* data, const float* scales, cons
 // The reference's fp16 -> fp32 conversion (gguf_importer.cpp:202-237).
 float ref_fp16_to_fp32(uint16_t h) { return nexus::import::fp16_to_fp32(h); }
 
+// The reference's own NXF writer (format/nxf_writer.cpp: create, set_manifest,
+// begin_tensor, add_chunk, end_tensor, finalize), so that tests read files
+// made by the reference itself.  ref_nxf_finish finalizes and frees the writer.
+void* ref_nxf_create(const char* path) { return nexus::format::NXFWriter::create(path).release(); }
+
+void ref_nxf_manifest(void* w, const char* architecture, const char* name, uint32_t num_layers,
+                      uint32_t hidden_dim, float rope_theta, float rms_norm_eps, uint32_t default_codec,
+                      uint32_t default_group_size) {
+    nexus::format::ModelManifest m{};
+    m.architecture = architecture;
+    m.name = name;
+    m.num_layers = num_layers;
+    m.hidden_dim = hidden_dim;
+    m.rope_theta = rope_theta;
+    m.rms_norm_eps = rms_norm_eps;
+    m.default_codec = static_cast<nexus::Codec>(default_codec);
+    m.default_group_size = static_cast<uint8_t>(default_group_size);
+    static_cast<nexus::format::NXFWriter*>(w)->set_manifest(m);
+}
+
+void ref_nxf_begin(void* w, const char* name, int ndim, const int64_t* shape, int dtype) {
+    static_cast<nexus::format::NXFWriter*>(w)->begin_tensor(
+        name, std::vector<int64_t>(shape, shape + ndim), static_cast<nexus::DType>(dtype));
+}
+
+void ref_nxf_chunk(void* w, const void* data, size_t size, int codec, int group_size) {
+    static_cast<nexus::format::NXFWriter*>(w)->add_chunk(data, size, static_cast<nexus::Codec>(codec),
+                                                         static_cast<uint8_t>(group_size));
+}
+
+void ref_nxf_end(void* w) { static_cast<nexus::format::NXFWriter*>(w)->end_tensor(); }
+
+void ref_nxf_finish(void* w) {
+    auto* writer = static_cast<nexus::format::NXFWriter*>(w);
+    writer->finalize();
+    delete writer;
+}
+
 }  // extern "C"
