@@ -73,6 +73,29 @@ def test_matrix_fixture_through_oracle(gs):
     assert np.array_equal(y, g[f"g{gs}_mat_y"])
 
 
+def test_gemm_int4_scaleless_weights_map_to_groups():
+    """The reference's gemm_int4 weights (gemv_int4_nr8.metal:31-80: [K/2][N]
+    bytes, byte (k/2)*N + n holding k low and k+1 high, w = (q - 8) * 0.125,
+    no scales) are NXF INT4 groups in the K-major order with every scale 0.125
+    and every zero 8: the same bits, and the same product as the shader's
+    formula."""
+    rng = np.random.default_rng(11)
+    N, K, gs = 48, 256, 128
+    km = rng.integers(0, 256, (K // 2, N), dtype=np.uint8)
+    q = np.empty((N, K), np.float32)
+    q[:, 0::2] = (km & 15).T
+    q[:, 1::2] = (km >> 4).T
+    w_shader = (q - 8.0) * 0.125
+    blocks = nxq.int4_pack(km, np.full((K // gs, N), 0.125, np.float32), np.full((K // gs, N), 8.0, np.float32),
+                           N, K, gs, nxq.INT4_KMAJOR)
+    t = 100 + gs // 32
+    assert loader.same_bits(loader.dequant(t, blocks, N * K), w_shader.reshape(-1))
+    x = rng.standard_normal((1, K)).astype(np.float32)
+    y = loader.qmatmul(t, blocks, N, K, x)
+    want = (x.astype(np.float64) @ w_shader.astype(np.float64).T)
+    assert synth.rel_l2(y, want) < 1e-6
+
+
 def test_pack_errors():
     c = np.zeros(64, np.uint8)
     s = np.ones(1, np.float32)
