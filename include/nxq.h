@@ -401,7 +401,7 @@ NXQ_API int nxq_nxf_manifest_string(nxq_nxf_t f, const char* key, char* buf, siz
 /* Register tensor i as a weight [N][K]: K = dims[0], N = dims[1]; for a
  * 3-D tensor [E][N][K] (stacked experts) `slice` picks one, else pass 0.  The
  * _shard form registers this rank's tensor-parallel shard
- * (nxq_weight_register_shard rules; block passthrough codecs only). */
+ * (nxq_weight_register_shard rules; INT4 tensors as their group blocks). */
 NXQ_API int nxq_nxf_register(nxq_nxf_t f, int64_t i, int64_t slice, nxq_weight_t* out);
 NXQ_API int nxq_nxf_register_shard(nxq_nxf_t f, int64_t i, int64_t slice, int split, int rank,
                                    int world, nxq_weight_t* out);

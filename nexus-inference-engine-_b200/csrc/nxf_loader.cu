@@ -310,7 +310,6 @@ int register_tensor(const NxfFile& f, int64_t i, int64_t slice, bool sharded, in
         if (gs != 32 && gs != 64 && gs != 128)
             return fail(NXQ_ERR_CODEC, "nxf: '%s': INT4 group size %d (32, 64, 128 are supported)", t.name.c_str(), gs);
         if (K % gs) return fail(NXQ_ERR_SHAPE, "nxf: '%s': K=%lld is not a multiple of %d", t.name.c_str(), (long long)K, gs);
-        if (sharded) return fail(NXQ_ERR_CODEC, "nxf: tensor-parallel shards of INT4 tensors are not supported");
         // A chunk of n elements holds n/2 code bytes and n/gs (scale, zero) pairs.
         std::vector<uint8_t> codes;
         std::vector<float> scales, zeros;
@@ -332,8 +331,15 @@ int register_tensor(const NxfFile& f, int64_t i, int64_t slice, bool sharded, in
             return fail(NXQ_ERR_SHAPE, "nxf: '%s' holds %lld INT4 elements, its shape needs %lld", t.name.c_str(),
                         (long long)codes.size() * 2, (long long)elems);
         const size_t co = (size_t)(slice * slice_elems / 2), go = (size_t)(slice * slice_elems / gs);
-        return nxq_weight_register_int4(codes.data() + co, scales.data() + go, zeros.data() + go, N, K, gs,
-                                        NXQ_INT4_ROWS, out);
+        if (!sharded)
+            return nxq_weight_register_int4(codes.data() + co, scales.data() + go, zeros.data() + go, N, K, gs,
+                                            NXQ_INT4_ROWS, out);
+        // A shard: the group blocks on the host, then the block shard path.
+        std::vector<uint8_t> blocks((size_t)(N * (K / gs) * (8 + gs / 2)));
+        if (int rc = nxq_int4_pack(codes.data() + co, scales.data() + go, zeros.data() + go, N, K, gs,
+                                   NXQ_INT4_ROWS, blocks.data(), blocks.size()))
+            return rc;
+        return nxq_weight_register_shard(blocks.data(), blocks.size(), 100 + gs / 32, N, K, split, rank, world, out);
     }
     return fail(NXQ_ERR_CODEC, "nxf: '%s': codec %d is not a quantized-matmul weight codec", t.name.c_str(), codec);
 }

@@ -8,7 +8,8 @@ index, chunk descriptors, manifest values) and refuses corrupt, truncated and
 inconsistent ones; a codec that is no matmul weight is NXQ_ERR_CODEC.
 GPU: INT4 (groups of 64 and 128, one slice of a 3-D tensor) and Q4K / Q3K
 passthrough tensors (one of them in two chunks) register bit-exactly (device
-decode against the oracle) and multiply within the parity bar."""
+decode against the oracle) and multiply within the parity bar; column and row
+shards decode to their slices of the whole tensor."""
 from __future__ import annotations
 
 import ctypes
@@ -194,6 +195,33 @@ def test_xxh32_known_lengths():
     data = bytes(range(256)) * 2
     seen = {nxq.xxh32(data[:n]) for n in range(0, 70)}
     assert len(seen) == 70
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["blk.0.ffn_gate.weight", "blk.0.ffn_down.weight"])
+def test_register_shards(gpu, tmp_path, name):
+    """Each rank's COL / ROW shard of an INT4 and a two-chunk Q3K tensor
+    decodes to its slice of the whole tensor's decode (ranks registered one
+    after another on one GPU)."""
+    path = tmp_path / "w.nxf"
+    _write_ours(path)
+    world = 2
+    with gpu.NXF(path) as f:
+        w = f.register(name)
+        full = w.dequant().cpu().numpy().reshape(w.N, w.K)
+        w.release()
+        for split in (gpu.SPLIT_COL, gpu.SPLIT_ROW):
+            for rank in range(world):
+                s = f.register_shard(name, split, rank, world)
+                try:
+                    got = s.dequant().cpu().numpy().reshape(s.N, s.K)
+                    if split == gpu.SPLIT_COL:
+                        want = full[rank * s.N:(rank + 1) * s.N]
+                    else:
+                        want = full[:, rank * s.K:(rank + 1) * s.K]
+                    assert loader.same_bits(got.reshape(-1), want.reshape(-1)), (split, rank)
+                finally:
+                    s.release()
 
 
 @pytest.mark.gpu
