@@ -5,7 +5,10 @@
  *   MetalBackend::gemv_int4_nr8 / gemm_int4_gpu / wrap_pointer
  *                                            nexus/src/compute/metal/metal_backend.h:60-87
  * applied to GGUF block-quantized weights (Q4_0, Q8_0, Q4_K, Q3_K, ...) whose
- * values are defined by nexus/src/import/gguf_importer.cpp:677-1000.
+ * values are defined by nexus/src/import/gguf_importer.cpp:677-1000, and to
+ * the NXF INT4 group format (nexus/src/quant/gptq.cpp:9-70).  Weights reach
+ * HBM from host arrays (nxq_weight_register*), GGUF files (nxq_gguf_*) or NXF
+ * files (nxq_nxf_*).
  *
  * Conventions
  *   - Plain C types only; every call returns an nxq_status (0 = ok, < 0 error)
