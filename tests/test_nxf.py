@@ -6,7 +6,8 @@ reference's own NXFWriter (compiled into oracle/_ref), which pins both the
 layout and the xxHash32 chunk checksums; the loader reads such a file (tensor
 index, chunk descriptors, manifest values) and refuses corrupt, truncated and
 inconsistent ones; a codec that is no matmul weight is NXQ_ERR_CODEC.
-GPU: INT4 (groups of 64 and 128, one slice of a 3-D tensor) and Q4K / Q3K
+GPU: INT4 (groups of 32 in two chunks, 64 and 128, one slice of a 3-D
+tensor) and Q4K / Q3K
 passthrough tensors (one of them in two chunks) register bit-exactly (device
 decode against the oracle) and multiply within the parity bar; column and row
 shards decode to their slices of the whole tensor."""
@@ -39,6 +40,7 @@ def _content():
     c128 = _int4(256, 1024, 128, 1)
     c64 = _int4(128, 512, 64, 2)
     e3 = _int4(2 * 128, 512, 128, 3)  # two stacked [128][512] slices
+    m2 = _int4(192, 256, 32, 7)  # stored in two chunks of 96 rows
     q4k = synth.make_blocks(12, 128, 512, seed=4).tobytes()
     q3k = synth.make_blocks(11, 256, 512, seed=5).tobytes()
     rng = np.random.default_rng(6)
@@ -50,10 +52,13 @@ def _content():
         ("blk.0.ffn_gate_exps.weight", [512, 128, 2], nxf_file.DTYPE_I4,
          [(nxf_file.int4_chunk(*e3), nxf_file.CODEC_INT4, 128)]),
         ("blk.0.attn_q.weight", [512, 128], nxf_file.DTYPE_I4, [(q4k, nxf_file.CODEC_Q4K, 0)]),
+        ("blk.0.attn_v.weight", [256, 192], nxf_file.DTYPE_I4,
+         [(nxf_file.int4_chunk(m2[0][:96 * 128], m2[1][:96 * 8], m2[2][:96 * 8]), nxf_file.CODEC_INT4, 32),
+          (nxf_file.int4_chunk(m2[0][96 * 128:], m2[1][96 * 8:], m2[2][96 * 8:]), nxf_file.CODEC_INT4, 32)]),
         ("blk.0.ffn_down.weight", [512, 256], nxf_file.DTYPE_I4,
          [(q3k[: 128 * 2 * 110], nxf_file.CODEC_Q3K, 0), (q3k[128 * 2 * 110:], nxf_file.CODEC_Q3K, 0)]),
         ("raw.odd_sizes", [151], nxf_file.DTYPE_F32, [(r, nxf_file.CODEC_FP32, 0) for r in raw]),
-    ], {"c128": c128, "c64": c64, "e3": e3, "q4k": q4k, "q3k": q3k}
+    ], {"c128": c128, "c64": c64, "e3": e3, "m2": m2, "q4k": q4k, "q3k": q3k}
 
 
 MANIFEST = dict(architecture="llama", name='tiny "test"\tmodel', num_layers=2, hidden_dim=4096,
@@ -198,7 +203,7 @@ def test_xxh32_known_lengths():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("name", ["blk.0.ffn_gate.weight", "blk.0.ffn_down.weight"])
+@pytest.mark.parametrize("name", ["blk.0.ffn_gate.weight", "blk.0.attn_v.weight", "blk.0.ffn_down.weight"])
 def test_register_shards(gpu, tmp_path, name):
     """Each rank's COL / ROW shard of an INT4 and a two-chunk Q3K tensor
     decodes to its slice of the whole tensor's decode (ranks registered one
@@ -237,6 +242,7 @@ def test_register_and_matmul(gpu, tmp_path):
         ("blk.0.ffn_gate_exps.weight", 1, 104, 128, 512,
          gpu.int4_pack(*d["e3"], 256, 512, 128)[128 * 4 * (8 + 64):]),
         ("blk.0.attn_q.weight", 0, 12, 128, 512, np.frombuffer(d["q4k"], np.uint8)),
+        ("blk.0.attn_v.weight", 0, 101, 192, 256, gpu.int4_pack(*d["m2"], 192, 256, 32)),
         ("blk.0.ffn_down.weight", 0, 11, 256, 512, np.frombuffer(d["q3k"], np.uint8)),
     ]
     with gpu.NXF(path) as f:
