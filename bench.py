@@ -2,37 +2,44 @@
 """Benchmark of the dequant-fused quantized matmul (the BASELINE.json metric).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl nxq|reference]
+    python bench.py --case Q4_K:14336x4096:M1 [--iters 3 --copies 2 --graph R]   (profiling)
 
 Workload (one "step"): BASELINE.json config 2 - the Q4_K GEMV over a
 Llama-3-8B MLP, gate and up (K=4096, N=14336) and down (K=14336, N=4096), at
 every decode batch M in {1, 4, 8, 16, 32}: 15 quantized matmuls per step,
 fp16 activations, fp32 output, fp32 accumulation.  Weights are synthetic
-(seeded; nxq.synth) and HBM-resident; every call reads a different weight
-replica, and the replicas of each projection span more than 4x the 126 MB L2,
-so each call streams its weights from HBM.
+(seeded; nxq.synth) and HBM-resident; every call of a step reads its own
+weight replica and the replicas of a projection span more than 4x the
+126 MB L2, so each call streams its weights from HBM.
 
-value      = algorithmic bytes of all calls (packed weight blocks + x + y) over
-             the device time of the K timed steps (CUDA events, max over ranks)
-e2e        = the same workload through the drop-in host entry point
-             nxq_qmatmul_host (fp32 host activations in, fp32 host output out,
-             copies inside the timed region), wall clock
+N = 1: the step on one GPU.  N > 1 (torchrun, one process per GPU): the same
+step split tensor-parallel over the N GPUs - gate/up by column, down by row
+with the library's NCCL allreduce of the partial outputs - so the whole job
+is fixed as N grows (strong scaling); the matmul and allreduce times of the
+step are also reported on their own (tp_split).
+
+value      = algorithmic bytes of the whole step (packed weight blocks + x + y)
+             times K steps over the device time of the K timed steps (CUDA
+             events, max over ranks)
+e2e        = the same workload through the public host-facing calls with the
+             host<->device copies inside the timed region: nxq_qmatmul_host
+             (N = 1) or nxq_tp_qmatmul with pinned-host copies (N > 1)
 roofline   = the dominant kernel's algorithmic GB/s against the measured HBM
              copy bandwidth in MEASURED_PEAKS.json
 prefill    = BASELINE.json config 4: Q4_K GEMM at M in {512, 2048, 8192},
-             K=4096, N=14336, bf16 activations and bf16 output, TFLOP/s
+             K=4096, N=14336, bf16 activations and bf16 output, TFLOP/s (N = 1)
 config1 / config3 = BASELINE.json configs 1 (Q4_0 GEMV M=1, 4096x4096, fp32 x)
              and 3 (Q8_0 GEMV M=1 over the 7 projections of a Llama-3-8B layer),
              one GPU
 tp_config5 = BASELINE.json config 5 (Q3_K 405B-shaped layer, M in {1,8,32}),
              tensor-parallel over the launched ranks (NCCL allreduce after the
-             row-split projections); max over ranks
+             row-split projections); max over ranks; matmuls and allreduces
+             also timed on their own
 cpu_baseline = the reference's CPU path (its own decoders from
              oracle/_ref when built, else the oracle restatement, plus fp32
              dot products) on a bounded row sample of the same workload
 
-With --gpus N > 1 (torchrun, one process per GPU) every rank runs the same
-per-GPU workload on its own weights (weak scaling).  --impl reference times
-the reference CPU path instead, on rank 0 only.
+--impl reference times the reference CPU path instead, on rank 0 only.
 """
 from __future__ import annotations
 
@@ -510,7 +517,9 @@ def bench_tp_layer(dev, stream, pk, rank: int, world: int) -> dict:
     row) and summed with the library's NCCL allreduce.  Each rank generates its
     own shard (synthetic data of the config's distribution).  The timed step is
     the layer's 7 matmuls + 2 allreduces (attention and SwiGLU are not part of
-    the path), captured in one CUDA graph; time = max over ranks."""
+    the path), captured in one CUDA graph; time = max over ranks.  The 7
+    matmuls alone and the 2 allreduces alone are timed the same way.  Keys are
+    flat (M<m>_...) so that records keep them."""
     import torch
 
     import nxq
@@ -537,140 +546,178 @@ def bench_tp_layer(dev, stream, pk, rank: int, world: int) -> dict:
         blocks = synth.make_blocks(Q3, n_l, k_l, seed=5000 + 97 * i + rank)
         weights[name] = [nxq.Weight.register(blocks, Q3, n_l, k_l) for _ in range(R)]
         del blocks
-    cases = {}
+    total_b = sum(N * (K // 256) * 110 for _, K, N, _ in projs)
+    out = {"workload": "BASELINE config 5: Llama-3.1-405B-shaped layer, Q3_K, decode, 7 projections + "
+                       "2 allreduces per step", "tp": world, "layer_weight_bytes": total_b,
+           "shard_bytes_per_gpu": shard_bytes, "replicas": R,
+           "timing": "CUDA graph of R layer steps, CUDA events, max over ranks"}
     for M in (1, 8, 32):
         x = {k: torch.randn(M, k, generator=torch.Generator().manual_seed(M + k), dtype=torch.float32)
              .to(torch.float16).to(dev) for k in {k_l for _, k_l, _, _ in loc}}
         y = {(name, n_l): torch.empty(M, n_l, dtype=torch.float32, device=dev) for name, _, n_l, _ in loc}
 
-        def issue(M=M, x=x, y=y):
+        def issue(x=x, y=y, matmul=True, allreduce=True):
             for r in range(R):
                 for name, k_l, n_l, split in loc:
                     w = weights[name][r]
-                    if world > 1:
+                    if world > 1 and matmul and allreduce:
                         nxq.tp_qmatmul(w, x[k_l], y[(name, n_l)], nxq.SPLIT_ROW if split else nxq.SPLIT_COL,
                                        stream=stream)
-                    else:
+                    elif matmul:
                         nxq.qmatmul(w, x[k_l], out=y[(name, n_l)], stream=stream)
+                    elif split and world > 1:
+                        nxq.tp_allreduce_f32(y[(name, n_l)], stream=stream)
 
         with torch.cuda.stream(stream):
             issue()
         stream.synchronize()
         barrier(world)
         ms = max_over_ranks(graph_time_ms(issue, stream) / R, world)
-        total_b = sum(N * (K // 256) * 110 for _, K, N, _ in projs)
-        cases[f"M{M}"] = {"us_per_layer": round(ms * 1e3, 2),
-                          "GB/s": round(total_b / (ms / 1e3) / 1e9, 1),
-                          "frac_of_hbm_per_gpu": round(total_b / world / (ms / 1e3) / 1e9 / pk["hbm_gbs"], 3)}
+        out[f"M{M}_us"] = round(ms * 1e3, 2)
+        out[f"M{M}_GBps"] = round(total_b / (ms / 1e3) / 1e9, 1)
+        out[f"M{M}_frac_of_hbm_per_gpu"] = round(total_b / world / (ms / 1e3) / 1e9 / pk["hbm_gbs"], 3)
+        if world > 1:
+            barrier(world)
+            ms_mm = max_over_ranks(graph_time_ms(lambda: issue(allreduce=False), stream) / R, world)
+            barrier(world)
+            ms_ar = max_over_ranks(graph_time_ms(lambda: issue(matmul=False), stream) / R, world)
+            out[f"M{M}_matmul_us"] = round(ms_mm * 1e3, 2)
+            out[f"M{M}_allreduce_us"] = round(ms_ar * 1e3, 2)
         del x, y
     for ws in weights.values():
         for w in ws:
             w.release()
     if world > 1:
         nxq.tp_shutdown()
-    return {"workload": "BASELINE config 5: Llama-3.1-405B-shaped layer, Q3_K, decode, 7 projections + "
-                        "2 allreduces per step", "tp": world, "cases": cases,
-            "layer_weight_bytes": sum(N * (K // 256) * 110 for _, K, N, _ in projs),
-            "shard_bytes_per_gpu": shard_bytes, "replicas": R,
-            "timing": "CUDA graph of R layer steps, CUDA events, max over ranks"}
+    return out
 
 
-def run_gpu_arm(args, rank, world, local):
+def bench_prefill(dev, stream, pk, pk_kind) -> dict:
+    """Q4_K GEMM K=4096 N=14336, bf16 activations and bf16
+    output, M in {512, 2048, 8192}; a graph of back-to-back calls rotating
+    over weight replicas that together exceed 4x L2.  Flat keys."""
     import torch
 
     import nxq
     from nxq import synth
 
-    torch.cuda.set_device(local)
-    nxq.init(local)
-    pk, pk_kind = peaks()
-    dev = torch.device("cuda", local)
+    K, N = 4096, 14336
+    blocks = synth.make_blocks(Q4_K, N, K, seed=4000)
+    R = replicas_for(weight_bytes(K, N))
+    ws = [nxq.Weight.register(blocks, Q4_K, N, K) for _ in range(R)]
+    del blocks
+    out = {"workload": "BASELINE config 4: Q4_K GEMM K=4096 N=14336, bf16 x, bf16 y, fp32 accumulate",
+           "unit": "TFLOP/s", "peak_source": f"{pk_kind} bf16_tflops (burst; kernel timed on its own)",
+           "replicas": R}
+    for M in PREFILL_MS:
+        x = torch.randn(M, K, generator=torch.Generator().manual_seed(M), dtype=torch.float32).to(
+            torch.bfloat16).to(dev)
+        y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        out["kernel"] = nxq.kernel_name(ws[0], M, nxq.BF16, nxq.BF16)
+        iters = R if M <= 2048 else 4
+        with torch.cuda.stream(stream):
+            for i in range(3):
+                nxq.qmatmul(ws[i % R], x, out=y, stream=stream)
+        stream.synchronize()
+        ms = graph_time_ms(lambda: [nxq.qmatmul(ws[i % R], x, out=y, stream=stream) for i in range(iters)],
+                           stream) / iters
+        tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
+        out[f"M{M}_us"] = round(ms * 1e3, 2)
+        out[f"M{M}_TFLOPs"] = round(tf, 1)
+        out[f"M{M}_frac_of_bf16_burst"] = round(tf / pk["bf16_tflops"], 4)
+        del x, y
+    nxq.stream_sync()
+    for w in ws:
+        w.release()
+    return out
 
-    # --- weights: R replicas per projection, R * bytes(proj) > 4 x L2 --------
-    reps = max(2, -(-4 * L2_BYTES // weight_bytes(4096, 14336)) + 1)
+
+def time_replays(graphs, stream, steps: int, world: int) -> float:
+    """Barrier, then `steps` replays of graphs[s % len(graphs)] between CUDA
+    events on `stream`; returns the max over ranks of the elapsed ms."""
+    import torch
+
+    barrier(world)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        a.record(stream)
+        for s_i in range(steps):
+            graphs[s_i % len(graphs)].replay()
+        b.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(a.elapsed_time(b), world)
+
+
+def capture(fn, stream):
+    import torch
+
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        fn()
+    return g
+
+
+def headline_single(args, dev, stream, pk) -> dict:
+    """N = 1: the config-2 step (15 calls) on one GPU.  Every call of a step
+    reads its own weight replica: the j-th use of a projection in step graph r
+    takes replica (5 r + j) mod R, so within a step no weight is read twice and
+    a replica comes back only after R/5 steps (R x 33 MB > 4 x L2)."""
+    import torch
+
+    import nxq
+    from nxq import synth
+
+    reps = replicas_for(weight_bytes(4096, 14336))
     weights = {}
     for name, K, N in PROJ:
-        blocks = synth.make_blocks(Q4_K, N, K, seed=1000 + K + N + rank)
+        blocks = synth.make_blocks(Q4_K, N, K, seed=1000 + K + N)
         weights[name] = [nxq.Weight.register(blocks, Q4_K, N, K) for _ in range(reps)]
         del blocks
     xs = {M: {K: torch.randn(M, K, generator=torch.Generator().manual_seed(M * 7 + K), dtype=torch.float32)
               .to(torch.float16).to(dev) for K in (4096, 14336)} for M in GEMV_MS}
     ys = {M: {N: torch.empty(M, N, dtype=torch.float32, device=dev) for N in (4096, 14336)} for M in GEMV_MS}
-    calls = []  # (weight list, K, N, M)
-    for M in GEMV_MS:
-        for name, K, N in PROJ:
-            calls.append((name, K, N, M))
+    calls = [(name, K, N, M) for M in GEMV_MS for name, K, N in PROJ]
+    uses = len(GEMV_MS)  # uses of each projection per step
     step_bytes = sum(call_bytes(M, K, N) for _, K, N, M in calls)
     names = {(name, M): nxq.kernel_name(weights[name][0], M, nxq.F16, nxq.F32) for name, K, N, M in calls}
-    counter = [0]
-    stream = torch.cuda.Stream(device=dev)
 
-    def step_calls(rep):
-        for name, K, N, M in calls:
-            nxq.qmatmul(weights[name][rep], xs[M][K], out=ys[M][N], stream=stream)
+    def step_calls(r):
+        for j, M in enumerate(GEMV_MS):
+            for name, K, N in PROJ:
+                nxq.qmatmul(weights[name][(uses * r + j) % reps], xs[M][K], out=ys[M][N], stream=stream)
 
-    # Warm up on the capture stream (sizes its scratch), then capture one graph
-    # per weight replica: replaying graph r runs the 15 calls on replica r.
     with torch.cuda.stream(stream):
         for r in range(args.warmup):
-            step_calls(r % reps)
+            step_calls(r)
     stream.synchronize()
     nxq.stream_sync(stream)
-    step_graphs = []
-    for r in range(reps):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            step_calls(r)
-        step_graphs.append(g)
+    step_graphs = [capture(lambda r=r: step_calls(r), stream) for r in range(reps)]
     with torch.cuda.stream(stream):
         for r in range(args.warmup):
             step_graphs[r % reps].replay()
     torch.cuda.synchronize()
 
-    # --- timed region: K step-graph replays ------------------------------------
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(torch.cuda.current_device())
     time.sleep(0.3)
-    barrier(world)
-    torch.cuda.synchronize()
-    t_start = torch.cuda.Event(enable_timing=True)
-    t_end = torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        t_start.record(stream)
-        for s_i in range(args.steps):
-            step_graphs[s_i % reps].replay()
-        t_end.record(stream)
-    torch.cuda.synchronize()
-    # Graph replays bypass the library's host-side launch counter: every
-    # captured call is one kernel node of ours.
-    launches = len(calls) * args.steps
-    barrier(world)
+    ms = time_replays(step_graphs, stream, args.steps, 1)
     clk = clocks.stop()
     nxq.stream_sync(stream)
-    ms = t_start.elapsed_time(t_end)
-    ms_max = max_over_ranks(ms, world)
-    value = step_bytes * args.steps * world / (ms_max / 1e3) / 1e9
+    del step_graphs
 
-    # --- per-case device time: a graph of `reps` back-to-back launches of one
-    # (projection, M), each on a different replica ------------------------------
-    per_kernel = {}
-    per_case = {}
+    # Per-case device time: a graph of `reps` back-to-back launches of one
+    # (projection, M), each on a different replica.
+    per_kernel, per_case = {}, {}
     for name, K, N, M in calls:
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            for r in range(reps):
-                nxq.qmatmul(weights[name][r], xs[M][K], out=ys[M][N], stream=stream)
+        g = capture(lambda name=name, K=K, N=N, M=M: [nxq.qmatmul(weights[name][r], xs[M][K], out=ys[M][N],
+                                                                  stream=stream) for r in range(reps)], stream)
         with torch.cuda.stream(stream):
-            g.replay()  # warm, on the timing stream and finished before timing
+            g.replay()
         torch.cuda.synchronize()
-        a_ev, b_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            a_ev.record(stream)
-            for _ in range(3):
-                g.replay()
-            b_ev.record(stream)
-        torch.cuda.synchronize()
+        d = time_replays([g], stream, 3, 1)
+        del g
         n_l = 3 * reps
-        d = a_ev.elapsed_time(b_ev)
         kname = names[(name, M)]
         k = per_kernel.setdefault(kname, {"ms": 0.0, "bytes": 0, "launches": 0, "shapes": {}})
         k["ms"] += d
@@ -681,104 +728,227 @@ def run_gpu_arm(args, rank, world, local):
         c = per_case.setdefault(f"{name}_M{M}", {"ms": 0.0, "bytes": 0})
         c["ms"] += d
         c["bytes"] += call_bytes(M, K, N) * n_l
-        del g
     nxq.stream_sync(stream)
     total_k = sum(k["ms"] for k in per_kernel.values())
     dom_name, dom = max(per_kernel.items(), key=lambda kv: kv[1]["ms"])
     achieved = dom["bytes"] / (dom["ms"] / 1e3) / 1e9
-    traffic = traffic_lookup(dom_name, dom["shapes"])
     roofline = {"bound": "hbm", "kernel": dom_name, "achieved": achieved, "peak": pk["hbm_gbs"],
-                "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": traffic,
-                "peak_source": f"{pk_kind} hbm_gbs", "share_of_step": dom["ms"] / total_k,
+                "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                "traffic": traffic_lookup(dom_name, dom["shapes"]),
+                "peak_source": "hbm_gbs of MEASURED_PEAKS.json (burst copy)", "share_of_step": dom["ms"] / total_k,
                 "algorithmic_bytes_per_launch": dom["bytes"] / dom["launches"],
                 "avg_launch_us": dom["ms"] / dom["launches"] * 1e3, "shapes": sorted(dom["shapes"]),
                 "timing": "CUDA events on the launching stream around graph replays of back-to-back "
-                          "launches of each shape (PDL overlap between launches included)"}
-    cases_out = {k: round(v["bytes"] / (v["ms"] / 1e3) / 1e9, 1) for k, v in per_case.items()}
-    kernels_out = {k: {"launches": v["launches"], "ms": round(v["ms"], 3),
-                       "GB/s": round(v["bytes"] / (v["ms"] / 1e3) / 1e9, 1),
-                       "share": round(v["ms"] / total_k, 4)} for k, v in per_kernel.items()}
+                          "launches of each shape on distinct weight replicas (PDL overlap included)"}
 
-    # --- e2e through the host drop-in ------------------------------------------
     e2e = None
     if not args.no_e2e:
         hx = {M: {K: torch.randn(M, K, generator=torch.Generator().manual_seed(M + K)).to(torch.float16)
                   .float().pin_memory().numpy() for K in (4096, 14336)} for M in GEMV_MS}
         hy = {M: {N: torch.empty(M, N, dtype=torch.float32).pin_memory().numpy() for N in (4096, 14336)}
               for M in GEMV_MS}
-        e2e_steps = max(1, min(args.steps, 10))
-        h2d = sum(M * K * 4 for _, K, N, M in calls)
-        d2h = sum(M * N * 4 for _, K, N, M in calls)
-        e2e_bytes = sum(call_bytes(M, K, N, x_size=4) for _, K, N, M in calls)
+        counter = [0]
 
         def host_step():
-            for name, K, N, M in calls:
-                nxq.qmatmul_host(weights[name][counter[0] % reps], hx[M][K], out=hy[M][N])
+            r = counter[0]
+            for j, M in enumerate(GEMV_MS):
+                for name, K, N in PROJ:
+                    nxq.qmatmul_host(weights[name][(uses * r + j) % reps], hx[M][K], out=hy[M][N])
             counter[0] += 1
 
         for _ in range(2):
             host_step()
         nxq.stream_sync()
+        e2e_steps = max(3, min(args.steps, 20))
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            host_step()
+        el = time.perf_counter() - t0
+        e2e_bytes = sum(call_bytes(M, K, N, x_size=4) for _, K, N, M in calls)
+        h2d = sum(M * K * 4 for _, K, N, M in calls)
+        d2h = sum(M * N * 4 for _, K, N, M in calls)
+        e2e = {"value": e2e_bytes * e2e_steps / el / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "pcie_GBps": (h2d + d2h) * e2e_steps / el / 1e9,
+               "api": "nxq_qmatmul_host (fp32 host x/y, weights resident), one synchronous call per matmul",
+               "steps": e2e_steps, "ms_per_step": el / e2e_steps * 1e3,
+               "timing": "wall clock around the steps (host call returns after its result is in host memory)"}
+
+    for ws in weights.values():
+        for w in ws:
+            w.release()
+    torch.cuda.empty_cache()
+    return {"value": step_bytes * args.steps / (ms / 1e3) / 1e9, "ms": ms, "step_bytes": step_bytes,
+            "launches": len(calls) * args.steps, "clocks": clk, "roofline": roofline, "e2e": e2e,
+            "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 3),
+                            "GB/s": round(v["bytes"] / (v["ms"] / 1e3) / 1e9, 1),
+                            "share": round(v["ms"] / total_k, 4)} for k, v in per_kernel.items()},
+            "per_case_GBps": {k: round(v["bytes"] / (v["ms"] / 1e3) / 1e9, 1) for k, v in per_case.items()},
+            "l2": f"inputs larger than L2: {reps} weight replicas per projection "
+                  f"({reps * weight_bytes(4096, 14336) / 2**20:.0f} MiB each); every call of a step reads "
+                  f"its own replica",
+            "parallelism": "single GPU", "scaling": "strong"}
+
+
+def headline_tp(args, dev, stream, pk, rank: int, world: int) -> dict:
+    """N > 1: the same config-2 step split over the ranks the way the north
+    star splits a layer: gate and up by column (rank r computes rows
+    [r N/T, (r+1) N/T) of y), down by row (rank r holds K/T of every row,
+    takes its K/T slice of the activations - the slice of SwiGLU(gate, up) it
+    computed itself - and the partial outputs are summed by the library's NCCL
+    allreduce).  Strong scaling: the whole job is the unsharded step, value =
+    its bytes over the time (max over ranks).  Also timed on their own, in
+    graphs of the same calls: the matmuls without the allreduces, and the five
+    allreduces (one per M) without the matmuls."""
+    import torch
+    import torch.distributed as dist
+
+    import nxq
+    from nxq import synth
+
+    uid = [nxq.tp_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    nxq.tp_init(rank, world, uid[0])
+    # name, K, N, split; the shard's local K and N.
+    proj = [(name, K, N, nxq.SPLIT_ROW if name == "down" else nxq.SPLIT_COL) for name, K, N in PROJ]
+    loc = {name: ((K, N // world) if sp == nxq.SPLIT_COL else (K // world, N)) for name, K, N, sp in proj}
+    shard_b = {name: weight_bytes(k, n) for name, (k, n) in loc.items()}
+    reps = replicas_for(min(shard_b.values()))
+    weights = {}
+    for i, (name, K, N, sp) in enumerate(proj):
+        k, n = loc[name]
+        blocks = synth.make_blocks(Q4_K, n, k, seed=2000 + 97 * i + rank)
+        weights[name] = [nxq.Weight.register(blocks, Q4_K, n, k) for _ in range(reps)]
+        del blocks
+    xs = {M: {name: torch.randn(M, loc[name][0], generator=torch.Generator().manual_seed(M * 7 + loc[name][0] + rank),
+                                dtype=torch.float32).to(torch.float16).to(dev) for name, _, _, _ in proj}
+          for M in GEMV_MS}
+    ys = {M: {name: torch.empty(M, loc[name][1], dtype=torch.float32, device=dev) for name, _, _, _ in proj}
+          for M in GEMV_MS}
+    uses = len(GEMV_MS)
+    calls = [(name, K, N, sp, M) for M in GEMV_MS for name, K, N, sp in proj]
+    step_bytes = sum(call_bytes(M, K, N) for _, K, N, _, M in calls)
+
+    def step_calls(r, allreduce=True, matmul=True):
+        for j, M in enumerate(GEMV_MS):
+            for name, K, N, sp in proj:
+                w = weights[name][(uses * r + j) % reps]
+                if matmul and allreduce:
+                    nxq.tp_qmatmul(w, xs[M][name], ys[M][name], sp, stream=stream)
+                elif matmul:
+                    nxq.qmatmul(w, xs[M][name], out=ys[M][name], stream=stream)
+                elif sp == nxq.SPLIT_ROW:
+                    nxq.tp_allreduce_f32(ys[M][name], stream=stream)
+
+    with torch.cuda.stream(stream):
+        for r in range(args.warmup):
+            step_calls(r)
+    stream.synchronize()
+    nxq.stream_sync(stream)
+    barrier(world)
+    graphs = [capture(lambda r=r: step_calls(r), stream) for r in range(reps)]
+    with torch.cuda.stream(stream):
+        for r in range(args.warmup):
+            graphs[r % reps].replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(torch.cuda.current_device())
+    time.sleep(0.3)
+    ms = time_replays(graphs, stream, args.steps, world)
+    clk = clocks.stop()
+    del graphs
+    mm_graphs = [capture(lambda r=r: step_calls(r, allreduce=False), stream) for r in range(reps)]
+    ms_mm = time_replays(mm_graphs, stream, args.steps, world)
+    del mm_graphs
+    ar_graph = capture(lambda: step_calls(0, matmul=False), stream)
+    with torch.cuda.stream(stream):
+        ar_graph.replay()
+    ms_ar = time_replays([ar_graph], stream, args.steps, world)
+    del ar_graph
+    nxq.stream_sync(stream)
+
+    e2e = None
+    if not args.no_e2e:
+        # Through the public API as a caller would: each step copies this
+        # rank's activations from pinned host memory, issues the 15
+        # nxq_tp_qmatmul calls, and reads every output back to pinned host
+        # memory; timed on the host, max over ranks.
+        hx = {M: {name: xs[M][name].cpu().pin_memory() for name, _, _, _ in proj} for M in GEMV_MS}
+        hy = {M: {name: torch.empty_like(ys[M][name], device="cpu").pin_memory() for name, _, _, _ in proj}
+              for M in GEMV_MS}
+        counter = [0]
+
+        def host_step():
+            r = counter[0]
+            with torch.cuda.stream(stream):
+                for j, M in enumerate(GEMV_MS):
+                    for name, K, N, sp in proj:
+                        xs[M][name].copy_(hx[M][name], non_blocking=True)
+                    for name, K, N, sp in proj:
+                        nxq.tp_qmatmul(weights[name][(uses * r + j) % reps], xs[M][name], ys[M][name], sp,
+                                       stream=stream)
+                    for name, K, N, sp in proj:
+                        hy[M][name].copy_(ys[M][name], non_blocking=True)
+            stream.synchronize()
+            counter[0] += 1
+
+        for _ in range(2):
+            host_step()
+        nxq.stream_sync(stream)
+        e2e_steps = max(3, min(args.steps, 20))
         barrier(world)
         t0 = time.perf_counter()
         for _ in range(e2e_steps):
             host_step()
         el = max_over_ranks(time.perf_counter() - t0, world)
-        e2e = {"value": e2e_bytes * e2e_steps * world / el / 1e9, "unit": "GB/s",
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "api": "nxq_qmatmul_host (fp32 host x/y, weights resident)", "steps": e2e_steps,
-               "ms_per_step": el / e2e_steps * 1e3}
+        h2d = sum(xs[M][name].numel() * 2 for M in GEMV_MS for name, _, _, _ in proj)
+        d2h = sum(ys[M][name].numel() * 4 for M in GEMV_MS for name, _, _, _ in proj)
+        e2e = {"value": step_bytes * e2e_steps / el / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+               "api": "nxq_tp_qmatmul per projection (f16 activations copied from pinned host memory, "
+                      "fp32 outputs copied back), all ranks", "steps": e2e_steps,
+               "ms_per_step": el / e2e_steps * 1e3,
+               "timing": "wall clock around the steps, max over ranks"}
 
-    del step_graphs
-    for name in weights:
-        for w in weights[name]:
+    for ws in weights.values():
+        for w in ws:
             w.release()
+    nxq.tp_shutdown()
     torch.cuda.empty_cache()
+    return {"value": step_bytes * args.steps / (ms / 1e3) / 1e9, "ms": ms, "step_bytes": step_bytes,
+            "launches": len(calls) * args.steps, "clocks": clk, "e2e": e2e,
+            "roofline": {"bound": "hbm", "kernel": "mma_gemv (tensor-parallel shards)",
+                         "achieved": step_bytes / world * args.steps / (ms_mm / 1e3) / 1e9,
+                         "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": step_bytes / world * args.steps / (ms_mm / 1e3) / 1e9 / pk["hbm_gbs"],
+                         "traffic": None,
+                         "timing": "per-GPU bytes of the step's matmuls over their time without the allreduces"},
+            "tp_split": {"matmul_us_per_step": round(ms_mm / args.steps * 1e3, 2),
+                         "allreduce_us_per_step": round(ms_ar / args.steps * 1e3, 2),
+                         "step_us": round(ms / args.steps * 1e3, 2), "allreduces_per_step": len(GEMV_MS),
+                         "allreduce_bytes": [M * 4096 * 4 for M in GEMV_MS]},
+            "l2": f"inputs larger than L2: {reps} replicas of each shard per rank; every call of a step reads its "
+                  f"own replica",
+            "parallelism": f"tp{world}: gate/up column split, down row split + NCCL allreduce (fp32)",
+            "scaling": "strong"}
+
+
+def run_gpu_arm(args, rank, world, local):
+    import torch
+
+    import nxq
+
+    torch.cuda.set_device(local)
+    nxq.init(local)
+    pk, pk_kind = peaks()
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.Stream(device=dev)
+
+    head = headline_single(args, dev, stream, pk) if world == 1 else headline_tp(args, dev, stream, pk, rank, world)
 
     # --- prefill GEMM (config 4) ------------------------------------------------
     prefill = None
-    if not args.no_prefill:
-        K, N = 4096, 14336
-        blocks = synth.make_blocks(Q4_K, N, K, seed=4000)
-        w = nxq.Weight.register(blocks, Q4_K, N, K)
-        del blocks
-        prefill = {"kernel": None, "cases": {}}
-        for M in PREFILL_MS:
-            x = torch.randn(M, K, generator=torch.Generator().manual_seed(M), dtype=torch.float32).to(
-                torch.bfloat16).to(dev)
-            y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
-            prefill["kernel"] = nxq.kernel_name(w, M, nxq.BF16, nxq.BF16)
-            with torch.cuda.stream(stream):
-                for _ in range(3):
-                    nxq.qmatmul(w, x, out=y, stream=stream)
-            stream.synchronize()
-            iters = 4
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                for _ in range(iters):
-                    nxq.qmatmul(w, x, out=y, stream=stream)
-            with torch.cuda.stream(stream):
-                g.replay()
-            torch.cuda.synchronize()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            barrier(world)
-            with torch.cuda.stream(stream):
-                a.record(stream)
-                g.replay()
-                b.record(stream)
-            torch.cuda.synchronize()
-            del g
-            t = max_over_ranks(a.elapsed_time(b) / iters, world)
-            tf = 2.0 * M * N * K / (t / 1e3) / 1e12
-            prefill["cases"][f"M{M}"] = {"ms": t, "TFLOP/s": tf,
-                                         "frac_of_bf16_burst": tf / pk["bf16_tflops"],
-                                         "frac_of_bf16_sustained": tf / pk["bf16_tflops_sustained"]}
-            del x, y
-        nxq.stream_sync()
-        w.release()
-        prefill["unit"] = "TFLOP/s"
-        prefill["workload"] = "BASELINE config 4: Q4_K GEMM K=4096 N=14336, bf16 x, bf16 y, fp32 accumulate"
-        prefill["peak_source"] = f"{pk_kind} bf16_tflops / bf16_tflops_sustained"
+    if not args.no_prefill and world == 1:
+        prefill = bench_prefill(dev, stream, pk, pk_kind)
 
     # --- configs 1 and 3 (one GPU), config 5 (tensor parallel over the ranks) -------
     extra = {}
@@ -796,25 +966,96 @@ def run_gpu_arm(args, rank, world, local):
         cpu = cpu_reference_sample(args.cpu_seconds)
 
     if rank == 0:
+        workload = ("BASELINE config 2: Q4_K GEMV over a Llama-3-8B MLP, gate/up K=4096 N=14336 and down "
+                    "K=14336 N=4096, M in {1,4,8,16,32}; 15 calls per step")
+        if world > 1:
+            workload += f", tensor-parallel over {world} GPUs (the whole step is the unit of work)"
         line = {
-            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "accumulate": "f32",
+            "metric": METRIC, "value": head["value"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": head["ms"] / args.steps, "higher_is_better": True,
+            "scaling": head["scaling"], "vs_baseline": None, "dtype": "f16", "accumulate": "f32",
             "data": "synthetic",
-            "config": {"workload": "BASELINE config 2: Q4_K GEMV over a Llama-3-8B MLP, gate/up K=4096 "
-                                   "N=14336 and down K=14336 N=4096, M in {1,4,8,16,32}; 15 calls per step "
-                                   "(per GPU)",
+            "config": {"workload": workload,
                        "weights": "Q4_K, d/dmin fp16 U(1e-4,1e-3), codes uniform (seeded)",
-                       "x": "fp16 N(0,1)", "y": "fp32",
-                       "l2": f"inputs larger than L2: {reps} weight replicas per projection "
-                             f"({reps * weight_bytes(4096, 14336) / 2**20:.0f} MiB each), rotated every call",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
-            "roofline": roofline, "kernels": kernels_out, "per_case_GBps": cases_out,
-            "gpu_launches": launches, "clocks": clk, "e2e": e2e, "prefill": prefill,
-            "cpu_baseline": cpu, "nominal_hbm_frac": value / world / 8000.0,
+                       "x": "fp16 N(0,1)", "y": "fp32", "l2": head["l2"], "parallelism": head["parallelism"]},
+            "roofline": head["roofline"], "gpu_launches": head["launches"], "clocks": head["clocks"],
+            "e2e": head["e2e"], "prefill": prefill, "cpu_baseline": cpu,
+            "nominal_hbm_frac": head["value"] / world / 8000.0,
         }
+        for k in ("kernels", "per_case_GBps", "tp_split"):
+            if k in head:
+                line[k] = head[k]
         line.update(extra)
         emit(line)
+    return 0
+
+
+# ---------------------------------------------------------------- one case (profiling)
+def run_case(args) -> int:
+    """One quantized-matmul configuration run a few times, small enough for an
+    ncu capture: --case TYPE:NxK:M (e.g. Q4_K:14336x4096:M1).  Registers
+    --copies replicas of a seeded synthetic weight (a capture then sees cold
+    L2), calls nxq_qmatmul --iters times rotating through them and prints the
+    kernel name and the CUDA-event time of each call; with --graph R it also
+    replays a CUDA graph of R back-to-back calls (no host launch overhead).
+    Prints to stderr; the one JSON line is not emitted in this mode."""
+    import torch
+
+    import nxq
+    from nxq import synth
+
+    try:
+        tname, shape, mtxt = args.case.split(":")
+        N, K = (int(v) for v in shape.lower().split("x"))
+        M = int(mtxt.lstrip("Mm"))
+    except ValueError:
+        log(f"--case wants TYPE:NxK:M, e.g. Q4_K:14336x4096:M1 (got {args.case!r})")
+        return 2
+    dt = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}
+    t = nxq.TYPES[tname]
+    nxq.init(0)
+    blocks = synth.make_blocks(t, N, K, seed=1)
+    ws = [nxq.Weight.register(blocks, t, N, K) for _ in range(args.copies)]
+    x = torch.randn(M, K, generator=torch.Generator().manual_seed(2)).to(dt[args.x_dtype]).cuda()
+    y = torch.empty(M, N, dtype=dt[args.y_dtype], device="cuda")
+    name = nxq.kernel_name(ws[0], M, nxq._dtype_code(x.dtype), nxq._dtype_code(y.dtype))
+    times = []
+    for i in range(args.iters):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        nxq.qmatmul(ws[i % len(ws)], x, out=y)
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) * 1e3)
+    nxq.stream_sync()
+    nbytes = ws[0].packed_bytes + x.numel() * x.element_size() + y.numel() * y.element_size()
+    if args.graph > 0:
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            nxq.qmatmul(ws[0], x, out=y, stream=s)
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(args.graph):
+                nxq.qmatmul(ws[i % len(ws)], x, out=y, stream=s)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 10
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * args.graph)
+        log(f"graph: {us:.2f} us/call, {nbytes / (us * 1e-6) / 1e9:.0f} GB/s over {reps}x{args.graph} calls")
+        del g
+        nxq.stream_sync()
+    gbs = [nbytes / (us * 1e-6) / 1e9 for us in times]
+    log(f"{name} {tname} N={N} K={K} M={M}: " + ", ".join(f"{u:.1f}us {g:.0f}GB/s" for u, g in zip(times, gbs)))
+    for w in ws:
+        w.release()
     return 0
 
 
@@ -829,7 +1070,16 @@ def main() -> int:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-configs", action="store_true", help="skip configs 1, 3 and 5")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--case", default=None,
+                    help="profiling mode: run one TYPE:NxK:M case (e.g. Q4_K:14336x4096:M1) and exit")
+    ap.add_argument("--iters", type=int, default=3, help="--case: timed single calls")
+    ap.add_argument("--copies", type=int, default=4, help="--case: weight replicas")
+    ap.add_argument("--x-dtype", default="f16", choices=["f16", "bf16", "f32"], help="--case: activations")
+    ap.add_argument("--y-dtype", default="f32", choices=["f16", "bf16", "f32"], help="--case: output")
+    ap.add_argument("--graph", type=int, default=0, help="--case: launches per replayed CUDA graph (0 = off)")
     args = ap.parse_args()
+    if args.case:
+        return run_case(args)
     global _RESULT
     sys.stdout.flush()
     _RESULT = os.fdopen(os.dup(1), "w")

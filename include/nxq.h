@@ -55,8 +55,19 @@ typedef enum {
     NXQ_ERR_STATE = -7,       /* not initialised / wrong device / TP not set up */
     NXQ_ERR_NCCL = -8,        /* NCCL unavailable or a collective failed       */
     NXQ_ERR_UNSUPPORTED = -9, /* no GPU of the required architecture           */
-    NXQ_ERR_FORMAT = -10      /* a GGUF / NXF file that is malformed or truncated */
+    NXQ_ERR_FORMAT = -10,     /* a GGUF / NXF file that is malformed or truncated */
+    NXQ_ERR_RANGE = -11       /* an activation outside the f16 range (see below) */
 } nxq_status;
+
+/* Numeric range of the tensor-core kernels.  The decode GEMV and the prefill
+ * GEMM multiply in f16 with fp32 accumulation: f16 activations are used as
+ * they are, fp32 and bf16 activations are rounded to f16 first (the reference
+ * keeps them in fp32).  A finite activation of magnitude >= 65520 has no f16
+ * value; the kernel that rounds it records NXQ_ERR_RANGE in the context's
+ * status word, which the next nxq_stream_sync (or the synchronous
+ * nxq_qmatmul_host) returns, and that call's outputs are not finite.  The
+ * CUDA-core kernel (NXQ_DECODE_KERNEL=simt / NXQ_PREFILL_KERNEL=simt, and
+ * nxq_qmatmul_noalloc) computes in fp32 and has no such limit. */
 
 /* Block types: the GGUF type ids of nexus/src/import/gguf_importer.h:28-57,
  * and the NXF INT4 group format (quant/gptq.cpp:9-70: w = (q - zero) * scale,
@@ -251,8 +262,10 @@ NXQ_API int nxq_rmsnorm_qmatmul(const nxq_weight_t* w, int count, const void* x_
  * (compute_dispatch.cpp:156-164); here every row of x is used. */
 NXQ_API int nxq_qmatmul_host(nxq_weight_t w, const float* x_host, float* y_host, int64_t M);
 
-/* Block until all work nxq queued on `stream` is done; reports any device-side
- * error flag raised by a bounded wait as NXQ_ERR_TIMEOUT. */
+/* Block until all work nxq queued on `stream` is done; reports the first
+ * device-side error recorded since the last report: a bounded wait that ran
+ * out (NXQ_ERR_TIMEOUT) or an activation outside the f16 range
+ * (NXQ_ERR_RANGE). */
 NXQ_API int nxq_stream_sync(void* stream);
 
 /* Name of the kernel nxq_qmatmul would launch for (w, M, dtypes), e.g.

@@ -82,16 +82,22 @@ int grow(void** buf, size_t* have, size_t need) {
     return NXQ_OK;
 }
 
-// Reads the device status word after a synchronize; a nonzero code means a
-// bounded wait inside a kernel gave up.
+// Reads the device status word after a synchronize: a bounded wait that
+// gave up (NXQ_ERR_TIMEOUT), or an activation too large for f16
+// (NXQ_ERR_RANGE).  The word is cleared once reported.
 int report_status(const DeviceStatus& st) {
-    if (st.code) {
-        cudaMemset(g_ctx.status, 0, sizeof(DeviceStatus));
-        scratch_reset_counters();
-        return fail(NXQ_ERR_TIMEOUT, "device-side bounded wait expired (code %u at %u)", st.code,
-                    st.where);
+    if (!st.code) return NXQ_OK;
+    cudaMemset(g_ctx.status, 0, sizeof(DeviceStatus));
+    if (st.code == kStatusRange) {
+        static const char* const what[] = {"?", "the f16 conversion of fp32/bf16 activations",
+                                           "the RMSNorm prologue", "the decode GEMV's activation staging"};
+        return fail(NXQ_ERR_RANGE,
+                    "an activation of magnitude >= 65520 reached %s: it is outside the f16 range the "
+                    "tensor-core kernels compute in (results of that call are not finite)",
+                    what[st.where < 4 ? st.where : 0]);
     }
-    return NXQ_OK;
+    scratch_reset_counters();
+    return fail(NXQ_ERR_TIMEOUT, "device-side bounded wait expired (code %u at %u)", st.code, st.where);
 }
 
 int check_device_status() {

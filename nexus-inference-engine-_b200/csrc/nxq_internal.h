@@ -34,12 +34,33 @@ int cuda_fail(cudaError_t e, const char* what);
         if (e_ != cudaSuccess) return ::nxq::cuda_fail(e_, #call); \
     } while (0)
 
-// Device-side error word every bounded wait reports into (see tc kernels):
-// 0 = ok; nonzero = code of the wait that ran out.  Lives in the context.
+// Device-side error word of the context: 0 = ok, else the first error a
+// kernel raised (kStatusTimeout: a bounded wait ran out; kStatusRange: a
+// finite activation was too large for f16).  `where` says which wait or
+// conversion.  Read by the host after a synchronize (nxq_stream_sync,
+// nxq_qmatmul_host).
 struct DeviceStatus {
     unsigned int code;
     unsigned int where;
 };
+constexpr unsigned kStatusTimeout = 1u;
+constexpr unsigned kStatusRange = 2u;
+
+// True when a finite v rounds to an infinite f16 (|v| >= 65520): the
+// tensor-core kernels compute in f16, so such an activation would turn a
+// finite result into inf or NaN.
+__device__ __forceinline__ bool f16_overflows(float v) {
+    const float a = fabsf(v);
+    return a >= 65520.0f && a <= 3.402823466e38f;
+}
+// Records a range error (first error wins; `where` names the conversion).
+__device__ __forceinline__ void raise_range(DeviceStatus* st, unsigned where) {
+    if (st && atomicCAS(&st->code, 0u, kStatusRange) == 0u) st->where = where;
+}
+
+// The context's device status word and SM count (nxq_api.cu).
+DeviceStatus* context_status();
+int context_sm_count();
 
 // Process-wide count of kernels launched by the library (nxq_launch_count).
 void note_launches(unsigned n);

@@ -4,7 +4,7 @@
 // reference has no batched quantized GEMM at all (its prefill runs token by
 // token through gemm_int4, hybrid_model.cpp:608-633, and its fp32 fallback is
 // the Metal gemm_f32_tiled, gemm_dequant.metal:77-119); this kernel is the
-// prefill path of BASELINE config 4.
+// prefill path for batches of more than 32 tokens.
 //
 // Work: a persistent grid of one CTA per SM walks (weight tile, token tile)
 // work tiles of 128 weight rows x 256 tokens.  Per 64-element k-step:
@@ -380,13 +380,20 @@ bool type_ok(int type) {
 int gemm_init(int) {
     const char* env = getenv("NXQ_PREFILL_KERNEL");
     g_gemm_enabled = !(env && env[0] == 's');  // "simt" selects the CUDA-core kernel
+    if (!g_gemm_enabled) return NXQ_OK;
+    // The activation boxes are TMA copies described by a tensor map, which
+    // only the driver can encode.  Without that entry point the tensor-core
+    // GEMM cannot run; prefill would silently fall to the CUDA-core kernel,
+    // so initialisation fails instead (NXQ_PREFILL_KERNEL=simt asks for the
+    // CUDA-core kernel explicitly).
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
     cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) {
-        g_gemm_enabled = false;
-        return NXQ_OK;
-    }
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+        return fail(NXQ_ERR_UNSUPPORTED,
+                    "the driver does not provide cuTensorMapEncodeTiled (%s, query result %d): the tcgen05 "
+                    "prefill GEMM cannot run; set NXQ_PREFILL_KERNEL=simt to use the CUDA-core kernel",
+                    e == cudaSuccess ? "no error" : cudaGetErrorName(e), (int)q);
     g_encode = reinterpret_cast<EncodeTiledFn>(fn);
     int rc;
     if ((rc = set_attr<T_Q4_K>()) || (rc = set_attr<T_Q4_0>()) || (rc = set_attr<T_Q8_0>()) ||

@@ -693,8 +693,14 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
                     }
                 }
             };
-            auto bf2h = [](uint32_t w) {
-                return h2u(__float22half2_rn(__bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w))));
+            // A finite activation beyond the f16 range is reported in the
+            // status word (kStatusRange, where = 3) and still rounded (to inf).
+            bool over = false;
+            auto ovf2 = [&](float a, float b) { over |= f16_overflows(a) || f16_overflows(b); };
+            auto bf2h = [&](uint32_t w) {
+                const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+                ovf2(f.x, f.y);
+                return h2u(__float22half2_rn(f));
             };
             auto finish = [&](int u) {
                 uint4* xd = reinterpret_cast<uint4*>(xst + (u % S) * XB);
@@ -705,6 +711,10 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
                     const int tok = i >> 5, t4 = (i >> 3) & 3, m = i & 7;
                     uint4 h;
                     if (f32) {
+                        ovf2(ra[j].x, ra[j].y);
+                        ovf2(ra[j].z, ra[j].w);
+                        ovf2(rb[j].x, rb[j].y);
+                        ovf2(rb[j].z, rb[j].w);
                         h = make_uint4(h2u(__floats2half2_rn(ra[j].x, ra[j].y)), h2u(__floats2half2_rn(ra[j].z, ra[j].w)),
                                        h2u(__floats2half2_rn(rb[j].x, rb[j].y)), h2u(__floats2half2_rn(rb[j].z, rb[j].w)));
                     } else {
@@ -723,6 +733,7 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
                     issue(u);
                 }
                 if (u == n && n > 0) finish(n - 1);
+                if (over) raise_range(p.status, 3u);
             } else {
                 for (; u < n; ++u) {
                     if (!refill(u)) break;

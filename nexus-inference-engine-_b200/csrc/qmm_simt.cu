@@ -35,16 +35,17 @@ __device__ __forceinline__ void store_out(void* y, int dtype, int64_t i, float v
     }
 }
 
-// grid = (tiles, splits, ceil(M / MB)); block = 128 threads.
+// grid = (tiles, splits, token blocks of this launch); block = 128 threads.
+// Token block z of the launch covers rows m_base + z MB .. + MB - 1.
 template <int MB>
 __global__ void __launch_bounds__(TILE_ROWS) qmm_simt_kernel(
     const uint8_t* __restrict__ tiled, TiledShape s, const void* __restrict__ x, int x_dtype,
-    void* __restrict__ y, int y_dtype, int64_t M, float* __restrict__ partials, int splits) {
+    void* __restrict__ y, int y_dtype, int64_t M, float* __restrict__ partials, int splits, int64_t m_base) {
     __shared__ float xs[MB][CHUNK_K];
     const int r = threadIdx.x;
     const int64_t tile = blockIdx.x;
     const int split = blockIdx.y;
-    const int64_t m0 = (int64_t)blockIdx.z * MB;
+    const int64_t m0 = m_base + (int64_t)blockIdx.z * MB;
     const int mb = (int)(M - m0 < MB ? M - m0 : MB);
     const int64_t n = tile * TILE_ROWS + r;
     const int64_t c_begin = s.chunks * split / splits;
@@ -117,22 +118,30 @@ cudaError_t launch_qmm_simt(const uint8_t* tiled, const TiledShape& s, const voi
                             cudaStream_t st) {
     if (splits < 1) splits = 1;
     const int mb = simt_rows_per_pass(M);
-    dim3 grid((unsigned)s.tiles, (unsigned)splits, (unsigned)((M + mb - 1) / mb));
-    switch (mb) {
+    // The grid's z extent is at most 65535: more token blocks than that run
+    // as several launches, each starting at its own first token.
+    const int64_t zblocks = (M + mb - 1) / mb;
+    cudaError_t e = cudaSuccess;
+    for (int64_t z0 = 0; z0 < zblocks && e == cudaSuccess; z0 += 65535) {
+        const int64_t zn = zblocks - z0 < 65535 ? zblocks - z0 : 65535;
+        dim3 grid((unsigned)s.tiles, (unsigned)splits, (unsigned)zn);
+        const int64_t m_base = z0 * mb;
+        switch (mb) {
 #define NXQ_SIMT_CASE(MB)                                                                       \
     case MB:                                                                                    \
         qmm_simt_kernel<MB><<<grid, TILE_ROWS, 0, st>>>(tiled, s, x, x_dtype, y, y_dtype, M,     \
-                                                        partials, splits);                      \
+                                                        partials, splits, m_base);              \
         break;
-        NXQ_SIMT_CASE(1)
-        NXQ_SIMT_CASE(4)
-        NXQ_SIMT_CASE(8)
-        NXQ_SIMT_CASE(16)
-        NXQ_SIMT_CASE(kMaxMB)
+            NXQ_SIMT_CASE(1)
+            NXQ_SIMT_CASE(4)
+            NXQ_SIMT_CASE(8)
+            NXQ_SIMT_CASE(16)
+            NXQ_SIMT_CASE(kMaxMB)
 #undef NXQ_SIMT_CASE
+        }
+        e = cudaGetLastError();
+        note_launches(1);
     }
-    cudaError_t e = cudaGetLastError();
-    note_launches(1);
     if (e != cudaSuccess || splits == 1) return e;
     int64_t count = M * s.N;
     int64_t g = (count + 255) / 256;

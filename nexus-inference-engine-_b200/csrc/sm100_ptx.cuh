@@ -70,7 +70,7 @@ struct WaitCtl {
 
 static __device__ __noinline__ void raise_timeout(const WaitCtl& c, unsigned where) {
     *c.abort = 1;
-    if (atomicCAS(&c.status->code, 0u, 1u) == 0u) c.status->where = where;
+    if (atomicCAS(&c.status->code, 0u, kStatusTimeout) == 0u) c.status->where = where;
     __threadfence();
 }
 

@@ -10,7 +10,11 @@ namespace nxq {
 
 namespace {
 
-__global__ void to_half_kernel(const void* __restrict__ x, int dt, __half* __restrict__ out, int64_t n) {
+// Rounds fp32 / bf16 activations to f16; a finite value beyond the f16
+// range is reported in the status word (kStatusRange, where = 1).
+__global__ void to_half_kernel(const void* __restrict__ x, int dt, __half* __restrict__ out, int64_t n,
+                               DeviceStatus* status) {
+    bool over = false;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         float v;
         if (dt == NXQ_F32)
@@ -19,8 +23,10 @@ __global__ void to_half_kernel(const void* __restrict__ x, int dt, __half* __res
             v = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[i]);
         else
             v = __half2float(reinterpret_cast<const __half*>(x)[i]);
+        over |= f16_overflows(v);
         out[i] = __float2half_rn(v);
     }
+    if (over) raise_range(status, 1u);
 }
 
 std::mutex g_scratch_mu;
@@ -148,7 +154,8 @@ constexpr int kNormThreads = 512;
 // CTA), r = rsqrtf(sum / K + eps), then the scaled row.
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_to_half_kernel(const void* __restrict__ x, int dt,
                                                                      const float* __restrict__ w, float eps,
-                                                                     __half* __restrict__ out, int64_t K) {
+                                                                     __half* __restrict__ out, int64_t K,
+                                                                     DeviceStatus* status) {
     __shared__ float part[kNormThreads / 32];
     __shared__ float r_s;
     const int64_t row = blockIdx.x;
@@ -169,8 +176,13 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_to_half_kernel(const voi
     }
     __syncthreads();
     const float r = r_s;
-    for (int64_t i = threadIdx.x; i < K; i += kNormThreads)
-        out[row * K + i] = __float2half_rn(load_as(x, dt, row * K + i) * r * w[i]);
+    bool over = false;
+    for (int64_t i = threadIdx.x; i < K; i += kNormThreads) {
+        const float v = load_as(x, dt, row * K + i) * r * w[i];
+        over |= f16_overflows(v);
+        out[row * K + i] = __float2half_rn(v);
+    }
+    if (over) raise_range(status, 2u);
 }
 
 unsigned elementwise_grid(int64_t n) {
@@ -188,7 +200,7 @@ cudaError_t launch_swiglu(const float* g, const float* u, void* h, int h_dtype, 
 
 cudaError_t launch_rmsnorm_to_half(const void* x, int x_dtype, const float* w, float eps, __half* out, int64_t M,
                                    int64_t K, cudaStream_t st) {
-    rmsnorm_to_half_kernel<<<(unsigned)M, kNormThreads, 0, st>>>(x, x_dtype, w, eps, out, K);
+    rmsnorm_to_half_kernel<<<(unsigned)M, kNormThreads, 0, st>>>(x, x_dtype, w, eps, out, K, context_status());
     note_launches(1);
     return cudaGetLastError();
 }
@@ -203,7 +215,7 @@ cudaError_t launch_to_half(const void* x, int dtype, __half* out, int64_t n, cud
     int64_t g = (n + 255) / 256;
     if (g > 4096) g = 4096;
     if (g < 1) g = 1;
-    to_half_kernel<<<(unsigned)g, 256, 0, st>>>(x, dtype, out, n);
+    to_half_kernel<<<(unsigned)g, 256, 0, st>>>(x, dtype, out, n, context_status());
     note_launches(1);
     return cudaGetLastError();
 }

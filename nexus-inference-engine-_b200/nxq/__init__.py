@@ -40,7 +40,7 @@ SPLIT_COL, SPLIT_ROW = 0, 1
 
 STATUS = {0: "OK", -1: "ERR_ARG", -2: "ERR_CODEC", -3: "ERR_SHAPE", -4: "ERR_CUDA",
           -5: "ERR_TIMEOUT", -6: "ERR_NOMEM", -7: "ERR_STATE", -8: "ERR_NCCL", -9: "ERR_UNSUPPORTED",
-          -10: "ERR_FORMAT"}
+          -10: "ERR_FORMAT", -11: "ERR_RANGE"}
 
 
 class NxqError(RuntimeError):

@@ -347,3 +347,60 @@ def test_other_types_run_on_the_tensor_core_kernels(gpu, t):
             assert gpu.kernel_name(w, M) == name
     finally:
         w.release()
+
+
+@pytest.mark.parametrize("M,x_dt", [(1, "f32"), (2, "bf16"), (4, "f32"), (64, "f32"), (64, "bf16")])
+def test_activation_beyond_f16_range_is_reported(gpu, M, x_dt):
+    """The tensor-core kernels compute in f16.  An fp32 / bf16 activation of
+    magnitude >= 65520 has no f16 value (the CPU oracle's fp32 result stays
+    finite), so the call is reported as NXQ_ERR_RANGE at the next
+    synchronization - from the GEMV's own staging (M <= 2), the conversion
+    kernel (M > 2) and before the prefill GEMM (M > 32).  65519 rounds to
+    65504 and is accepted.  The context is usable afterwards."""
+    torch = _torch()
+    dt = {"f32": torch.float32, "bf16": torch.bfloat16}[x_dt]
+    t, N, K = 12, 256, 1024
+    blocks = synth.make_blocks(t, N, K, seed=90)
+    w = gpu.Weight.register(blocks, t, N, K)
+    try:
+        x = torch.from_numpy(synth.make_activations(M, K, seed=91, dtype=np.float32))
+        big = x.clone()
+        big[M - 1, 17] = 1.0e5 if x_dt == "f32" else 6.6e4
+        gpu.qmatmul(w, big.to(dt).cuda())
+        torch.cuda.synchronize()
+        with pytest.raises(gpu.NxqError) as ei:
+            gpu.stream_sync()
+        assert ei.value.code == -11 and "f16 range" in str(ei.value)
+        if x_dt == "f32":
+            edge = x.clone()
+            edge[M - 1, 17] = 65519.0
+            gpu.qmatmul(w, edge.cuda())
+            torch.cuda.synchronize()
+            gpu.stream_sync()
+        y = gpu.qmatmul(w, x.to(dt).cuda())
+        torch.cuda.synchronize()
+        gpu.stream_sync()
+        want = loader.qmatmul(t, blocks, N, K, x.to(dt).float().numpy())
+        assert synth.rel_l2(y.cpu().numpy(), want) < TOL
+    finally:
+        w.release()
+
+
+def test_rmsnorm_output_beyond_f16_range_is_reported(gpu):
+    """The RMSNorm prologue rounds the normalized row to f16: a norm weight
+    that takes it past 65519 is reported as NXQ_ERR_RANGE."""
+    torch = _torch()
+    t, N, K, M = 12, 256, 1024, 2
+    w = gpu.Weight.register(synth.make_blocks(t, N, K, seed=92), t, N, K)
+    try:
+        x = torch.from_numpy(synth.make_activations(M, K, seed=93, dtype=np.float32)).cuda()
+        norm = torch.full((K,), 1.0e6, dtype=torch.float32, device="cuda")
+        y = torch.empty(M, N, dtype=torch.float32, device="cuda")
+        gpu.rmsnorm_qmatmul([w], x, norm, 1e-5, outs=[y])
+        torch.cuda.synchronize()
+        with pytest.raises(gpu.NxqError) as ei:
+            gpu.stream_sync()
+        assert ei.value.code == -11
+        gpu.stream_sync()
+    finally:
+        w.release()
