@@ -268,6 +268,26 @@ NXQ_API int nxq_qmatmul_host(nxq_weight_t w, const float* x_host, float* y_host,
  * (NXQ_ERR_RANGE). */
 NXQ_API int nxq_stream_sync(void* stream);
 
+/* Limit of every bounded device-side wait on another thread's progress (a
+ * copy landing, a stream-K partial sum arriving), in microseconds; 0 restores
+ * the default of about 2 s.  A wait that runs out ends its kernel with
+ * NXQ_ERR_TIMEOUT at the next nxq_stream_sync instead of hanging the GPU; a
+ * short limit detects a lost arrival sooner.  Synchronizes the device.  No
+ * counterpart in the reference (its Metal command buffers have no
+ * device-side waits). */
+NXQ_API int nxq_set_wait_limit(uint64_t microseconds);
+
+/* Test hooks for failure-detection tests: they make a bounded wait run out on
+ * purpose (nothing faults, traps or waits beyond the limit).  Off by default;
+ * each call synchronizes the device.
+ *   NXQ_HOOK_STREAMK_SKIP_COUNT: in the decode GEMV's stream-K split, the CTAs
+ *     that publish a partial sum of a row tile another CTA finishes do not
+ *     count themselves in, so that CTA's wait for the counts runs out
+ *     (NXQ_ERR_TIMEOUT; that call's output is incomplete).  No counterpart in
+ *     the reference. */
+typedef enum { NXQ_HOOK_STREAMK_SKIP_COUNT = 1, NXQ_HOOK_TP_STREAM_PENDING = 2 } nxq_test_hook_id;
+NXQ_API int nxq_test_hook(int hook, int on);
+
 /* Name of the kernel nxq_qmatmul would launch for (w, M, dtypes), e.g.
  * "tc_gemv<Q4_K,n32>" or "simt<Q3_K,mb8>".  Profiling aid; the reference's
  * counterpart is the pipeline-name log of metal_context_impl.h:77-78. */
@@ -299,8 +319,27 @@ NXQ_API int nxq_tp_shutdown(void);
 NXQ_API int nxq_tp_qmatmul(nxq_weight_t shard, const void* x_dev, int x_dtype, void* y_dev,
                            int y_dtype, int64_t M, int split, void* stream);
 
-/* Sum `count` fp32 values across the TP group in place on `stream`. */
+/* Sum `count` fp32 values across the TP group in place on `stream`.  A
+ * collective that fails to enqueue aborts the communicator (NXQ_ERR_NCCL). */
 NXQ_API int nxq_tp_allreduce_f32(float* buf_dev, int64_t count, void* stream);
+
+/* Failure detection for the TP group (the reference has one device and
+ * zero-fills silently, compute_dispatch.cpp:174-176): waits until the work
+ * queued on `stream` (matmuls and allreduces) has finished, polling the stream
+ * and ncclCommGetAsyncError.  If NCCL reports an error, the stream fails, or
+ * timeout_ms passes first (a peer that left never joins its collective), the
+ * communicator is aborted (ncclCommAbort, which ends the NCCL kernels still
+ * waiting) and NXQ_ERR_NCCL / NXQ_ERR_CUDA / NXQ_ERR_TIMEOUT is returned; from
+ * then on every TP call returns NXQ_ERR_STATE until nxq_tp_shutdown and a new
+ * nxq_tp_init.  Every TP call also checks for a pending asynchronous NCCL
+ * error first.  Host-only logic apart from the stream query. */
+NXQ_API int nxq_tp_wait(void* stream, int64_t timeout_ms);
+
+/* Host-side test hook of the TP layer (needs no GPU):
+ *   NXQ_HOOK_TP_STREAM_PENDING: nxq_tp_wait sees the stream as still running,
+ *     as it would while a collective waits for a peer that left, so its
+ *     deadline path runs. */
+NXQ_API int nxq_tp_test_hook(int hook, int on);
 
 /* ---- residency loader: GGUF v2/v3 files straight into HBM ---------------------
  * Replaces the reference's import path (GGUFImporter::parse_gguf,

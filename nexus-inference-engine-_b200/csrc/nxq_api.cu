@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cstddef>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -87,7 +88,8 @@ int grow(void** buf, size_t* have, size_t need) {
 // (NXQ_ERR_RANGE).  The word is cleared once reported.
 int report_status(const DeviceStatus& st) {
     if (!st.code) return NXQ_OK;
-    cudaMemset(g_ctx.status, 0, sizeof(DeviceStatus));
+    // Clear the error (code and where); the settings after it stay.
+    cudaMemset(g_ctx.status, 0, 2 * sizeof(unsigned));
     if (st.code == kStatusRange) {
         static const char* const what[] = {"?", "the f16 conversion of fp32/bf16 activations",
                                            "the RMSNorm prologue", "the decode GEMV's activation staging"};
@@ -293,7 +295,11 @@ NXQ_API int nxq_init(int device) {
     g_ctx.smem_optin = p.sharedMemPerBlockOptin;
     NXQ_CUDA(cudaStreamCreateWithFlags(&g_ctx.host_stream, cudaStreamNonBlocking));
     NXQ_CUDA(cudaMalloc(&g_ctx.status, sizeof(DeviceStatus)));
-    NXQ_CUDA(cudaMemset(g_ctx.status, 0, sizeof(DeviceStatus)));
+    {
+        DeviceStatus init{};
+        init.wait_cycles = kDefaultWaitCycles;
+        NXQ_CUDA(cudaMemcpy(g_ctx.status, &init, sizeof init, cudaMemcpyHostToDevice));
+    }
     NXQ_CUDA(cudaMallocHost(&g_ctx.status_host, sizeof(DeviceStatus)));
     // Keep stream-ordered scratch in the pool between calls instead of
     // returning it to the driver after every synchronize.
@@ -669,6 +675,36 @@ NXQ_API int nxq_qmatmul_kernel_name(nxq_weight_t h, int64_t M, int x_dtype, int 
 NXQ_API int nxq_launch_count(uint64_t* out) {
     if (!out) return fail(NXQ_ERR_ARG, "null argument");
     *out = g_launches.load(std::memory_order_relaxed);
+    return NXQ_OK;
+}
+
+NXQ_API int nxq_set_wait_limit(uint64_t microseconds) {
+    int rc = check_ready();
+    if (rc) return rc;
+    if (microseconds > 60ull * 1000 * 1000) return fail(NXQ_ERR_ARG, "wait limit above 60 s");
+    // Converted at 2 cycles per ns (the SM clock is at most 1965 MHz, so the
+    // wait lasts at least this long).
+    const long long cycles = microseconds ? (long long)microseconds * 2000 : kDefaultWaitCycles;
+    cudaDeviceSynchronize();
+    NXQ_CUDA(cudaMemcpy(reinterpret_cast<char*>(g_ctx.status) + offsetof(DeviceStatus, wait_cycles), &cycles,
+                        sizeof cycles, cudaMemcpyHostToDevice));
+    return NXQ_OK;
+}
+
+NXQ_API int nxq_test_hook(int hook, int on) {
+    int rc = check_ready();
+    if (rc) return rc;
+    unsigned bit = 0;
+    switch (hook) {
+        case NXQ_HOOK_STREAMK_SKIP_COUNT: bit = kHookStreamKSkipCount; break;
+        default: return fail(NXQ_ERR_ARG, "unknown test hook %d", hook);
+    }
+    cudaDeviceSynchronize();
+    unsigned hooks = 0;
+    char* at = reinterpret_cast<char*>(g_ctx.status) + offsetof(DeviceStatus, hooks);
+    NXQ_CUDA(cudaMemcpy(&hooks, at, sizeof hooks, cudaMemcpyDeviceToHost));
+    hooks = on ? (hooks | bit) : (hooks & ~bit);
+    NXQ_CUDA(cudaMemcpy(at, &hooks, sizeof hooks, cudaMemcpyHostToDevice));
     return NXQ_OK;
 }
 

@@ -39,12 +39,26 @@ int cuda_fail(cudaError_t e, const char* what);
 // finite activation was too large for f16).  `where` says which wait or
 // conversion.  Read by the host after a synchronize (nxq_stream_sync,
 // nxq_qmatmul_host).
+// The same device allocation also holds the settings kernels read on their
+// slow paths: the limit of a bounded wait on another CTA's progress (in SM
+// clock cycles; nxq_set_wait_limit) and test hooks (nxq_test_hook).  Drain
+// waits (letting a CTA's own copies land before it exits) always use the
+// fixed kDrainWaitCycles.
 struct DeviceStatus {
     unsigned int code;
     unsigned int where;
+    long long wait_cycles;
+    unsigned int hooks;  // kHook* bits
+    unsigned int pad;
 };
 constexpr unsigned kStatusTimeout = 1u;
 constexpr unsigned kStatusRange = 2u;
+constexpr long long kDefaultWaitCycles = 4000000000LL;  // ~2 s at 2 GHz
+constexpr long long kDrainWaitCycles = 4000000000LL;
+// Test hook: CTAs of a stream-K launch that publish a partial sum for a tile
+// another CTA finishes do not count themselves in, so that CTA's bounded wait
+// for the counts runs out (a lost arrival, made on purpose and bounded).
+constexpr unsigned kHookStreamKSkipCount = 1u;
 
 // True when a finite v rounds to an infinite f16 (|v| >= 65520): the
 // tensor-core kernels compute in f16, so such an activation would turn a

@@ -881,7 +881,8 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
                     named_sync(3, kThreads);
                     if (tid == 0) {
                         __threadfence();  // the group's partial (ordered by the barrier) before the count
-                        atomicAdd(cn, 1u);
+                        const unsigned hooks = *reinterpret_cast<const volatile unsigned*>(&p.status->hooks);
+                        if (!(hooks & kHookStreamKSkipCount)) atomicAdd(cn, 1u);
                     }
                 } else {
                     // Wait (bounded) for the b1 - b0 counts, then add the
@@ -889,13 +890,13 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
                     // whatever the timing.
                     if (tid == 0) {
                         const unsigned need = (unsigned)(b1 - b0);
-                        const long long w0 = clock64();
+                        const long long w0 = clock64(), lim = ptx::wait_limit(p.status);
                         int ok = 1;
                         for (;;) {
                             unsigned v;
                             asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(cn) : "memory");
                             if (v >= need) break;
-                            if (*ctl.abort || clock64() - w0 > ptx::kWaitCycles) {
+                            if (*ctl.abort || clock64() - w0 > lim) {
                                 if (!*ctl.abort) ptx::raise_timeout(ctl, 34);
                                 ok = 0;
                                 break;

@@ -15,8 +15,16 @@
 namespace nxq {
 namespace ptx {
 
-// ~2 s at 2 GHz; far above any legitimate wait in these kernels.
-constexpr long long kWaitCycles = 4000000000LL;
+// Fixed limit of drain waits (a CTA's own copies in flight): ~2 s at 2 GHz.
+// Waits on other threads' progress use the context's runtime limit
+// (DeviceStatus::wait_cycles, default the same ~2 s).
+constexpr long long kWaitCycles = kDrainWaitCycles;
+
+// The runtime wait limit, read from global memory on a wait's slow path.
+__device__ __forceinline__ long long wait_limit(const DeviceStatus* st) {
+    const long long v = *reinterpret_cast<const volatile long long*>(&st->wait_cycles);
+    return v > 0 ? v : kDefaultWaitCycles;
+}
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -80,10 +88,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
                                           unsigned where) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
+    const long long lim = wait_limit(c.status);
     while (true) {
         if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
         if (*c.abort) return false;
-        if (clock64() - t0 > kWaitCycles) {
+        if (clock64() - t0 > lim) {
             raise_timeout(c, where);
             return false;
         }

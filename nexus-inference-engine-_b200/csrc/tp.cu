@@ -6,14 +6,28 @@
 //                         the fp32 partial outputs are summed by ncclAllReduce.
 //
 // NCCL is resolved at run time (dlopen of libnccl.so.2, preferring the copy
-// already loaded into the process, e.g. by torch.distributed), so libnxq.so
-// has no link-time NCCL dependency and the single-GPU entry points work
-// without it.
+// already loaded into the process, e.g. by torch.distributed; NXQ_NCCL_LIB
+// names another library), so libnxq.so has no link-time NCCL dependency and
+// the single-GPU entry points work without it.
+//
+// Failure detection.  The reference has a single device and silently
+// zero-fills on failure (compute_dispatch.cpp:174-176).  Here a collective
+// whose peer has died never completes on its own, so nxq_tp_wait polls the
+// stream and ncclCommGetAsyncError until the work is done, NCCL reports an
+// error, or a deadline passes; in the last two cases it aborts the
+// communicator (ncclCommAbort ends the NCCL kernels still waiting) and every
+// later TP call fails with NXQ_ERR_STATE until nxq_tp_shutdown and a new
+// nxq_tp_init.  Every TP call also checks for an asynchronous error first.
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <atomic>
+#include <chrono>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <thread>
 
 #include "qmm_tc.h"
 
@@ -42,10 +56,19 @@ NcclApi g_nccl;
 std::mutex g_tp_mu;
 ncclComm_t g_comm = nullptr;
 int g_rank = -1, g_world = 0;
+bool g_dead = false;  // the communicator was aborted: TP calls fail until shutdown + init
+char g_dead_why[256] = "";
+std::atomic<bool> g_hook_stream_pending{false};  // NXQ_HOOK_TP_STREAM_PENDING
 
 int load_nccl() {
     if (g_nccl.lib) return NXQ_OK;
-    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    void* h = nullptr;
+    const char* forced = getenv("NXQ_NCCL_LIB");
+    if (forced && forced[0]) {
+        h = dlopen(forced, RTLD_NOW | RTLD_LOCAL);
+        if (!h) return fail(NXQ_ERR_NCCL, "cannot load NXQ_NCCL_LIB=%s: %s", forced, dlerror());
+    }
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
     if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
     if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
     if (!h) return fail(NXQ_ERR_NCCL, "cannot load libnccl.so.2: %s", dlerror());
@@ -66,6 +89,30 @@ int load_nccl() {
 
 int nccl_fail(ncclResult_t r, const char* what) {
     return fail(NXQ_ERR_NCCL, "%s: %s", what, g_nccl.GetErrorString ? g_nccl.GetErrorString(r) : "?");
+}
+
+// Aborts the communicator (caller holds g_tp_mu); later TP calls fail.
+int abort_comm(int status, const char* why) {
+    if (g_comm && !g_dead) g_nccl.CommAbort(g_comm);
+    g_dead = true;
+    snprintf(g_dead_why, sizeof g_dead_why, "%s", why);
+    return fail(status, "%s; the TP communicator was aborted (nxq_tp_shutdown, then nxq_tp_init, to rejoin)", why);
+}
+
+// A usable communicator with no pending asynchronous error (caller holds
+// g_tp_mu); aborts it when NCCL reports one.
+int check_comm() {
+    if (!g_comm) return fail(NXQ_ERR_STATE, "nxq_tp_init has not been called");
+    if (g_dead) return fail(NXQ_ERR_STATE, "the TP communicator was aborted earlier (%s)", g_dead_why);
+    ncclResult_t async_err = ncclSuccess;
+    ncclResult_t r = g_nccl.CommGetAsyncError(g_comm, &async_err);
+    if (r != ncclSuccess) return abort_comm(NXQ_ERR_NCCL, "ncclCommGetAsyncError failed");
+    if (async_err != ncclSuccess && async_err != ncclInProgress) {
+        char why[200];
+        snprintf(why, sizeof why, "NCCL reported an asynchronous error: %s", g_nccl.GetErrorString(async_err));
+        return abort_comm(NXQ_ERR_NCCL, why);
+    }
+    return NXQ_OK;
 }
 
 int check_weight_ptr(nxq_weight_t h, const Weight** out) {
@@ -109,29 +156,75 @@ NXQ_API int nxq_tp_init(int rank, int world, const void* unique_id, size_t n) {
     }
     g_rank = rank;
     g_world = world;
+    g_dead = false;
+    g_dead_why[0] = 0;
     return NXQ_OK;
 }
 
 NXQ_API int nxq_tp_shutdown(void) {
     std::lock_guard<std::mutex> lk(g_tp_mu);
     if (!g_comm) return NXQ_OK;
-    ncclResult_t async_err = ncclSuccess;
-    g_nccl.CommGetAsyncError(g_comm, &async_err);
-    // A communicator with a pending error cannot be destroyed cleanly.
-    ncclResult_t r = async_err == ncclSuccess ? g_nccl.CommDestroy(g_comm) : g_nccl.CommAbort(g_comm);
+    ncclResult_t r = ncclSuccess;
+    if (!g_dead) {
+        ncclResult_t async_err = ncclSuccess;
+        g_nccl.CommGetAsyncError(g_comm, &async_err);
+        // A communicator with a pending error cannot be destroyed cleanly.
+        r = async_err == ncclSuccess ? g_nccl.CommDestroy(g_comm) : g_nccl.CommAbort(g_comm);
+    }
     g_comm = nullptr;
     g_rank = -1;
     g_world = 0;
+    g_dead = false;
     if (r != ncclSuccess) return nccl_fail(r, "ncclCommDestroy");
     return NXQ_OK;
 }
 
 NXQ_API int nxq_tp_allreduce_f32(float* buf_dev, int64_t count, void* stream) {
     if (!buf_dev || count < 0) return fail(NXQ_ERR_ARG, "bad buffer");
-    if (!g_comm) return fail(NXQ_ERR_STATE, "nxq_tp_init has not been called");
+    std::lock_guard<std::mutex> lk(g_tp_mu);
+    if (int rc = check_comm()) return rc;
     ncclResult_t r = g_nccl.AllReduce(buf_dev, buf_dev, (size_t)count, ncclFloat32, ncclSum, g_comm,
                                       (cudaStream_t)stream);
-    if (r != ncclSuccess) return nccl_fail(r, "ncclAllReduce");
+    if (r != ncclSuccess) {
+        // A collective that failed to enqueue on this rank leaves the others
+        // waiting for it: abort rather than leave the group half-entered.
+        char why[200];
+        snprintf(why, sizeof why, "ncclAllReduce failed: %s", g_nccl.GetErrorString(r));
+        return abort_comm(NXQ_ERR_NCCL, why);
+    }
+    return NXQ_OK;
+}
+
+NXQ_API int nxq_tp_wait(void* stream, int64_t timeout_ms) {
+    if (timeout_ms < 0) return fail(NXQ_ERR_ARG, "negative timeout");
+    using clk = std::chrono::steady_clock;
+    const auto deadline = clk::now() + std::chrono::milliseconds(timeout_ms);
+    for (int polls = 0;; ++polls) {
+        {
+            std::lock_guard<std::mutex> lk(g_tp_mu);
+            if (int rc = check_comm()) return rc;
+            cudaError_t q = g_hook_stream_pending.load() ? cudaErrorNotReady : cudaStreamQuery((cudaStream_t)stream);
+            if (q == cudaSuccess) return NXQ_OK;
+            if (q != cudaErrorNotReady) {
+                cudaGetLastError();
+                char why[200];
+                snprintf(why, sizeof why, "the TP stream failed: %s", cudaGetErrorName(q));
+                return abort_comm(NXQ_ERR_CUDA, why);
+            }
+            if (clk::now() >= deadline) {
+                char why[200];
+                snprintf(why, sizeof why, "TP work on the stream did not finish within %lld ms (a peer may have "
+                         "left)", (long long)timeout_ms);
+                return abort_comm(NXQ_ERR_TIMEOUT, why);
+            }
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(polls < 100 ? 20 : 1000));
+    }
+}
+
+NXQ_API int nxq_tp_test_hook(int hook, int on) {
+    if (hook != NXQ_HOOK_TP_STREAM_PENDING) return fail(NXQ_ERR_ARG, "unknown TP test hook %d", hook);
+    g_hook_stream_pending.store(on != 0);
     return NXQ_OK;
 }
 
@@ -141,7 +234,10 @@ NXQ_API int nxq_tp_qmatmul(nxq_weight_t shard, const void* x_dev, int x_dtype, v
     int rc = check_weight_ptr(shard, &w);
     if (rc) return rc;
     if (split != NXQ_SPLIT_COL && split != NXQ_SPLIT_ROW) return fail(NXQ_ERR_ARG, "bad split");
-    if (!g_comm) return fail(NXQ_ERR_STATE, "nxq_tp_init has not been called");
+    {
+        std::lock_guard<std::mutex> lk(g_tp_mu);
+        if (int crc = check_comm()) return crc;
+    }
     if (split == NXQ_SPLIT_ROW && y_dtype != NXQ_F32)
         return fail(NXQ_ERR_ARG, "ROW split produces fp32 partial sums; y_dtype must be NXQ_F32");
     rc = nxq_qmatmul(shard, x_dev, x_dtype, y_dev, y_dtype, M, stream);

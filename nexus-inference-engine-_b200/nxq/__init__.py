@@ -89,6 +89,10 @@ _SIGS = {
     "nxq_qmatmul_noalloc": [_c.c_void_p, _c.c_void_p, _c.c_int, _c.c_void_p, _c.c_int, _c.c_int64,
                             _c.c_void_p],
     "nxq_stream_sync": [_c.c_void_p],
+    "nxq_set_wait_limit": [_c.c_uint64],
+    "nxq_test_hook": [_c.c_int, _c.c_int],
+    "nxq_tp_wait": [_c.c_void_p, _c.c_int64],
+    "nxq_tp_test_hook": [_c.c_int, _c.c_int],
     "nxq_qmatmul_kernel_name": [_c.c_void_p, _c.c_int64, _c.c_int, _c.c_int, _c.c_char_p, _c.c_size_t],
     "nxq_launch_count": [_c.POINTER(_c.c_uint64)],
     "nxq_tp_unique_id_size": [],
@@ -395,6 +399,19 @@ def stream_sync(stream=None) -> None:
     _check(lib().nxq_stream_sync(_stream_ptr(stream)))
 
 
+def set_wait_limit(microseconds: int) -> None:
+    """Limit of every bounded device-side wait (0 = the default, about 2 s)."""
+    _check(lib().nxq_set_wait_limit(microseconds))
+
+
+HOOK_STREAMK_SKIP_COUNT = 1
+
+
+def test_hook(hook: int, on: bool) -> None:
+    """Failure-detection test hooks (nxq_test_hook); off by default."""
+    _check(lib().nxq_test_hook(hook, 1 if on else 0))
+
+
 def kernel_name(w: Weight, M: int, x_dtype: int = F16, y_dtype: int = F32) -> str:
     """The kernel nxq_qmatmul launches for this weight, M and dtypes."""
     buf = ctypes.create_string_buffer(128)
@@ -663,6 +680,15 @@ def tp_qmatmul(shard: Weight, x, out, split: int, stream=None):
     _check(lib().nxq_tp_qmatmul(shard.handle, x.data_ptr(), _dtype_code(x.dtype), out.data_ptr(),
                                 _dtype_code(out.dtype), M, split, _stream_ptr(stream)))
     return out
+
+
+def tp_wait(stream=None, timeout_ms: int = 10000) -> None:
+    """Wait for the TP work on `stream`; aborts the communicator on an NCCL
+    error or when the deadline passes (nxq_tp_wait)."""
+    _check(lib().nxq_tp_wait(_stream_ptr(stream), timeout_ms))
+
+
+HOOK_TP_STREAM_PENDING = 2
 
 
 def tp_allreduce_f32(buf, stream=None):

@@ -404,3 +404,41 @@ def test_rmsnorm_output_beyond_f16_range_is_reported(gpu):
         gpu.stream_sync()
     finally:
         w.release()
+
+
+def test_streamk_wait_runs_out_and_the_context_recovers(gpu):
+    """Failure detection on the GPU without a fault: with a 2 ms wait limit
+    and the stream-K publishers told not to count themselves in, the CTA that
+    finishes a shared row tile waits for counts that never come; its bounded
+    wait runs out, the kernel ends, and the next synchronization reports
+    NXQ_ERR_TIMEOUT.  With the hook off and the limit back to default, the
+    next ordinary call on the same stream is correct (the host cleared the
+    tile counters when it reported the timeout)."""
+    torch = _torch()
+    t, N, K, M = 12, 14336, 4096, 1  # 112 row tiles x 16 chunks over 148 SMs: stream-K
+    blocks = synth.make_blocks(t, N, K, seed=95)
+    w = gpu.Weight.register(blocks, t, N, K)
+    stream = torch.cuda.Stream()
+    try:
+        x = torch.from_numpy(synth.make_activations(M, K, seed=96)).cuda()
+        want = loader.qmatmul(t, blocks, N, K, x.float().cpu().numpy())
+        y = torch.empty(M, N, device="cuda")
+        gpu.qmatmul(w, x, out=y, stream=stream)  # sizes this stream's stream-K scratch
+        gpu.stream_sync(stream)
+        assert synth.rel_l2(y.cpu().numpy(), want) < TOL
+        gpu.set_wait_limit(2000)
+        gpu.test_hook(gpu.HOOK_STREAMK_SKIP_COUNT, True)
+        try:
+            gpu.qmatmul(w, x, out=y, stream=stream)
+            with pytest.raises(gpu.NxqError) as ei:
+                gpu.stream_sync(stream)
+            assert ei.value.code == -5 and "bounded wait" in str(ei.value)
+        finally:
+            gpu.test_hook(gpu.HOOK_STREAMK_SKIP_COUNT, False)
+            gpu.set_wait_limit(0)
+        y.fill_(float("nan"))
+        gpu.qmatmul(w, x, out=y, stream=stream)
+        gpu.stream_sync(stream)
+        assert synth.rel_l2(y.cpu().numpy(), want) < TOL
+    finally:
+        w.release()
