@@ -23,6 +23,8 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 OUT = PKG / "nxq" / "libnxq.so"
+SHIM_SRC = PKG / "shim" / "compute_dispatch_nxq.cpp"
+SHIM_OUT = PKG / "nxq" / "libnxq_dispatch.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -104,7 +106,25 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    build_shim(force=force, verbose=verbose)
     return OUT
+
+
+def build_shim(force: bool = False, verbose: bool = False) -> Path:
+    """The C++ ComputeDispatch shim (shim/compute_dispatch_nxq.cpp) as
+    nxq/libnxq_dispatch.so, linked against libnxq.so beside it."""
+    deps = [SHIM_SRC, SHIM_SRC.with_suffix(".h"), ROOT / "include" / "nxq.h", OUT]
+    if not force and SHIM_OUT.exists() and all(p.stat().st_mtime <= SHIM_OUT.stat().st_mtime for p in deps):
+        return SHIM_OUT
+    cmd = [shutil.which("g++") or "g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra",
+           "-o", str(SHIM_OUT), str(SHIM_SRC), f"-I{ROOT / 'include'}", f"-L{OUT.parent}", "-lnxq",
+           "-Wl,-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd))
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"shim build failed:\n{r.stdout}\n{r.stderr}")
+    return SHIM_OUT
 
 
 def main() -> int:
