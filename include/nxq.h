@@ -86,7 +86,20 @@ typedef enum {
     NXQ_TYPE_I4G32 = 101,
     NXQ_TYPE_I4G64 = 102,
     NXQ_TYPE_I4G128 = 104,
-    NXQ_TYPE_I4G256 = 108
+    NXQ_TYPE_I4G256 = 108,
+    /* NXF chunks the reference's engine decodes at load time
+     * (HybridModel::Impl::load_tensor, hybrid_model.cpp:145-265), as blocks of
+     * 32 consecutive elements along K of the chunk's flat [N][K] array:
+     *   NXQ_TYPE_NXF_I8   Codec::INT8: 32 int8 codes, w = (float)q / 127
+     *                     (hybrid_model.cpp:248-255); decode GEMV and prefill
+     *                     GEMM as Q8_0 with the scale fl16(1/127)
+     *   NXQ_TYPE_NXF_F16  Codec::FP16: 32 halves, subnormals read as zero
+     *                     (hybrid_model.cpp:192-210); CUDA-core kernel
+     *   NXQ_TYPE_NXF_F32  Codec::FP32, or any chunk of 4 bytes per element
+     *                     (hybrid_model.cpp:165-176): 32 floats; CUDA-core kernel */
+    NXQ_TYPE_NXF_I8 = 120,
+    NXQ_TYPE_NXF_F16 = 121,
+    NXQ_TYPE_NXF_F32 = 122
 } nxq_type;
 
 /* Activation / output element types: nexus::DType F32=0, F16=1, BF16=2
@@ -417,8 +430,12 @@ NXQ_API int nxq_gguf_register_shard(nxq_gguf_t g, int64_t i, int64_t slice, int 
  * Registered codecs (Codec, core/config.h:21-36): INT4 = 4 - a chunk is
  * [4-bit codes in NXQ_INT4_ROWS order][fp32 scales][fp32 zeros] per group of
  * the descriptor's group size (32, 64, 128), as GGUFImporter writes it
- * (import/gguf_importer.cpp:1144-1170) - and the GGUF-block passthroughs
- * Q3K = 11, Q4K = 12, Q2K = 13.  Parsing needs no GPU; registration needs
+ * (import/gguf_importer.cpp:1144-1170) -, the GGUF-block passthroughs
+ * Q3K = 11, Q4K = 12, Q2K = 13, and the flat arrays the engine decodes at
+ * load time (hybrid_model.cpp:165-255): INT8 = 3 (w = q / 127), FP16 = 1
+ * (subnormals read as zero) and FP32 = 0, also any chunk of 4 bytes per
+ * element (the writer's small-tensor passthrough), as NXQ_TYPE_NXF_I8 / F16 /
+ * F32 (K a multiple of 32).  Parsing needs no GPU; registration needs
  * nxq_init.  A malformed or truncated file, or a checksum mismatch, is
  * NXQ_ERR_FORMAT; another codec is NXQ_ERR_CODEC. */
 typedef struct nxq_nxf_s* nxq_nxf_t;

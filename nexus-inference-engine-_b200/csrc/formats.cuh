@@ -38,8 +38,22 @@ enum BlockType : int {
     // (quant/gptq.cpp:9-27: w = (q - zero) * scale), as blocks of one group:
     // [scale f32][zero f32][gs/2 code bytes, element 2i low / 2i+1 high nibble
     // of byte i].  Ids outside the GGUF range: 100 + gs / 32.
-    T_I4G32 = 101, T_I4G64 = 102, T_I4G128 = 104, T_I4G256 = 108
+    T_I4G32 = 101, T_I4G64 = 102, T_I4G128 = 104, T_I4G256 = 108,
+    // NXF chunks decoded by the reference's engine at load time
+    // (hybrid_model.cpp:190-255), as blocks of 32 consecutive elements along
+    // K of the chunk's flat [N][K] array:
+    //   T_NXF_I8   Codec::INT8, 32 int8 codes, w = (float)q / 127
+    //   T_NXF_F16  Codec::FP16, 32 IEEE halves, subnormals read as zero
+    //   T_NXF_F32  Codec::FP32 (and any chunk of 4 bytes per element), 32 floats
+    T_NXF_I8 = 120, T_NXF_F16 = 121, T_NXF_F32 = 122
 };
+
+__host__ __device__ constexpr bool is_nxf_flat(int type) {
+    return type == T_NXF_I8 || type == T_NXF_F16 || type == T_NXF_F32;
+}
+// The f16 value of 1/127 (0x2008 = 0.0078735...): the scale every tiled
+// T_NXF_I8 block carries so the tensor-core kernels read it as Q8_0.
+constexpr uint16_t kNxfI8ScaleHalf = 0x2008;
 
 __host__ __device__ constexpr bool is_i4g(int type) {
     return type == T_I4G32 || type == T_I4G64 || type == T_I4G128 || type == T_I4G256;
@@ -70,11 +84,15 @@ __host__ __device__ inline bool geometry_of(int type, Geometry* g) {
             qk = i4g_gs(type);
             bb = 8 + qk / 2;
             break;
+        case T_NXF_I8: qk = 32; bb = 32; break;
+        case T_NXF_F16: qk = 32; bb = 64; break;
+        case T_NXF_F32: qk = 32; bb = 128; break;
         default: return false;
     }
     g->qk = qk;
     g->bb = bb;
-    g->crb = is_i4g(type) ? i4g_hdr(type) + CHUNK_K / 2 : (CHUNK_K / qk) * bb;
+    // T_NXF_I8 rows are tiled as Q8_0 records (a constant f16 scale per block).
+    g->crb = is_i4g(type) ? i4g_hdr(type) + CHUNK_K / 2 : type == T_NXF_I8 ? 272 : (CHUNK_K / qk) * bb;
     return true;
 }
 
@@ -127,6 +145,9 @@ inline bool make_tiled_shape(int type, int64_t N, int64_t K, TiledShape* s) {
 //         q6_lo_bit); plane B 128 x 16 B (scales); plane C 128 x 2 B (d)
 //   I4G   record H + 128 B: [(scale, zero) x 256/gs, padded to H = 16..64 B]
 //         [codes: 8 groups of 32 elements x 16 B, tiled code order]
+//   NXF_I8  record 272 B as Q8_0: [fl16(1/127) x8][codes x8 of 32 B]
+//   NXF_F16 record 512 B: the halves in order (subnormals written as zero)
+//   NXF_F32 record 1024 B: the floats in order
 // ---------------------------------------------------------------------------
 struct Segment {
     int src, len;
@@ -173,6 +194,15 @@ __host__ __device__ inline int block_segments(int type, int r, int j, Segment* s
             s[1] = {8, gs / 2, (int64_t)r * crb + i4g_hdr(type) + (gs / 2) * j};
             return 2;
         }
+        case T_NXF_I8:  // the scale field is not in the source (repack_kernel writes it)
+            s[0] = {0, 32, (int64_t)r * 272 + 16 + 32 * j};
+            return 1;
+        case T_NXF_F16:
+            s[0] = {0, 64, (int64_t)r * 512 + 64 * j};
+            return 1;
+        case T_NXF_F32:
+            s[0] = {0, 128, (int64_t)r * 1024 + 128 * j};
+            return 1;
         default:
             return 0;
     }
@@ -514,6 +544,25 @@ __device__ inline void decode8(int type, const uint8_t* chunk, int r, int e0, fl
             const uint8_t* q = rec + i4g_hdr(type) + 16 * (e0 >> 5);
             for (int i = 0; i < 8; ++i)
                 out[i] = __fmul_rn(__fsub_rn((float)q4_tiled_code(q, (e0 & 31) + i), zero), scale);
+            break;
+        }
+        case T_NXF_I8: {  // hybrid_model.cpp:248-255: (float)i8 / 127.0f
+            const int8_t* q = (const int8_t*)(chunk + (int64_t)r * 272 + 16 + 32 * (e0 >> 5) + (e0 & 31));
+            for (int i = 0; i < 8; ++i) out[i] = __fdiv_rn((float)q[i], 127.0f);
+            break;
+        }
+        case T_NXF_F16: {  // hybrid_model.cpp:192-210: subnormals to zero, Inf/NaN keep the mantissa
+            const uint8_t* h = chunk + (int64_t)r * 512 + 2 * e0;
+            for (int i = 0; i < 8; ++i) {
+                const uint32_t b = rd16(h + 2 * i), sign = (b & 0x8000u) << 16, e = (b >> 10) & 31u, m = b & 1023u;
+                out[i] = __uint_as_float(e == 0 ? sign : e == 31 ? (sign | 0x7F800000u | (m << 13))
+                                                                 : (sign | ((e + 112u) << 23) | (m << 13)));
+            }
+            break;
+        }
+        case T_NXF_F32: {  // hybrid_model.cpp:165-176: the chunk's floats as they are
+            const float* f = reinterpret_cast<const float*>(chunk + (int64_t)r * 1024) + e0;
+            for (int i = 0; i < 8; ++i) out[i] = f[i];
             break;
         }
         case T_Q6_K: {  // :924-954

@@ -28,6 +28,21 @@ __global__ void repack_kernel(const uint8_t* __restrict__ src, uint8_t* __restri
         uint8_t* base = dst + s.chunk_offset(tile, chunk);
         Segment seg[3];
         const int ns = block_segments(s.type, (int)r, (int)j, seg);
+        if (s.type == T_NXF_I8) {
+            // The Q8_0 record's scale field: fl16(1/127) for every block.
+            if (lane == 0) {
+                base[r * 272 + 2 * j] = (uint8_t)(kNxfI8ScaleHalf & 0xFF);
+                base[r * 272 + 2 * j + 1] = (uint8_t)(kNxfI8ScaleHalf >> 8);
+            }
+        } else if (s.type == T_NXF_F16) {
+            // One half per lane; subnormals become (signed) zero, as the
+            // reference's FP16 decode reads them.
+            uint32_t h = (uint32_t)blk[2 * lane] | ((uint32_t)blk[2 * lane + 1] << 8);
+            if ((h & 0x7C00u) == 0) h &= 0x8000u;
+            base[seg[0].dst + 2 * lane] = (uint8_t)(h & 0xFF);
+            base[seg[0].dst + 2 * lane + 1] = (uint8_t)(h >> 8);
+            continue;
+        }
         // Bytes [c0, c1) of the block are 4-bit codes stored in the tiled order;
         // Q3_K's first 96 bytes (hmask, qs), Q6_K's first 192 (ql, qh), Q5_K's
         // last 160 (qh, qs) and Q2_K's qs are regrouped (q3/q6/q5/q2_tiled_byte).

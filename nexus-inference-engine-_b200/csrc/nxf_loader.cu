@@ -21,7 +21,13 @@
 // a violation is NXQ_ERR_FORMAT.  Codecs registered (Codec, core/config.h:
 // 21-36): INT4 - a chunk of [4-bit codes in quant/gptq.cpp's flat order][fp32
 // scales][fp32 zeros], as GGUFImporter writes it (gguf_importer.cpp:1144-1170)
-// - and the native passthroughs Q3K / Q4K / Q2K (GGUF blocks).
+// -, the native passthroughs Q3K / Q4K / Q2K (GGUF blocks), and the flat
+// arrays the engine decodes at load time (hybrid_model.cpp:165-255): INT8
+// (w = q / 127), FP16 (subnormals read as zero) and FP32 (also any chunk of
+// 4 bytes per element, the writer's passthrough), as NXQ_TYPE_NXF_I8 / F16 /
+// F32.  Other codecs (BF16, GPTQ, AWQ, QuIP#, AQLM, TurboQuant) and
+// entropy-coded chunks are refused with NXQ_ERR_CODEC; the reference's engine
+// zero-fills the ones it does not know (hybrid_model.cpp:256-262).
 #include <fcntl.h>
 #include <sys/mman.h>
 #include <sys/stat.h>
@@ -47,8 +53,9 @@ constexpr int kMaxDims = 4;
 constexpr size_t kHeaderBytes = 64;
 constexpr size_t kChunkDescBytes = 24;
 
-// Codec ids of the chunk descriptors.
-constexpr int kCodecInt4 = 4, kCodecQ3K = 11, kCodecQ4K = 12, kCodecQ2K = 13;
+// Codec ids of the chunk descriptors (Codec, core/config.h:21-36).
+constexpr int kCodecFp32 = 0, kCodecFp16 = 1, kCodecInt8 = 3, kCodecInt4 = 4, kCodecQ3K = 11, kCodecQ4K = 12,
+              kCodecQ2K = 13;
 
 struct Chunk {
     uint64_t offset;
@@ -284,6 +291,34 @@ int register_tensor(const NxfFile& f, int64_t i, int64_t slice, bool sharded, in
         return fail(NXQ_ERR_ARG, "nxf: slice %lld of '%s' (%lld slices)", (long long)slice, t.name.c_str(), (long long)E);
     if (K <= 0 || N <= 0) return fail(NXQ_ERR_SHAPE, "nxf: tensor '%s' is empty", t.name.c_str());
     const int64_t elems = E * N * K, slice_elems = N * K;
+    uint64_t stored_total = 0;
+    for (const Chunk& k : t.chunks) stored_total += k.stored;
+    // Flat element arrays, decoded by the reference's engine at load time
+    // (HybridModel::Impl::load_tensor, hybrid_model.cpp:165-255): FP32, and
+    // any chunk that holds 4 bytes per element whatever its codec (the
+    // writer's passthrough of small tensors, :170-176); FP16; INT8.
+    if (codec == kCodecFp32 || codec == kCodecFp16 || codec == kCodecInt8 || stored_total == (uint64_t)elems * 4) {
+        const bool f32 = codec == kCodecFp32 || stored_total == (uint64_t)elems * 4;
+        const int type = f32 ? NXQ_TYPE_NXF_F32 : codec == kCodecFp16 ? NXQ_TYPE_NXF_F16 : NXQ_TYPE_NXF_I8;
+        const int64_t bpe = f32 ? 4 : codec == kCodecFp16 ? 2 : 1;
+        if (stored_total != (uint64_t)(elems * bpe))
+            return fail(NXQ_ERR_SHAPE, "nxf: '%s' holds %llu bytes, its shape needs %lld", t.name.c_str(),
+                        (unsigned long long)stored_total, (long long)(elems * bpe));
+        if (K % 32)
+            return fail(NXQ_ERR_SHAPE, "nxf: '%s': K=%lld is not a multiple of 32 (the block of the flat codecs)",
+                        t.name.c_str(), (long long)K);
+        std::vector<uint8_t> joined;
+        const uint8_t* base = f.bytes() + t.chunks[0].offset;
+        if (t.chunks.size() > 1) {
+            joined.reserve(stored_total);
+            for (const Chunk& k : t.chunks) joined.insert(joined.end(), f.bytes() + k.offset, f.bytes() + k.offset + k.stored);
+            base = joined.data();
+        }
+        const size_t sb = (size_t)(slice_elems * bpe);
+        const uint8_t* src = base + (size_t)slice * sb;
+        return sharded ? nxq_weight_register_shard(src, sb, type, N, K, split, rank, world, out)
+                       : nxq_weight_register(src, sb, type, N, K, out);
+    }
     if (codec == kCodecQ3K || codec == kCodecQ4K || codec == kCodecQ2K) {
         const int type = codec == kCodecQ3K ? NXQ_TYPE_Q3_K : codec == kCodecQ4K ? NXQ_TYPE_Q4_K : NXQ_TYPE_Q2_K;
         const int64_t bb = codec == kCodecQ3K ? 110 : codec == kCodecQ4K ? 144 : 84;

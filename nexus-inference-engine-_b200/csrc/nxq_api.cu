@@ -211,6 +211,9 @@ const char* type_name(int type) {
         case T_I4G64: return "I4G64";
         case T_I4G128: return "I4G128";
         case T_I4G256: return "I4G256";
+        case T_NXF_I8: return "NXF_I8";
+        case T_NXF_F16: return "NXF_F16";
+        case T_NXF_F32: return "NXF_F32";
         default: return "?";
     }
 }

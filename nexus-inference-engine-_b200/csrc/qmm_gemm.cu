@@ -370,9 +370,10 @@ int launch(const Weight* w, const CUtensorMap& tmap, void* y, int y_dtype, int64
     return NXQ_OK;
 }
 
+// NXF INT8 weights are tiled as Q8_0 records and run on its kernel.
 bool type_ok(int type) {
     return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || type == T_Q3_K || type == T_Q6_K ||
-           type == T_Q5_K || type == T_Q4_1 || type == T_Q2_K || is_i4g(type);
+           type == T_Q5_K || type == T_Q4_1 || type == T_Q2_K || is_i4g(type) || type == T_NXF_I8;
 }
 
 }  // namespace
@@ -437,7 +438,8 @@ int gemm_qmatmul(const Weight* w, const void* x, int x_dtype, void* y, int y_dty
     switch (s.type) {
         case T_Q4_K: return launch<T_Q4_K>(w, tmap, y, y_dtype, M, st);
         case T_Q4_0: return launch<T_Q4_0>(w, tmap, y, y_dtype, M, st);
-        case T_Q8_0: return launch<T_Q8_0>(w, tmap, y, y_dtype, M, st);
+        case T_Q8_0:
+        case T_NXF_I8: return launch<T_Q8_0>(w, tmap, y, y_dtype, M, st);
         case T_Q3_K: return launch<T_Q3_K>(w, tmap, y, y_dtype, M, st);
         case T_I4G128: return launch<T_I4G128>(w, tmap, y, y_dtype, M, st);
         case T_Q6_K: return launch<T_Q6_K>(w, tmap, y, y_dtype, M, st);

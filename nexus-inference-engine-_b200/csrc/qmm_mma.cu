@@ -1186,9 +1186,10 @@ int launch(const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st)
     return NXQ_OK;
 }
 
+// NXF INT8 weights are tiled as Q8_0 records and run on its kernels.
 bool type_ok(int type) {
     return type == T_Q4_K || type == T_Q4_0 || type == T_Q8_0 || type == T_Q3_K || type == T_Q6_K ||
-           type == T_Q5_K || type == T_Q4_1 || type == T_Q2_K || is_i4g(type);
+           type == T_Q5_K || type == T_Q4_1 || type == T_Q2_K || is_i4g(type) || type == T_NXF_I8;
 }
 
 int launch_items(int type, int mt, const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st) {
@@ -1205,6 +1206,7 @@ int launch_items(int type, int mt, const HostItem* it, int n, int x_dtype, int y
     switch (type) {
         NXQ_CASE(T_Q4_K)
         NXQ_CASE(T_Q4_0)
+        case T_NXF_I8:
         NXQ_CASE(T_Q8_0)
         NXQ_CASE(T_Q3_K)
         NXQ_CASE(T_I4G128)

@@ -30,9 +30,11 @@ HEADER = Path(__file__).resolve().parents[2] / "include" / "nxq.h"
 # GGUF type ids (nexus/src/import/gguf_importer.h:28-57) and block geometry
 # (elements per block, bytes per block; gguf_importer.cpp:679-954).
 TYPES = {"Q4_0": 2, "Q4_1": 3, "Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14,
-         "I4G32": 101, "I4G64": 102, "I4G128": 104, "I4G256": 108}
+         "I4G32": 101, "I4G64": 102, "I4G128": 104, "I4G256": 108,
+         "NXF_I8": 120, "NXF_F16": 121, "NXF_F32": 122}
 GEOMETRY = {2: (32, 18), 3: (32, 20), 8: (32, 34), 10: (256, 84), 11: (256, 110), 12: (256, 144),
-            13: (256, 176), 14: (256, 210), 101: (32, 24), 102: (64, 40), 104: (128, 72), 108: (256, 136)}
+            13: (256, 176), 14: (256, 210), 101: (32, 24), 102: (64, 40), 104: (128, 72), 108: (256, 136),
+            120: (32, 32), 121: (32, 64), 122: (32, 128)}
 # NXF INT4 group weights: array orders accepted by register_int4 / int4_pack.
 INT4_ROWS, INT4_KMAJOR = 0, 1
 F32, F16, BF16 = 0, 1, 2

@@ -12,12 +12,14 @@ from __future__ import annotations
 import numpy as np
 
 GEOMETRY = {2: (32, 18), 3: (32, 20), 8: (32, 34), 10: (256, 84), 11: (256, 110),
-            12: (256, 144), 13: (256, 176), 14: (256, 210), 101: (32, 24), 102: (64, 40), 104: (128, 72), 108: (256, 136)}
+            12: (256, 144), 13: (256, 176), 14: (256, 210), 101: (32, 24), 102: (64, 40), 104: (128, 72), 108: (256, 136),
+            120: (32, 32), 121: (32, 64), 122: (32, 128)}
 # Byte offsets of the fp16 fields in each block.
 HALF_FIELDS = {2: [0], 3: [0, 2], 8: [0], 10: [80, 82], 11: [108], 12: [0, 2], 13: [0, 2],
                14: [208]}
 Q4_0, Q4_1, Q8_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K = 2, 3, 8, 10, 11, 12, 13, 14
 I4G = (101, 102, 104, 108)  # NXF INT4, groups of 32 / 64 / 128 / 256
+NXF_I8, NXF_F16, NXF_F32 = 120, 121, 122  # NXF INT8 / FP16 / FP32 chunks as blocks of 32
 
 
 def rng(seed: int) -> np.random.Generator:
@@ -44,6 +46,8 @@ def make_blocks(type_id: int, N: int, K: int, seed: int, dist: str = "config") -
       scale codes uniform
       I4G (NXF INT4 groups): scale fp32 U(1e-3, 5e-3), zero fp32 U(0, 15),
       codes uniform
+      NXF_I8: int8 codes uniform -127..127 (w = q / 127)
+      NXF_F16 / NXF_F32: w ~ N(0, 0.02)
     dist="raw": every byte uniform (fp16 fields may be subnormal, Inf or NaN).
     """
     qk, bb = GEOMETRY[type_id]
@@ -68,6 +72,11 @@ def make_blocks(type_id: int, N: int, K: int, seed: int, dist: str = "config") -
         if type_id == Q8_0:
             codes = g.integers(-127, 128, size=(nb, 32), dtype=np.int16).astype(np.int8)
             b2[:, 2:34] = codes.view(np.uint8)
+    elif type_id == NXF_I8:
+        buf[:] = g.integers(-127, 128, size=nb * bb, dtype=np.int16).astype(np.int8).view(np.uint8)
+    elif type_id in (NXF_F16, NXF_F32):
+        w = (g.standard_normal(nb * 32, dtype=np.float32) * 0.02).astype(np.float16 if type_id == NXF_F16 else np.float32)
+        buf[:] = w.view(np.uint8)
     elif type_id in I4G:
         b2[:, 0:4] = g.uniform(1e-3, 5e-3, size=nb).astype(np.float32).view(np.uint8).reshape(nb, 4)
         b2[:, 4:8] = g.uniform(0.0, 15.0, size=nb).astype(np.float32).view(np.uint8).reshape(nb, 4)

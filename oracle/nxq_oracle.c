@@ -53,6 +53,9 @@ int nxqo_block_shape(int type, int* elems, int* bytes) {
             break;
         case NXQO_Q5_K: e = 256; b = 176; break;
         case NXQO_Q6_K: e = 256; b = 210; break;
+        case NXQO_NXF_I8: e = 32; b = 32; break;
+        case NXQO_NXF_F16: e = 32; b = 64; break;
+        case NXQO_NXF_F32: e = 32; b = 128; break;
         default: return 0;
     }
     if (elems) *elems = e;
@@ -215,6 +218,25 @@ static void blk_i4g64(const uint8_t* b, float* y) { blk_i4g(b, y, 64); }
 static void blk_i4g128(const uint8_t* b, float* y) { blk_i4g(b, y, 128); }
 static void blk_i4g256(const uint8_t* b, float* y) { blk_i4g(b, y, 256); }
 
+/* NXF INT8 chunk (hybrid_model.cpp:248-255): out = (float)(int8)q / 127.0f. */
+static void blk_nxf_i8(const uint8_t* b, float* y) {
+    for (int j = 0; j < 32; ++j) y[j] = (float)(int8_t)b[j] / 127.0f;
+}
+
+/* NXF FP16 chunk (hybrid_model.cpp:192-210): exponent 0 (zero or subnormal)
+ * gives a signed zero; exponent 31 keeps the mantissa (Inf, NaN); otherwise
+ * the exponent is rebiased by 112 and the mantissa shifted by 13. */
+static void blk_nxf_f16(const uint8_t* b, float* y) {
+    for (int j = 0; j < 32; ++j) {
+        const uint32_t h = rd16(b + 2 * j), sign = (h & 0x8000u) << 16, e = (h >> 10) & 31u, m = h & 1023u;
+        const uint32_t f = e == 0 ? sign : e == 31 ? (sign | 0x7F800000u | (m << 13)) : (sign | ((e + 112u) << 23) | (m << 13));
+        y[j] = bits_to_float(f);
+    }
+}
+
+/* NXF FP32 chunk (hybrid_model.cpp:165-176): the floats as stored. */
+static void blk_nxf_f32(const uint8_t* b, float* y) { memcpy(y, b, 128); }
+
 typedef void (*blk_fn)(const uint8_t*, float*);
 
 static blk_fn block_decoder(int type) {
@@ -231,6 +253,9 @@ static blk_fn block_decoder(int type) {
         case NXQO_I4G64: return blk_i4g64;
         case NXQO_I4G128: return blk_i4g128;
         case NXQO_I4G256: return blk_i4g256;
+        case NXQO_NXF_I8: return blk_nxf_i8;
+        case NXQO_NXF_F16: return blk_nxf_f16;
+        case NXQO_NXF_F32: return blk_nxf_f32;
         default: return NULL;
     }
 }

@@ -33,7 +33,12 @@ enum {
     NXQO_Q6_K = 14, NXQO_BF16 = 30,
     /* NXF INT4 groups of 32/64/128/256 as blocks [scale f32][zero f32][codes]
      * (the library's NXQ_TYPE_I4G*; quant/gptq.cpp:9-27 per group) */
-    NXQO_I4G32 = 101, NXQO_I4G64 = 102, NXQO_I4G128 = 104, NXQO_I4G256 = 108
+    NXQO_I4G32 = 101, NXQO_I4G64 = 102, NXQO_I4G128 = 104, NXQO_I4G256 = 108,
+    /* NXF chunks decoded at load time by HybridModel::Impl::load_tensor
+     * (hybrid_model.cpp:145-265), as blocks of 32 elements (the library's
+     * NXQ_TYPE_NXF_*): INT8 (float)q / 127.0f; FP16 with subnormals read as
+     * zero; FP32 as stored */
+    NXQO_NXF_I8 = 120, NXQO_NXF_F16 = 121, NXQO_NXF_F32 = 122
 };
 
 /* quant/gptq.cpp:9-27, dequant_int4, over flat arrays: element i is nibble i of

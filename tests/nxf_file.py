@@ -17,8 +17,9 @@ import nxq
 ALIGN = 16 * 1024
 MAGIC = 0x3146584E
 # Codec (core/config.h:21-36) and DType (core/config.h:39-46) ids.
-CODEC_FP32, CODEC_INT4, CODEC_Q3K, CODEC_Q4K, CODEC_Q2K = 0, 4, 11, 12, 13
-DTYPE_F32, DTYPE_I8, DTYPE_I4 = 0, 3, 4
+CODEC_FP32, CODEC_FP16, CODEC_BF16, CODEC_INT8, CODEC_INT4 = 0, 1, 2, 3, 4
+CODEC_Q3K, CODEC_Q4K, CODEC_Q2K = 11, 12, 13
+DTYPE_F32, DTYPE_F16, DTYPE_BF16, DTYPE_I8, DTYPE_I4 = 0, 1, 2, 3, 4
 
 
 def _escape(s: str) -> str:

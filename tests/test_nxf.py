@@ -7,10 +7,12 @@ layout and the xxHash32 chunk checksums; the loader reads such a file (tensor
 index, chunk descriptors, manifest values) and refuses corrupt, truncated and
 inconsistent ones; a codec that is no matmul weight is NXQ_ERR_CODEC.
 GPU: INT4 (groups of 32 in two chunks, 64 and 128, one slice of a 3-D
-tensor) and Q4K / Q3K
-passthrough tensors (one of them in two chunks) register bit-exactly (device
-decode against the oracle) and multiply within the parity bar; column and row
-shards decode to their slices of the whole tensor."""
+tensor), Q4K / Q3K passthrough tensors (one of them in two chunks) and the
+flat codecs the engine decodes at load time - INT8 (two chunks), FP16 (with
+subnormal halves, read as zero) and an fp32 passthrough stored under another
+codec - register bit-exactly (device decode against the oracle) and multiply
+within the parity bar; column and row shards decode to their slices of the
+whole tensor."""
 from __future__ import annotations
 
 import ctypes
@@ -45,6 +47,12 @@ def _content():
     q3k = synth.make_blocks(11, 256, 512, seed=5).tobytes()
     rng = np.random.default_rng(6)
     raw = [rng.integers(0, 256, n, dtype=np.uint8).tobytes() for n in (1, 13, 37, 100)]
+    i8 = rng.integers(-128, 128, 64 * 512, dtype=np.int16).astype(np.int8).tobytes()
+    f16 = (rng.standard_normal(32 * 256) * 0.02).astype(np.float16)
+    f16[::97] = np.float16(3e-6)  # subnormal halves: the engine reads them as zero
+    f16[5] = -np.float16(1e-7)
+    f32 = (rng.standard_normal(16 * 128) * 0.02).astype(np.float32).tobytes()
+    bf16 = rng.integers(0, 1 << 16, 64 * 4, dtype=np.uint16).tobytes()
     return [
         ("blk.0.ffn_gate.weight", [1024, 256], nxf_file.DTYPE_I4,
          [(nxf_file.int4_chunk(*c128), nxf_file.CODEC_INT4, 128)]),
@@ -58,7 +66,14 @@ def _content():
         ("blk.0.ffn_down.weight", [512, 256], nxf_file.DTYPE_I4,
          [(q3k[: 128 * 2 * 110], nxf_file.CODEC_Q3K, 0), (q3k[128 * 2 * 110:], nxf_file.CODEC_Q3K, 0)]),
         ("raw.odd_sizes", [151], nxf_file.DTYPE_F32, [(r, nxf_file.CODEC_FP32, 0) for r in raw]),
-    ], {"c128": c128, "c64": c64, "e3": e3, "m2": m2, "q4k": q4k, "q3k": q3k}
+        ("blk.0.attn_o.weight", [512, 64], nxf_file.DTYPE_I8,
+         [(i8[:32 * 512], nxf_file.CODEC_INT8, 0), (i8[32 * 512:], nxf_file.CODEC_INT8, 0)]),
+        ("blk.0.ffn_up.weight", [256, 32], nxf_file.DTYPE_F16, [(f16.tobytes(), nxf_file.CODEC_FP16, 0)]),
+        # 4 bytes per element under another codec: the writer's fp32 passthrough
+        ("blk.0.small.weight", [128, 16], nxf_file.DTYPE_F32, [(f32, nxf_file.CODEC_INT8, 0)]),
+        ("raw.bf16", [64, 4], nxf_file.DTYPE_BF16, [(bf16, nxf_file.CODEC_BF16, 0)]),
+    ], {"c128": c128, "c64": c64, "e3": e3, "m2": m2, "q4k": q4k, "q3k": q3k, "i8": i8, "f16": f16.tobytes(),
+        "f32": f32}
 
 
 MANIFEST = dict(architecture="llama", name='tiny "test"\tmodel', num_layers=2, hidden_dim=4096,
@@ -144,7 +159,10 @@ def test_reads_reference_file(tmp_path):
             f.find("no.such.tensor")
         assert e.value.code == -1
         with pytest.raises(nxq.NxqError) as e:
-            f.register("raw.odd_sizes")  # FP32 bytes: not a matmul weight codec
+            f.register("raw.odd_sizes")  # FP32 codec, 151 bytes for 151 elements
+        assert e.value.code == -3
+        with pytest.raises(nxq.NxqError) as e:
+            f.register("raw.bf16")  # BF16: a codec the reference's engine does not decode
         assert e.value.code == -2
 
 
@@ -244,6 +262,9 @@ def test_register_and_matmul(gpu, tmp_path):
         ("blk.0.attn_q.weight", 0, 12, 128, 512, np.frombuffer(d["q4k"], np.uint8)),
         ("blk.0.attn_v.weight", 0, 101, 192, 256, gpu.int4_pack(*d["m2"], 192, 256, 32)),
         ("blk.0.ffn_down.weight", 0, 11, 256, 512, np.frombuffer(d["q3k"], np.uint8)),
+        ("blk.0.attn_o.weight", 0, 120, 64, 512, np.frombuffer(d["i8"], np.uint8)),
+        ("blk.0.ffn_up.weight", 0, 121, 32, 256, np.frombuffer(d["f16"], np.uint8)),
+        ("blk.0.small.weight", 0, 122, 16, 128, np.frombuffer(d["f32"], np.uint8)),
     ]
     with gpu.NXF(path) as f:
         for name, sl, t, N, K, blocks in cases:
@@ -258,3 +279,34 @@ def test_register_and_matmul(gpu, tmp_path):
                 assert synth.rel_l2(y.cpu().numpy(), want) < TOL, name
             finally:
                 w.release()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("t", [120, 121, 122], ids=["NXF_I8", "NXF_F16", "NXF_F32"])
+def test_flat_codecs_on_the_kernels(gpu, t):
+    """The flat NXF codecs registered from host arrays: device decode
+    bit-exact against the oracle's restatement of the engine's decode, and the
+    matmul within the parity bar at decode and prefill batch sizes (INT8 runs
+    on the Q8_0 tensor-core kernels, FP16 / FP32 on the CUDA-core kernel)."""
+    import torch
+
+    N, K = 640, 1536
+    blocks = synth.make_blocks(t, N, K, seed=t)
+    if t == 121:  # a few subnormal halves, which the engine reads as zero
+        h = blocks.view(np.uint16).copy()
+        h[::301] = 0x0003
+        blocks = h.view(np.uint8)
+    w = gpu.Weight.register(blocks, t, N, K)
+    try:
+        assert loader.same_bits(w.dequant().cpu().numpy().reshape(-1), loader.dequant(t, blocks, N * K))
+        name = gpu.kernel_name(w, 1)
+        assert name.startswith("mma_gemv<NXF_I8" if t == 120 else "simt<"), name
+        for M in (1, 8, 40):
+            x = torch.from_numpy(synth.make_activations(M, K, seed=M)).cuda()
+            y = gpu.qmatmul(w, x)
+            torch.cuda.synchronize()
+            gpu.stream_sync()
+            want = loader.qmatmul(t, blocks, N, K, x.float().cpu().numpy())
+            assert synth.rel_l2(y.cpu().numpy(), want) < TOL, M
+    finally:
+        w.release()

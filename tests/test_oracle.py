@@ -109,3 +109,22 @@ def test_synthetic_distributions():
 def test_oracle_rejects_bad_shape():
     with pytest.raises(ValueError):
         loader.qmatmul(12, np.zeros(144, np.uint8), 1, 100, np.zeros((1, 100), np.float32))
+
+
+def test_nxf_flat_codecs_known_answers():
+    """The oracle's NXF INT8 / FP16 / FP32 decoders (hybrid_model.cpp:165-255)
+    on every code: INT8 q / 127 in fp32 (numpy's correctly rounded float32
+    division); FP16 all 65,536 halves, with zero/subnormal exponents read as a
+    signed zero and the rest exact; FP32 unchanged."""
+    q = np.arange(-128, 128, dtype=np.int16).astype(np.int8)
+    got = loader.dequant(120, q.view(np.uint8), 256)
+    assert np.array_equal(got.view(np.uint32), (q.astype(np.float32) / np.float32(127.0)).view(np.uint32))
+    h = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    got = loader.dequant(121, h.view(np.uint8), 65536)
+    want = h.view(np.float16).astype(np.float32)
+    flush = (h & 0x7C00) == 0
+    want[flush] = np.where(h[flush] & 0x8000, np.float32(-0.0), np.float32(0.0))
+    assert loader.same_bits(got, want)
+    assert np.array_equal(np.signbit(got[flush]), (h[flush] & 0x8000) != 0)
+    f = np.random.default_rng(1).standard_normal(96).astype(np.float32)
+    assert np.array_equal(loader.dequant(122, f.view(np.uint8), 96), f)
