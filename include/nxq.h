@@ -302,7 +302,7 @@ typedef enum { NXQ_HOOK_STREAMK_SKIP_COUNT = 1, NXQ_HOOK_TP_STREAM_PENDING = 2 }
 NXQ_API int nxq_test_hook(int hook, int on);
 
 /* Name of the kernel nxq_qmatmul would launch for (w, M, dtypes), e.g.
- * "tc_gemv<Q4_K,n32>" or "simt<Q3_K,mb8>".  Profiling aid; the reference's
+ * "mma_gemv<Q4_K,m8>", "tc_gemm<Q4_K,n256>" or "simt<Q3_K,mb8>".  Profiling aid; the reference's
  * counterpart is the pipeline-name log of metal_context_impl.h:77-78. */
 NXQ_API int nxq_qmatmul_kernel_name(nxq_weight_t w, int64_t M, int x_dtype, int y_dtype,
                                     char* buf, size_t n);

@@ -20,7 +20,6 @@
 #include "qmm_gemm.h"
 #include "qmm_mma.h"
 #include "stream_scratch.h"
-#include "qmm_tc.h"
 
 namespace nxq {
 
@@ -34,20 +33,51 @@ struct Context {
     int sm_count = 0;
     int cc_major = 0, cc_minor = 0;
     size_t smem_optin = 0;
-    cudaStream_t host_stream = nullptr;  // nxq_qmatmul_host and registration
-    // Device buffers of the host-buffer entry point (grown on demand).
-    void* hx = nullptr;
-    size_t hx_bytes = 0;
-    void* hy = nullptr;
-    size_t hy_bytes = 0;
-    DeviceStatus* status = nullptr;  // bounded-wait error word (device memory)
-    DeviceStatus* status_host = nullptr;  // pinned copy read by the host entry point
-    std::mutex mu;                   // registration, host entry point, teardown
+    cudaStream_t host_stream = nullptr;  // registration
+    DeviceStatus* status = nullptr;  // error word and wait settings (device memory)
+    unsigned int* flag_host = nullptr;  // mapped pinned word kernels set on an error
+    std::mutex mu;                   // registration, teardown
     std::unordered_set<Weight*> live;
+    unsigned generation = 0;         // bumped by every nxq_init: host-call contexts of an old one are stale
 };
 
 Context g_ctx;
 std::mutex g_init_mu;
+
+// One per calling thread for nxq_qmatmul_host: its own stream and device
+// buffers, so concurrent host calls neither share buffers nor take a global
+// lock; the buffers grow on the thread's first calls and stay.  All of them
+// are freed by nxq_shutdown.
+struct HostCall {
+    unsigned generation = 0;
+    cudaStream_t st = nullptr;
+    void* dx = nullptr;
+    size_t dx_bytes = 0;
+    void* dy = nullptr;
+    size_t dy_bytes = 0;
+};
+std::mutex g_hostcall_mu;
+std::vector<HostCall*> g_hostcalls;
+thread_local HostCall* t_hostcall = nullptr;
+
+int host_call_context(HostCall** out) {
+    HostCall* hc = t_hostcall;
+    if (!hc || hc->generation != g_ctx.generation) {
+        hc = new (std::nothrow) HostCall();
+        if (!hc) return fail(NXQ_ERR_NOMEM, "host allocation failed");
+        hc->generation = g_ctx.generation;
+        cudaError_t e = cudaStreamCreateWithFlags(&hc->st, cudaStreamNonBlocking);
+        if (e != cudaSuccess) {
+            delete hc;
+            return cuda_fail(e, "cudaStreamCreate (host-call stream)");
+        }
+        std::lock_guard<std::mutex> lk(g_hostcall_mu);
+        g_hostcalls.push_back(hc);
+        t_hostcall = hc;
+    }
+    *out = hc;
+    return NXQ_OK;
+}
 
 int check_ready() {
     if (!g_ctx.ready) return fail(NXQ_ERR_STATE, "nxq_init has not been called");
@@ -106,7 +136,14 @@ int check_device_status() {
     DeviceStatus st{};
     cudaError_t e = cudaMemcpy(&st, g_ctx.status, sizeof st, cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return cuda_fail(e, "read device status");
+    if (st.code) *reinterpret_cast<volatile unsigned int*>(g_ctx.flag_host) = 0u;
     return report_status(st);
+}
+
+// After a synchronize: the device status only when a kernel flagged an error.
+int check_host_flag() {
+    if (!*reinterpret_cast<volatile unsigned int*>(g_ctx.flag_host)) return NXQ_OK;
+    return check_device_status();
 }
 
 // Registers N rows of K from GGUF blocks.  `src` is host (is_host) or device
@@ -234,10 +271,6 @@ int qmatmul_dispatch(const Weight* w, const void* x, int x_dtype, void* y, int y
         int rc = gemm_qmatmul(w, x, x_dtype, y, y_dtype, M, st);
         if (rc != NXQ_ERR_UNSUPPORTED) return rc;
     }
-    if (tc_supported(s, M, x_dtype, y_dtype)) {
-        int rc = tc_qmatmul(w, x, x_dtype, y, y_dtype, M, st);
-        if (rc != NXQ_ERR_UNSUPPORTED) return rc;
-    }
     int splits = simt_pick_splits(s, M, g_ctx.sm_count);
     float* partials = nullptr;
     cudaError_t e;
@@ -298,12 +331,15 @@ NXQ_API int nxq_init(int device) {
     g_ctx.smem_optin = p.sharedMemPerBlockOptin;
     NXQ_CUDA(cudaStreamCreateWithFlags(&g_ctx.host_stream, cudaStreamNonBlocking));
     NXQ_CUDA(cudaMalloc(&g_ctx.status, sizeof(DeviceStatus)));
+    NXQ_CUDA(cudaHostAlloc(&g_ctx.flag_host, sizeof(unsigned int), cudaHostAllocMapped));
+    *g_ctx.flag_host = 0u;
     {
         DeviceStatus init{};
         init.wait_cycles = kDefaultWaitCycles;
+        NXQ_CUDA(cudaHostGetDevicePointer((void**)&init.host_flag, g_ctx.flag_host, 0));
         NXQ_CUDA(cudaMemcpy(g_ctx.status, &init, sizeof init, cudaMemcpyHostToDevice));
     }
-    NXQ_CUDA(cudaMallocHost(&g_ctx.status_host, sizeof(DeviceStatus)));
+    ++g_ctx.generation;
     // Keep stream-ordered scratch in the pool between calls instead of
     // returning it to the driver after every synchronize.
     cudaMemPool_t pool;
@@ -311,9 +347,8 @@ NXQ_API int nxq_init(int device) {
         uint64_t keep = 1ull << 30;
         cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
     }
-    int rc = tc_init(device);
+    int rc = mma_init(device);
     if (rc != NXQ_OK) return rc;
-    if ((rc = mma_init(device)) != NXQ_OK) return rc;
     if ((rc = gemm_init(device)) != NXQ_OK) return rc;
     g_ctx.ready = true;
     return NXQ_OK;
@@ -333,14 +368,22 @@ NXQ_API int nxq_shutdown(void) {
         }
         g_ctx.live.clear();
     }
-    if (g_ctx.hx) cudaFree(g_ctx.hx);
-    if (g_ctx.hy) cudaFree(g_ctx.hy);
-    g_ctx.hx = g_ctx.hy = nullptr;
-    g_ctx.hx_bytes = g_ctx.hy_bytes = 0;
+    {
+        std::lock_guard<std::mutex> lk2(g_hostcall_mu);
+        for (HostCall* hc : g_hostcalls) {
+            if (hc->dx) cudaFree(hc->dx);
+            if (hc->dy) cudaFree(hc->dy);
+            if (hc->st) cudaStreamDestroy(hc->st);
+            hc->dx = hc->dy = nullptr;
+            hc->st = nullptr;
+            hc->generation = 0;  // the owning thread makes a new one on its next call
+        }
+        g_hostcalls.clear();  // the structs themselves stay with their threads' pointers
+    }
     if (g_ctx.status) cudaFree(g_ctx.status);
     g_ctx.status = nullptr;
-    if (g_ctx.status_host) cudaFreeHost(g_ctx.status_host);
-    g_ctx.status_host = nullptr;
+    if (g_ctx.flag_host) cudaFreeHost(g_ctx.flag_host);
+    g_ctx.flag_host = nullptr;
     if (g_ctx.host_stream) cudaStreamDestroy(g_ctx.host_stream);
     g_ctx.host_stream = nullptr;
     g_ctx.ready = false;
@@ -636,20 +679,21 @@ NXQ_API int nxq_qmatmul_host(nxq_weight_t h, const float* x_host, float* y_host,
     if (M == 0) return NXQ_OK;
     if (!x_host || !y_host) return fail(NXQ_ERR_ARG, "null activation or output");
     if ((rc = check_ready())) return rc;
-    std::lock_guard<std::mutex> lk(g_init_mu);
+    HostCall* hc = nullptr;
+    if ((rc = host_call_context(&hc))) return rc;
     const size_t xb = (size_t)M * w->shape.K * sizeof(float);
     const size_t yb = (size_t)M * w->shape.N * sizeof(float);
-    if ((rc = grow(&g_ctx.hx, &g_ctx.hx_bytes, xb))) return rc;
-    if ((rc = grow(&g_ctx.hy, &g_ctx.hy_bytes, yb))) return rc;
-    cudaStream_t st = g_ctx.host_stream;
-    NXQ_CUDA(cudaMemcpyAsync(g_ctx.hx, x_host, xb, cudaMemcpyHostToDevice, st));
-    rc = qmatmul_dispatch(w, g_ctx.hx, NXQ_F32, g_ctx.hy, NXQ_F32, M, st);
+    if ((rc = grow(&hc->dx, &hc->dx_bytes, xb))) return rc;
+    if ((rc = grow(&hc->dy, &hc->dy_bytes, yb))) return rc;
+    cudaStream_t st = hc->st;
+    NXQ_CUDA(cudaMemcpyAsync(hc->dx, x_host, xb, cudaMemcpyHostToDevice, st));
+    rc = qmatmul_dispatch(w, hc->dx, NXQ_F32, hc->dy, NXQ_F32, M, st);
     if (rc) return rc;
-    NXQ_CUDA(cudaMemcpyAsync(y_host, g_ctx.hy, yb, cudaMemcpyDeviceToHost, st));
-    // The status word travels with the result: one synchronize per call.
-    NXQ_CUDA(cudaMemcpyAsync(g_ctx.status_host, g_ctx.status, sizeof(DeviceStatus), cudaMemcpyDeviceToHost, st));
+    NXQ_CUDA(cudaMemcpyAsync(y_host, hc->dy, yb, cudaMemcpyDeviceToHost, st));
     NXQ_CUDA(cudaStreamSynchronize(st));
-    return report_status(*g_ctx.status_host);
+    // A kernel that raised an error also set the mapped host flag: no device
+    // read on the normal path.
+    return check_host_flag();
 }
 
 NXQ_API int nxq_qmatmul_kernel_name(nxq_weight_t h, int64_t M, int x_dtype, int y_dtype, char* buf,
@@ -665,10 +709,6 @@ NXQ_API int nxq_qmatmul_kernel_name(nxq_weight_t h, int64_t M, int x_dtype, int 
     }
     if (gemm_supported(w->shape, M)) {
         gemm_kernel_name(w->shape, M, buf, n);
-        return NXQ_OK;
-    }
-    if (tc_supported(w->shape, M, x_dtype, y_dtype)) {
-        tc_kernel_name(w->shape, M, buf, n);
         return NXQ_OK;
     }
     snprintf(buf, n, "simt<%s,mb%d>", type_name(w->shape.type), simt_rows_per_pass(M));
@@ -715,7 +755,7 @@ NXQ_API int nxq_stream_sync(void* stream) {
     int rc = check_ready();
     if (rc) return rc;
     NXQ_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
-    return check_device_status();
+    return check_host_flag();
 }
 
 }  // extern "C"

@@ -44,12 +44,15 @@ int cuda_fail(cudaError_t e, const char* what);
 // clock cycles; nxq_set_wait_limit) and test hooks (nxq_test_hook).  Drain
 // waits (letting a CTA's own copies land before it exits) always use the
 // fixed kDrainWaitCycles.
+// host_flag is a word of mapped pinned host memory that a kernel raising an
+// error also sets, so a host call learns of an error without a device read.
 struct DeviceStatus {
     unsigned int code;
     unsigned int where;
     long long wait_cycles;
     unsigned int hooks;  // kHook* bits
     unsigned int pad;
+    unsigned int* host_flag;
 };
 constexpr unsigned kStatusTimeout = 1u;
 constexpr unsigned kStatusRange = 2u;
@@ -67,9 +70,20 @@ __device__ __forceinline__ bool f16_overflows(float v) {
     const float a = fabsf(v);
     return a >= 65520.0f && a <= 3.402823466e38f;
 }
+// Sets the host-visible error flag (mapped pinned memory, written over the bus).
+__device__ __forceinline__ void raise_host_flag(DeviceStatus* st) {
+    unsigned int* f = st->host_flag;
+    if (f) {
+        *reinterpret_cast<volatile unsigned int*>(f) = 1u;
+        __threadfence_system();
+    }
+}
 // Records a range error (first error wins; `where` names the conversion).
 __device__ __forceinline__ void raise_range(DeviceStatus* st, unsigned where) {
-    if (st && atomicCAS(&st->code, 0u, kStatusRange) == 0u) st->where = where;
+    if (st && atomicCAS(&st->code, 0u, kStatusRange) == 0u) {
+        st->where = where;
+        raise_host_flag(st);
+    }
 }
 
 // The context's device status word and SM count (nxq_api.cu).

@@ -1227,7 +1227,7 @@ int launch_items(int type, int mt, const HostItem* it, int n, int x_dtype, int y
 
 int mma_init(int) {
     const char* env = getenv("NXQ_DECODE_KERNEL");
-    g_mma_enabled = !(env && env[0] && env[0] != 'm');  // "tc" / "simt" select another decode kernel
+    g_mma_enabled = !(env && env[0] == 's');  // "simt" selects the exact CUDA-core kernel
     const char* split = getenv("NXQ_GEMV_SPLIT");
     g_streamk = !(split && strcmp(split, "tiles") == 0);
     g_sm_count = context_sm_count();

@@ -7,8 +7,8 @@ namespace nxq {
 int context_sm_count();
 DeviceStatus* context_status();
 
-// Kernel attributes; reads NXQ_DECODE_KERNEL ("tc" or "simt" select another
-// decode kernel, for comparisons).
+// Kernel attributes; reads NXQ_DECODE_KERNEL ("simt" selects the exact
+// CUDA-core kernel instead, for comparisons).
 int mma_init(int device);
 bool mma_supported(const TiledShape& s, int64_t M);
 void mma_kernel_name(const TiledShape& s, int64_t M, char* buf, size_t n);

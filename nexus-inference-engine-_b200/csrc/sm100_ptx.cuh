@@ -78,7 +78,10 @@ struct WaitCtl {
 
 static __device__ __noinline__ void raise_timeout(const WaitCtl& c, unsigned where) {
     *c.abort = 1;
-    if (atomicCAS(&c.status->code, 0u, kStatusTimeout) == 0u) c.status->where = where;
+    if (atomicCAS(&c.status->code, 0u, kStatusTimeout) == 0u) {
+        c.status->where = where;
+        raise_host_flag(c.status);
+    }
     __threadfence();
 }
 

@@ -29,7 +29,7 @@
 #include <mutex>
 #include <thread>
 
-#include "qmm_tc.h"
+#include "nxq_internal.h"
 
 namespace nxq {
 int qmatmul_dispatch(const Weight* w, const void* x, int x_dtype, void* y, int y_dtype, int64_t M,

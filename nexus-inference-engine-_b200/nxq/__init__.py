@@ -647,7 +647,9 @@ class NXF:
         info = self.tensor_info(i)
         h = ctypes.c_void_p()
         _check(lib().nxq_nxf_register(self.handle, i, slice_, ctypes.byref(h)))
-        return Weight(h.value, self._type(info), info["dims"][1], info["dims"][0])
+        w = Weight(h.value, self._type(info), info["dims"][1], info["dims"][0])
+        w.type = w.info()["type"]  # the block type the library chose for the chunk's codec
+        return w
 
     def register_shard(self, name_or_index, split: int, rank: int, world: int, slice_: int = 0) -> "Weight":
         i = self.find(name_or_index) if isinstance(name_or_index, str) else int(name_or_index)
@@ -655,8 +657,10 @@ class NXF:
         h = ctypes.c_void_p()
         _check(lib().nxq_nxf_register_shard(self.handle, i, slice_, split, rank, world, ctypes.byref(h)))
         N, K = info["dims"][1], info["dims"][0]
-        return Weight(h.value, self._type(info), N // world if split == SPLIT_COL else N,
-                      K // world if split == SPLIT_ROW else K)
+        w = Weight(h.value, self._type(info), N // world if split == SPLIT_COL else N,
+                   K // world if split == SPLIT_ROW else K)
+        w.type = w.info()["type"]
+        return w
 
 
 # ---- tensor parallelism ------------------------------------------------------
