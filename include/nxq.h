@@ -332,9 +332,22 @@ NXQ_API int nxq_tp_shutdown(void);
 NXQ_API int nxq_tp_qmatmul(nxq_weight_t shard, const void* x_dev, int x_dtype, void* y_dev,
                            int y_dtype, int64_t M, int split, void* stream);
 
-/* Sum `count` fp32 values across the TP group in place on `stream`.  A
+/* Sum `count` fp32 values across the TP group in place on `stream`, by
+ * ncclAllReduce.  With NXQ_TP_ALLREDUCE=p2p set when nxq_tp_init runs, sums
+ * of up to 2^21 values (8 MB) run instead as one kernel over NVLink peer
+ * memory: every rank's symmetric buffer is mapped by the others through CUDA
+ * IPC at nxq_tp_init (the handles travel over the NCCL communicator), each
+ * rank copies its partial into its own buffer, raises per-slice ready flags
+ * in the peers' buffers, waits (bounded) for theirs and adds the ranks'
+ * slices in rank order, so every rank gets the same bits (measured slower
+ * than NCCL on two B200, hence not the default).  Like NCCL collectives, every
+ * rank issues the same sequence of allreduces; the peer-memory path also
+ * wants one rank's allreduces on one stream (they share the buffers).  A
  * collective that fails to enqueue aborts the communicator (NXQ_ERR_NCCL). */
 NXQ_API int nxq_tp_allreduce_f32(float* buf_dev, int64_t count, void* stream);
+
+/* Whether this rank's allreduces up to 8 MB run over peer memory (1) or NCCL (0). */
+NXQ_API int nxq_tp_p2p_enabled(int* on);
 
 /* Failure detection for the TP group (the reference has one device and
  * zero-fills silently, compute_dispatch.cpp:174-176): waits until the work

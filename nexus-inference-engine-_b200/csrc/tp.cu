@@ -28,8 +28,10 @@
 #include <cstring>
 #include <mutex>
 #include <thread>
+#include <vector>
 
 #include "nxq_internal.h"
+#include "tp_p2p.h"
 
 namespace nxq {
 int qmatmul_dispatch(const Weight* w, const void* x, int x_dtype, void* y, int y_dtype, int64_t M,
@@ -49,6 +51,7 @@ struct NcclApi {
     ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
     ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                               cudaStream_t) = nullptr;
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     const char* (*GetErrorString)(ncclResult_t) = nullptr;
 };
 
@@ -59,6 +62,17 @@ int g_rank = -1, g_world = 0;
 bool g_dead = false;  // the communicator was aborted: TP calls fail until shutdown + init
 char g_dead_why[256] = "";
 std::atomic<bool> g_hook_stream_pending{false};  // NXQ_HOOK_TP_STREAM_PENDING
+
+// The peer-memory allreduce (tp_p2p.cu): this rank's symmetric buffer, the
+// peers' buffers mapped through CUDA IPC, and the launch parameters.
+struct P2PState {
+    bool on = false;
+    void* base = nullptr;
+    void* peer[kP2PMaxWorld] = {};
+    P2PParams tmpl{};
+};
+P2PState g_p2p;
+constexpr int64_t kP2PCap = 1 << 21;  // floats per data half: allreduces up to 8 MB use peer memory
 
 int load_nccl() {
     if (g_nccl.lib) return NXQ_OK;
@@ -81,6 +95,7 @@ int load_nccl() {
     NXQ_SYM(CommAbort, "ncclCommAbort")
     NXQ_SYM(CommGetAsyncError, "ncclCommGetAsyncError")
     NXQ_SYM(AllReduce, "ncclAllReduce")
+    NXQ_SYM(AllGather, "ncclAllGather")
     NXQ_SYM(GetErrorString, "ncclGetErrorString")
 #undef NXQ_SYM
     g_nccl.lib = h;
@@ -113,6 +128,103 @@ int check_comm() {
         return abort_comm(NXQ_ERR_NCCL, why);
     }
     return NXQ_OK;
+}
+
+void p2p_teardown() {
+    for (int r = 0; r < kP2PMaxWorld; ++r)
+        if (g_p2p.peer[r]) cudaIpcCloseMemHandle(g_p2p.peer[r]);
+    if (g_p2p.base) cudaFree(g_p2p.base);
+    g_p2p = P2PState{};
+}
+
+// Maps every rank's symmetric buffer (caller holds g_tp_mu, communicator
+// up) when NXQ_TP_ALLREDUCE=p2p asks for the peer-memory allreduce.  It is
+// not the default: on two B200 it took 16-19 us per call for 16 KB - 2 MB
+// against NCCL's 12 us (measured in a CUDA graph of the benchmark's calls).
+// Any failure leaves it off; the allreduce then runs on NCCL.
+void p2p_setup() {
+    const char* env = getenv("NXQ_TP_ALLREDUCE");
+    if (g_world < 2 || g_world > kP2PMaxWorld || !(env && strcmp(env, "p2p") == 0)) return;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return;
+    }
+    const size_t bytes = p2p_bytes(g_world, kP2PCap);
+    bool ok = cudaMalloc(&g_p2p.base, bytes) == cudaSuccess && cudaMemset(g_p2p.base, 0, bytes) == cudaSuccess;
+    cudaIpcMemHandle_t mine{};
+    ok = ok && cudaIpcGetMemHandle(&mine, g_p2p.base) == cudaSuccess;
+    // Every rank takes part in the exchange, whatever happened above (a rank
+    // that failed sends a zero handle and all of them then keep NCCL).
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    uint8_t* dh = nullptr;
+    if (cudaMalloc(&dh, (g_world + 1) * hb) != cudaSuccess) {
+        cudaGetLastError();
+        p2p_teardown();
+        return;  // no exchange possible: all ranks fail the same allocation in practice
+    }
+    uint8_t flag = ok ? 1 : 0;
+    cudaMemcpy(dh + (size_t)g_rank * hb, &mine, hb, cudaMemcpyHostToDevice);
+    cudaMemcpy(dh + (size_t)g_world * hb, &flag, 1, cudaMemcpyHostToDevice);
+    ncclResult_t r = g_nccl.AllGather(dh + (size_t)g_rank * hb, dh, hb, ncclUint8, g_comm, 0);
+    if (r == ncclSuccess) r = g_nccl.AllReduce(dh + (size_t)g_world * hb, dh + (size_t)g_world * hb, 1, ncclUint8, ncclMin, g_comm, 0);
+    std::vector<cudaIpcMemHandle_t> hs((size_t)g_world);
+    uint8_t all_ok = 0;
+    if (r == ncclSuccess && cudaStreamSynchronize(0) == cudaSuccess) {
+        cudaMemcpy(hs.data(), dh, g_world * hb, cudaMemcpyDeviceToHost);
+        cudaMemcpy(&all_ok, dh + (size_t)g_world * hb, 1, cudaMemcpyDeviceToHost);
+    }
+    cudaFree(dh);
+    if (!all_ok) {
+        cudaGetLastError();
+        p2p_teardown();
+        return;
+    }
+    P2PParams& t = g_p2p.tmpl;
+    t.rank = g_rank;
+    t.world = g_world;
+    t.cap = kP2PCap;
+    for (int q = 0; q < g_world && ok; ++q) {
+        void* ptr = g_p2p.base;
+        if (q != g_rank) {
+            ok = cudaIpcOpenMemHandle(&g_p2p.peer[q], hs[q], cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+            ptr = g_p2p.peer[q];
+        }
+        t.data[q] = static_cast<float*>(ptr);
+        t.flags[q] = reinterpret_cast<unsigned long long*>(static_cast<char*>(ptr) + 2 * kP2PCap * sizeof(float));
+    }
+    // Whether every rank could map every peer decides for all of them.
+    uint8_t* dflag = nullptr;
+    flag = ok ? 1 : 0;
+    all_ok = 0;
+    if (cudaMalloc(&dflag, 1) == cudaSuccess) {
+        cudaMemcpy(dflag, &flag, 1, cudaMemcpyHostToDevice);
+        if (g_nccl.AllReduce(dflag, dflag, 1, ncclUint8, ncclMin, g_comm, 0) == ncclSuccess &&
+            cudaStreamSynchronize(0) == cudaSuccess)
+            cudaMemcpy(&all_ok, dflag, 1, cudaMemcpyDeviceToHost);
+        cudaFree(dflag);
+    }
+    if (!all_ok) {
+        cudaGetLastError();
+        p2p_teardown();
+        return;
+    }
+    t.ctl = t.flags[g_rank] + (size_t)g_world * kP2PBlocks;
+    g_p2p.on = true;
+}
+
+// All ranks' queued work is done before any rank unmaps or frees its buffer
+// (a peer's kernel may still read it): a device synchronize and a one-byte
+// NCCL allreduce as a barrier.
+void p2p_shutdown() {
+    if (!g_p2p.base) return;
+    cudaDeviceSynchronize();
+    uint8_t* d = nullptr;
+    if (!g_dead && cudaMalloc(&d, 1) == cudaSuccess) {
+        if (g_nccl.AllReduce(d, d, 1, ncclUint8, ncclMin, g_comm, 0) == ncclSuccess) cudaStreamSynchronize(0);
+        cudaFree(d);
+    }
+    p2p_teardown();
 }
 
 int check_weight_ptr(nxq_weight_t h, const Weight** out) {
@@ -158,12 +270,21 @@ NXQ_API int nxq_tp_init(int rank, int world, const void* unique_id, size_t n) {
     g_world = world;
     g_dead = false;
     g_dead_why[0] = 0;
+    p2p_setup();
+    return NXQ_OK;
+}
+
+NXQ_API int nxq_tp_p2p_enabled(int* on) {
+    if (!on) return fail(NXQ_ERR_ARG, "null argument");
+    std::lock_guard<std::mutex> lk(g_tp_mu);
+    *on = g_p2p.on ? 1 : 0;
     return NXQ_OK;
 }
 
 NXQ_API int nxq_tp_shutdown(void) {
     std::lock_guard<std::mutex> lk(g_tp_mu);
     if (!g_comm) return NXQ_OK;
+    p2p_shutdown();
     ncclResult_t r = ncclSuccess;
     if (!g_dead) {
         ncclResult_t async_err = ncclSuccess;
@@ -183,6 +304,16 @@ NXQ_API int nxq_tp_allreduce_f32(float* buf_dev, int64_t count, void* stream) {
     if (!buf_dev || count < 0) return fail(NXQ_ERR_ARG, "bad buffer");
     std::lock_guard<std::mutex> lk(g_tp_mu);
     if (int rc = check_comm()) return rc;
+    if (count == 0) return NXQ_OK;
+    if (g_p2p.on && count <= kP2PCap) {
+        P2PParams p = g_p2p.tmpl;
+        p.buf = buf_dev;
+        p.count = count;
+        p.status = context_status();
+        cudaError_t e = launch_p2p_allreduce(p, (cudaStream_t)stream);
+        if (e != cudaSuccess) return cuda_fail(e, "peer-memory allreduce launch");
+        return NXQ_OK;
+    }
     ncclResult_t r = g_nccl.AllReduce(buf_dev, buf_dev, (size_t)count, ncclFloat32, ncclSum, g_comm,
                                       (cudaStream_t)stream);
     if (r != ncclSuccess) {

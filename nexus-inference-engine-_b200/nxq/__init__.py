@@ -94,6 +94,7 @@ _SIGS = {
     "nxq_set_wait_limit": [_c.c_uint64],
     "nxq_test_hook": [_c.c_int, _c.c_int],
     "nxq_tp_wait": [_c.c_void_p, _c.c_int64],
+    "nxq_tp_p2p_enabled": [_c.c_void_p],
     "nxq_tp_test_hook": [_c.c_int, _c.c_int],
     "nxq_qmatmul_kernel_name": [_c.c_void_p, _c.c_int64, _c.c_int, _c.c_int, _c.c_char_p, _c.c_size_t],
     "nxq_launch_count": [_c.POINTER(_c.c_uint64)],
@@ -686,6 +687,13 @@ def tp_qmatmul(shard: Weight, x, out, split: int, stream=None):
     _check(lib().nxq_tp_qmatmul(shard.handle, x.data_ptr(), _dtype_code(x.dtype), out.data_ptr(),
                                 _dtype_code(out.dtype), M, split, _stream_ptr(stream)))
     return out
+
+
+def tp_p2p_enabled() -> bool:
+    """Whether allreduces up to 8 MB run over NVLink peer memory (else NCCL)."""
+    v = ctypes.c_int()
+    _check(lib().nxq_tp_p2p_enabled(ctypes.byref(v)))
+    return bool(v.value)
 
 
 def tp_wait(stream=None, timeout_ms: int = 10000) -> None:

@@ -34,6 +34,10 @@ int ncclAllReduce(const void* s, void* r, size_t n, int dt, int op, ncclComm_t c
     g_calls[3]++;
     return g_allreduce_rc;
 }
+int ncclAllGather(const void* s, void* r, size_t n, int dt, ncclComm_t comm, void* stream) {
+    (void)s; (void)r; (void)n; (void)dt; (void)comm; (void)stream;
+    return 0;
+}
 const char* ncclGetErrorString(int r) {
     static char buf[64];
     snprintf(buf, sizeof buf, "fake nccl error %d", r);

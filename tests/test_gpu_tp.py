@@ -113,3 +113,120 @@ def test_tp_qmatmul_two_gpus_matches_full(t):
     for rank in range(world):
         for key, err in out[rank].items():
             assert err < TOL, (rank, key, err)
+
+
+def _allreduce_worker(rank, world, port, sizes, q):
+    sys.path.insert(0, str(ROOT))
+    sys.path.insert(0, str(ROOT / "nexus-inference-engine-_b200"))
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import nxq
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    joined = False
+    try:
+        os.environ["NXQ_TP_ALLREDUCE"] = "p2p"
+        torch.cuda.set_device(rank)
+        nxq.init(rank)
+        uid = [nxq.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        nxq.tp_init(rank, world, uid[0])
+        joined = True
+        res = {"p2p": nxq.tp_p2p_enabled()}
+
+        def data(r, n, call):
+            g = np.random.default_rng(1000 * r + 7 * call + n)
+            return g.standard_normal(n).astype(np.float32)
+
+        for n in sizes:
+            for call in range(3):  # three calls: both halves of the buffer, epochs advancing
+                buf = torch.from_numpy(data(rank, n, call)).cuda()
+                nxq.tp_allreduce_f32(buf)
+                nxq.tp_wait(None, 20000)
+                got = buf.cpu().numpy()
+                want = np.zeros(n, np.float32)
+                for r in range(world):  # fp32, in rank order
+                    want = (want + data(r, n, call)).astype(np.float32)
+                exact = bool(np.array_equal(got, want))
+                rel = float(np.abs(got - want).max() / (np.abs(want).max() + 1e-30))
+                res[(n, call)] = (exact, rel, float(np.float64(got).sum()))
+        # Replayed from a CUDA graph: the epoch is a device counter.
+        n = 4096
+        s = torch.cuda.Stream()
+        bufs = [torch.from_numpy(data(rank, n, 10 + i)).cuda() for i in range(3)]
+        keep = [b.clone() for b in bufs]
+        with torch.cuda.stream(s):
+            nxq.tp_allreduce_f32(bufs[0], stream=s)  # outside capture first
+        s.synchronize()
+        for b, k in zip(bufs, keep):
+            b.copy_(k)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for b in bufs:
+                nxq.tp_allreduce_f32(b, stream=s)
+        for rep in range(2):
+            for b, k in zip(bufs, keep):
+                b.copy_(k)
+            torch.cuda.synchronize()
+            with torch.cuda.stream(s):
+                g.replay()
+            s.synchronize()
+            for i, b in enumerate(bufs):
+                want = np.zeros(n, np.float32)
+                for r in range(world):
+                    want = (want + data(r, n, 10 + i)).astype(np.float32)
+                res[("graph", rep, i)] = (bool(np.array_equal(b.cpu().numpy(), want)), 0.0, 0.0)
+        del g
+        nxq.stream_sync()
+        q.put((rank, res))
+    finally:
+        if joined:
+            nxq.tp_shutdown()
+        dist.destroy_process_group()
+
+
+def test_tp_allreduce_peer_memory_two_gpus():
+    """nxq_tp_allreduce_f32 on two GPUs with NXQ_TP_ALLREDUCE=p2p: up to 2^21
+    values over NVLink peer memory (the same bits as adding the ranks' inputs in rank order in fp32,
+    on every rank), beyond that over NCCL (within fp32 rounding); three calls
+    per size so both halves of the symmetric buffer and advancing epochs are
+    used; and three allreduces captured in a CUDA graph and replayed twice."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    world = 2
+    sizes = (1, 1000, 4096, 131072, 524289, 2 ** 21, 2 ** 21 + 5)
+    procs = [ctx.Process(target=_allreduce_worker, args=(r, world, port, sizes, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        for p in procs:
+            p.join(300)
+            assert p.exitcode == 0
+    finally:
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+    out = dict(q.get(timeout=5) for _ in range(world))
+    for rank in range(world):
+        assert out[rank]["p2p"], "peer-memory allreduce not enabled on two NVLink GPUs"
+        for key, val in out[rank].items():
+            if key == "p2p":
+                continue
+            exact, rel, _ = val
+            if key[0] == "graph" or key[0] <= 2 ** 21:
+                assert exact, (rank, key, rel)
+            else:
+                assert rel < 1e-6, (rank, key, rel)
+    for key in out[0]:
+        if key != "p2p" and key[0] != "graph":
+            assert out[0][key][2] == out[1][key][2], key  # every rank holds the same sum
