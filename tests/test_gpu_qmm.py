@@ -271,6 +271,34 @@ def test_split_k_is_deterministic_and_streams_are_independent(gpu, t):
         w.release()
 
 
+@pytest.mark.parametrize("t", MAIN_TYPES, ids=lambda t: NAMES[t])
+def test_prefill_stream_k_is_deterministic_and_streams_are_independent(gpu, t):
+    """Prefill with tiles split over CTAs by tile-chunks (stream-K: 32 row
+    tiles x 2 token tiles x 56 chunks over all SMs, about 24 chunks per CTA,
+    so most tiles are shared by three CTAs): the finishing CTA adds the
+    partials in CTA order, so repeated calls give identical bits, also on a
+    second stream, and the result matches the oracle."""
+    torch = _torch()
+    N, K, M = 4096, 14336 if t != 8 else 4096, 512
+    blocks = synth.make_blocks(t, N, K, seed=23)
+    w = gpu.Weight.register(blocks, t, N, K)
+    try:
+        assert gpu.kernel_name(w, M, gpu.F16, gpu.F32).startswith("tc_gemm<")
+        x = torch.from_numpy(synth.make_activations(M, K, seed=24, dtype=np.float16)).cuda()
+        y1 = gpu.qmatmul(w, x)
+        y2 = gpu.qmatmul(w, x)
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            y3 = gpu.qmatmul(w, x, stream=s)
+        torch.cuda.synchronize()
+        gpu.stream_sync()
+        assert torch.equal(y1, y2) and torch.equal(y1, y3)
+        want = loader.qmatmul(t, blocks, N, K, x.float().cpu().numpy())
+        assert synth.rel_l2(y1.cpu().numpy(), want) < TOL
+    finally:
+        w.release()
+
+
 def test_launch_counter_counts_our_kernels(gpu):
     torch = _torch()
     blocks = synth.make_blocks(12, 512, 1024, seed=2)
@@ -406,16 +434,19 @@ def test_rmsnorm_output_beyond_f16_range_is_reported(gpu):
         w.release()
 
 
-def test_streamk_wait_runs_out_and_the_context_recovers(gpu):
+@pytest.mark.parametrize("N,M", [(14336, 1), (1024, 64)], ids=["decode_gemv", "prefill_gemm"])
+def test_streamk_wait_runs_out_and_the_context_recovers(gpu, N, M):
     """Failure detection on the GPU without a fault: with a 2 ms wait limit
     and the stream-K publishers told not to count themselves in, the CTA that
-    finishes a shared row tile waits for counts that never come; its bounded
+    finishes a shared tile waits for counts that never come; its bounded
     wait runs out, the kernel ends, and the next synchronization reports
     NXQ_ERR_TIMEOUT.  With the hook off and the limit back to default, the
     next ordinary call on the same stream is correct (the host cleared the
-    tile counters when it reported the timeout)."""
+    tile counters when it reported the timeout).  Decode: 112 row tiles x 16
+    chunks over the SMs; prefill: 8 row tiles x 16 chunks, one chunk per
+    CTA, each tile finished by one CTA for 15 publishers."""
     torch = _torch()
-    t, N, K, M = 12, 14336, 4096, 1  # 112 row tiles x 16 chunks over 148 SMs: stream-K
+    t, K = 12, 4096
     blocks = synth.make_blocks(t, N, K, seed=95)
     w = gpu.Weight.register(blocks, t, N, K)
     stream = torch.cuda.Stream()
