@@ -8,7 +8,7 @@
 //
 // Work: a persistent grid of one CTA per SM walks (weight tile, token tile)
 // work tiles of 128 weight rows x 256 tokens.  When whole tiles would leave
-// SMs idle in the last wave, the first tiles are instead split over all CTAs
+// SMs idle in the last wave, the last tiles are instead split over all CTAs
 // by 256-k tile-chunks (stream-K, the work list below), so every SM gets the
 // same number of tile-chunks.  Per 64-element k-step:
 //   warp 26      producer: the packed tile-chunk (256 k) by one 1-D bulk copy
@@ -85,7 +85,7 @@ struct GemmParams {
     int y_dtype;
     int m_tiles;
     int tiles;
-    int sk_tiles;    // tiles [0, sk_tiles) are split over the CTAs by tile-chunks (stream-K)
+    int sk_tiles;    // the last sk_tiles tiles are split over the CTAs by tile-chunks (stream-K)
     int sk_units;    // sk_tiles * chunks
     float* part;     // stream-K partials: [grid][kNT tokens][TILE_ROWS rows] fp32
     unsigned* cnt;   // stream-K counts, one per stream-K tile (zero between launches)
@@ -93,9 +93,12 @@ struct GemmParams {
 };
 
 // ---- work list ---------------------------------------------------------------
-// CTA q first takes units (tile-chunks, tile-major) [start(q), start(q+1)) of
-// the stream-K tiles, then whole tiles sk_tiles + q, + grid, ...  Within its
-// stream-K run a CTA meets a tile in one of three ways:
+// CTA q first takes whole tiles q, q + grid, ... of the first T - sk_tiles
+// tiles (a multiple of the grid: every CTA the same number, so all CTAs stay
+// in step, reading the same activation boxes and weight tile-chunks at about
+// the same time), then units (tile-chunks, tile-major) [start(q),
+// start(q+1)) of the last sk_tiles tiles.  Within its stream-K run a CTA
+// meets a tile in one of three ways:
 //   kWhole   it holds every chunk of the tile: stores y;
 //   kPublish its run starts inside the tile (only its first tile can): it
 //            writes its fp32 partial to its slot and counts it;
@@ -110,6 +113,7 @@ constexpr int kPartFloats = kNT * TILE_ROWS;
 
 struct WorkItem {
     int tile, c0, c1, mode, nshare;
+    int sk;  // stream-K tile index (its counter), or -1
 };
 
 __device__ __forceinline__ int sk_start(const GemmParams& p, int q) {
@@ -127,38 +131,37 @@ __device__ __forceinline__ int sk_owner(const GemmParams& p, int u) {
 // Item i of this CTA's list; false past its end.
 __device__ __forceinline__ bool work_item(const GemmParams& p, int i, WorkItem& w) {
     const int q = blockIdx.x, G = gridDim.x, C = (int)p.s.chunks;
-    int ns = 0, t0 = 0, u0 = 0, u1 = 0;
-    if (p.sk_units > 0) {
-        u0 = sk_start(p, q);
-        u1 = sk_start(p, q + 1);
-        if (u1 > u0) {
-            t0 = u0 / C;
-            ns = (u1 - 1) / C - t0 + 1;
-        }
-    }
-    if (i < ns) {
-        const int t = t0 + i;
-        w.tile = t;
-        w.c0 = u0 > t * C ? u0 - t * C : 0;
-        w.c1 = u1 < (t + 1) * C ? u1 - t * C : C;
+    const int dp_tiles = p.tiles - p.sk_tiles;
+    const int ndp = q < dp_tiles ? (dp_tiles - 1 - q) / G + 1 : 0;
+    if (i < ndp) {
+        w.tile = q + i * G;
+        w.c0 = 0;
+        w.c1 = C;
+        w.mode = kWhole;
         w.nshare = 0;
-        if (w.c0 > 0)
-            w.mode = kPublish;
-        else if (w.c1 == C)
-            w.mode = kWhole;
-        else {
-            w.mode = kFinish;
-            w.nshare = sk_owner(p, (t + 1) * C - 1) - q;
-        }
+        w.sk = -1;
         return true;
     }
-    const long long tile = (long long)p.sk_tiles + q + (long long)(i - ns) * G;
-    if (tile >= p.tiles) return false;
-    w.tile = (int)tile;
-    w.c0 = 0;
-    w.c1 = C;
-    w.mode = kWhole;
+    i -= ndp;
+    if (p.sk_units == 0) return false;
+    const int u0 = sk_start(p, q), u1 = sk_start(p, q + 1);
+    if (u1 <= u0) return false;
+    const int t0 = u0 / C, ns = (u1 - 1) / C - t0 + 1;
+    if (i >= ns) return false;
+    const int t = t0 + i;
+    w.sk = t;
+    w.tile = dp_tiles + t;
+    w.c0 = u0 > t * C ? u0 - t * C : 0;
+    w.c1 = u1 < (t + 1) * C ? u1 - t * C : C;
     w.nshare = 0;
+    if (w.c0 > 0)
+        w.mode = kPublish;
+    else if (w.c1 == C)
+        w.mode = kWhole;
+    else {
+        w.mode = kFinish;
+        w.nshare = sk_owner(p, (t + 1) * C - 1) - q;
+    }
     return true;
 }
 
@@ -405,7 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p
             // A finisher first waits (bounded) for the sharers' counts: one
             // per epilogue warp of each.
             const bool finish = it.mode == kFinish &&
-                                count_wait(p.cnt + it.tile, (unsigned)(kEpiWarps * it.nshare), ctl, p.status, 19);
+                                count_wait(p.cnt + it.sk, (unsigned)(kEpiWarps * it.nshare), ctl, p.status, 19);
 #pragma unroll 1
             for (int cb = 0; cb < 4; ++cb) {
                 uint32_t v[32];
@@ -447,13 +450,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p
                 if (lane == 0) {
                     __threadfence();
                     const unsigned hooks = *reinterpret_cast<const volatile unsigned*>(&p.status->hooks);
-                    if (!(hooks & kHookStreamKSkipCount)) atomicAdd(p.cnt + it.tile, 1u);
+                    if (!(hooks & kHookStreamKSkipCount)) atomicAdd(p.cnt + it.sk, 1u);
                 }
             } else if (finish && lane == 0) {
                 // The last of the finisher's warps to pass its wait clears the
                 // count for the next launch.
                 const unsigned need = (unsigned)(kEpiWarps * it.nshare);
-                if (atomicAdd(p.cnt + it.tile, 1u) == need + kEpiWarps - 1) atomicExch(p.cnt + it.tile, 0u);
+                if (atomicAdd(p.cnt + it.sk, 1u) == need + kEpiWarps - 1) atomicExch(p.cnt + it.sk, 0u);
             }
             ptx::tc_fence_before();
             __syncwarp();
@@ -507,20 +510,22 @@ int launch(const Weight* w, const CUtensorMap& tmap, void* y, int y_dtype, int64
     const int G = context_sm_count(), C = (int)w->shape.chunks;
     int grid = G < p.tiles ? G : p.tiles;
     // Stream-K when whole tiles would leave SMs idle in the last wave for at
-    // least two tile-chunks per CTA on average: the last partial wave plus one
-    // full wave (all tiles when there are fewer than two waves) are split by
-    // tile-chunks over all CTAs.  The partials need the stream's workspace; a
-    // stream being captured whose workspace is still too small runs whole tiles.
+    // least two tile-chunks per CTA on average: the tiles of the last partial
+    // wave (with one full wave more when they are fewer than half the grid, so
+    // that no CTA's run is much shorter than a tile; all tiles when there is
+    // less than one wave) are split by tile-chunks over all CTAs.  The
+    // partials need the stream's workspace; a stream being captured whose
+    // workspace is still too small runs whole tiles.
     const int rem = p.tiles % G;
     if (g_gemm_streamk && rem != 0 && (int64_t)(G - rem) * C >= 2 * (int64_t)G) {
         StreamScratch* sc = nullptr;
         if (int rc = scratch_try(st, (size_t)G * kPartFloats, (size_t)3 * G, &sc)) return rc;
         if (sc) {
-            p.sk_tiles = p.tiles < 2 * G ? p.tiles : rem + G;
+            p.sk_tiles = p.tiles < G ? p.tiles : 2 * rem >= G ? rem : rem + G;
             p.sk_units = p.sk_tiles * C;
             p.part = sc->ws;
             p.cnt = sc->counters + G;  // [0, G) belong to the decode GEMV
-            grid = p.tiles >= 2 * G || p.sk_units >= G ? G : p.sk_units;
+            grid = p.tiles >= G || p.sk_units >= G ? G : p.sk_units;
         }
     }
     tc_gemm_kernel<TYPE><<<grid, kThreads, smem_bytes<TYPE>(), st>>>(p, tmap);

@@ -163,6 +163,22 @@ def lib() -> ctypes.CDLL:
     return _lib
 
 
+_dispatch = None
+
+
+def dispatch_lib() -> ctypes.CDLL:
+    """Load the engine-side shim library libnxq_dispatch.so (built by build.py
+    beside libnxq.so, which it links; the same instance as lib())."""
+    global _dispatch
+    if _dispatch is None:
+        lib()
+        path = LIB_PATH.with_name("libnxq_dispatch.so")
+        if not path.exists():
+            raise ImportError(f"{path} is missing: run `python nexus-inference-engine-_b200/build.py`")
+        _dispatch = ctypes.CDLL(str(path))
+    return _dispatch
+
+
 def declared_symbols() -> list[str]:
     """Entry points declared in include/nxq.h (NXQ_API functions)."""
     text = HEADER.read_text()

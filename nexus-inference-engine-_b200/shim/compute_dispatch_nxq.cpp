@@ -2,6 +2,7 @@
 // gemv_int4 over libnxq.so.
 #include "compute_dispatch_nxq.h"
 
+#include <chrono>
 #include <cstring>
 #include <vector>
 
@@ -117,3 +118,15 @@ void ComputeDispatchShim::clear_buffer_cache() {
 }
 
 }  // namespace nxq
+
+extern "C" int nxq_dispatch_host_steps(const nxq_weight_t* w, const float* const* x, float* const* y,
+                                       const int64_t* M, int n, int steps, double* seconds) {
+    if (!w || !x || !y || !M || n < 0 || steps < 0 || !seconds) return NXQ_ERR_ARG;
+    const auto t0 = std::chrono::steady_clock::now();
+    for (int s = 0; s < steps; ++s)
+        for (int i = 0; i < n; ++i)
+            if (const int rc = nxq_qmatmul_host(w[i], x[i], y[i], M[i])) return rc;
+    *seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    return NXQ_OK;
+}
+

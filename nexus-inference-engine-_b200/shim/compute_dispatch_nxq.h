@@ -95,3 +95,13 @@ private:
 };
 
 }  // namespace nxq
+
+// The engine's synchronous call pattern, timed in C++: `steps` passes over the
+// n calls nxq_qmatmul_host(w[i], x[i], y[i], M[i]) (host fp32 activations and
+// outputs, weights resident), one after another on the calling thread, as
+// ComputeDispatch::gemm_int4 issues them (compute_dispatch.cpp:142-176).
+// Stores the wall time of all passes in *seconds; returns the first failing
+// call's status.  bench.py measures the host drop-in with it, so no Python
+// call overhead sits between the calls.
+extern "C" int nxq_dispatch_host_steps(const nxq_weight_t* w, const float* const* x, float* const* y,
+                                       const int64_t* M, int n, int steps, double* seconds);

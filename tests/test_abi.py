@@ -23,6 +23,23 @@ def test_library_exports_every_declared_symbol():
     assert L.nxq_abi_version() == 1
 
 
+def test_shim_library_loads_into_the_same_context():
+    """The engine-side shim library links libnxq.so and shares its instance:
+    a call through the shim's C++ loop sees the same (uninitialised, here)
+    context as a direct call, and its argument checks run without a GPU."""
+    D = nxq.dispatch_lib()
+    f = D.nxq_dispatch_host_steps
+    f.restype = ctypes.c_int
+    sec = ctypes.c_double(-1.0)
+    assert f(None, None, None, None, 0, 1, ctypes.byref(sec)) == -1  # null arrays
+    one = (ctypes.c_void_p * 1)(None)
+    m = (ctypes.c_int64 * 1)(1)
+    # A null weight handle is refused by libnxq itself: the loop forwards it.
+    assert f(one, one, one, m, 1, 1, ctypes.byref(sec)) == -1
+    assert "null weight handle" in nxq.last_error()
+    assert f(one, one, one, m, 0, 3, ctypes.byref(sec)) == 0 and sec.value >= 0.0
+
+
 def test_header_entry_points_cite_the_reference():
     text = nxq.HEADER.read_text()
     # Every declaration block carries a reference citation or states that the
