@@ -293,11 +293,11 @@ NXQ_API int nxq_set_wait_limit(uint64_t microseconds);
 /* Test hooks for failure-detection tests: they make a bounded wait run out on
  * purpose (nothing faults, traps or waits beyond the limit).  Off by default;
  * each call synchronizes the device.
- *   NXQ_HOOK_STREAMK_SKIP_COUNT: in the stream-K splits of the decode GEMV
- *     and the prefill GEMM, the CTAs that publish a partial sum of a tile
- *     another CTA finishes do not count themselves in, so that CTA's wait for
- *     the counts runs out (NXQ_ERR_TIMEOUT; that call's output is
- *     incomplete).  No counterpart in the reference. */
+ *   NXQ_HOOK_STREAMK_SKIP_COUNT: in the decode GEMV's stream-K split, the CTAs
+ *     that publish a partial sum of a row tile another CTA finishes do not
+ *     count themselves in, so that CTA's wait for the counts runs out
+ *     (NXQ_ERR_TIMEOUT; that call's output is incomplete).  No counterpart in
+ *     the reference. */
 typedef enum { NXQ_HOOK_STREAMK_SKIP_COUNT = 1, NXQ_HOOK_TP_STREAM_PENDING = 2 } nxq_test_hook_id;
 NXQ_API int nxq_test_hook(int hook, int on);
 

@@ -7,10 +7,7 @@
 // prefill path for batches of more than 32 tokens.
 //
 // Work: a persistent grid of one CTA per SM walks (weight tile, token tile)
-// work tiles of 128 weight rows x 256 tokens.  When whole tiles would leave
-// SMs idle in the last wave, the last tiles are instead split over all CTAs
-// by 256-k tile-chunks (stream-K, the work list below), so every SM gets the
-// same number of tile-chunks.  Per 64-element k-step:
+// work tiles of 128 weight rows x 256 tokens.  Per 64-element k-step:
 //   warp 26      producer: the packed tile-chunk (256 k) by one 1-D bulk copy
 //                per chunk, up to four chunks ahead (Rings)
 //   warp 0       producer: the 256 x 64 f16 activation box by TMA (128-byte
@@ -23,9 +20,7 @@
 //                (A from TMEM, B from shared memory) into a 256-column fp32
 //                accumulator in TMEM
 //   warps 18-25  epilogue: tcgen05.ld of the accumulator (two warps per lane
-//                quadrant), conversion, store (or, for a stream-K tile, the
-//                fp32 partial to the workspace, or the sharers' partials
-//                added before the store)
+//                quadrant), conversion, store
 // (Measured: two N=128 mma per K=16 into accumulator halves handed back
 // separately, so the next tile starts while the second half drains, ran 18 %
 // slower than one N=256 mma.)
@@ -85,85 +80,8 @@ struct GemmParams {
     int y_dtype;
     int m_tiles;
     int tiles;
-    int sk_tiles;    // the last sk_tiles tiles are split over the CTAs by tile-chunks (stream-K)
-    int sk_units;    // sk_tiles * chunks
-    float* part;     // stream-K partials: [grid][kNT tokens][TILE_ROWS rows] fp32
-    unsigned* cnt;   // stream-K counts, one per stream-K tile (zero between launches)
     DeviceStatus* status;
 };
-
-// ---- work list ---------------------------------------------------------------
-// CTA q first takes whole tiles q, q + grid, ... of the first T - sk_tiles
-// tiles (a multiple of the grid: every CTA the same number, so all CTAs stay
-// in step, reading the same activation boxes and weight tile-chunks at about
-// the same time), then units (tile-chunks, tile-major) [start(q),
-// start(q+1)) of the last sk_tiles tiles.  Within its stream-K run a CTA
-// meets a tile in one of three ways:
-//   kWhole   it holds every chunk of the tile: stores y;
-//   kPublish its run starts inside the tile (only its first tile can): it
-//            writes its fp32 partial to its slot and counts it;
-//   kFinish  it holds the tile's first chunks and the tile continues in CTAs
-//            q+1 .. q+nshare (its last tile): it waits for their counts and
-//            adds their partials after its own, in CTA order (the same bits on
-//            every call), then stores y.
-// Publishers count before they wait for anything, and a finisher waits only at
-// the end of its run, so with every CTA resident the waits form no cycle.
-constexpr int kWhole = 0, kPublish = 1, kFinish = 2;
-constexpr int kPartFloats = kNT * TILE_ROWS;
-
-struct WorkItem {
-    int tile, c0, c1, mode, nshare;
-    int sk;  // stream-K tile index (its counter), or -1
-};
-
-__device__ __forceinline__ int sk_start(const GemmParams& p, int q) {
-    return (int)(((long long)q * p.sk_units) / gridDim.x);
-}
-
-// The CTA whose stream-K run holds unit u.
-__device__ __forceinline__ int sk_owner(const GemmParams& p, int u) {
-    int q = (int)(((long long)u * gridDim.x) / p.sk_units);
-    while (q + 1 < (int)gridDim.x && sk_start(p, q + 1) <= u) ++q;
-    while (q > 0 && sk_start(p, q) > u) --q;
-    return q;
-}
-
-// Item i of this CTA's list; false past its end.
-__device__ __forceinline__ bool work_item(const GemmParams& p, int i, WorkItem& w) {
-    const int q = blockIdx.x, G = gridDim.x, C = (int)p.s.chunks;
-    const int dp_tiles = p.tiles - p.sk_tiles;
-    const int ndp = q < dp_tiles ? (dp_tiles - 1 - q) / G + 1 : 0;
-    if (i < ndp) {
-        w.tile = q + i * G;
-        w.c0 = 0;
-        w.c1 = C;
-        w.mode = kWhole;
-        w.nshare = 0;
-        w.sk = -1;
-        return true;
-    }
-    i -= ndp;
-    if (p.sk_units == 0) return false;
-    const int u0 = sk_start(p, q), u1 = sk_start(p, q + 1);
-    if (u1 <= u0) return false;
-    const int t0 = u0 / C, ns = (u1 - 1) / C - t0 + 1;
-    if (i >= ns) return false;
-    const int t = t0 + i;
-    w.sk = t;
-    w.tile = dp_tiles + t;
-    w.c0 = u0 > t * C ? u0 - t * C : 0;
-    w.c1 = u1 < (t + 1) * C ? u1 - t * C : C;
-    w.nshare = 0;
-    if (w.c0 > 0)
-        w.mode = kPublish;
-    else if (w.c1 == C)
-        w.mode = kWhole;
-    else {
-        w.mode = kFinish;
-        w.nshare = sk_owner(p, (t + 1) * C - 1) - q;
-    }
-    return true;
-}
 
 template <typename T>
 __device__ __forceinline__ T from_f32(float v);
@@ -191,28 +109,6 @@ __device__ __forceinline__ void store_col(void* y, int64_t off, int64_t N, int c
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const ptx::WaitCtl& c, unsigned where) {
     int ok = 0;
     if ((threadIdx.x & 31) == 0) ok = ptx::mbar_wait(bar, parity, c, where) ? 1 : 0;
-    return __shfl_sync(0xFFFFFFFFu, ok, 0) != 0;
-}
-
-// Lane 0 waits (bounded) until *c >= need (acquire); the warp learns whether
-// it did.  A wait that runs out records a timeout and raises the abort flag.
-__device__ __forceinline__ bool count_wait(const unsigned* c, unsigned need, const ptx::WaitCtl& ctl,
-                                           const DeviceStatus* status, unsigned where) {
-    int ok = 1;
-    if ((threadIdx.x & 31) == 0) {
-        const long long w0 = clock64(), lim = ptx::wait_limit(status);
-        for (;;) {
-            unsigned v;
-            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
-            if (v >= need) break;
-            if (*ctl.abort || clock64() - w0 > lim) {
-                if (!*ctl.abort) ptx::raise_timeout(ctl, where);
-                ok = 0;
-                break;
-            }
-            __nanosleep(64);
-        }
-    }
     return __shfl_sync(0xFFFFFFFFu, ok, 0) != 0;
 }
 
@@ -281,14 +177,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    const int chunks = (int)p.s.chunks;
+    const int G = gridDim.x;
+
     if (warp == kWarpWProducer) {
         if (lane == 0) {
             uint32_t qw = 0;
             bool ok = true;
-            WorkItem it;
-            for (int i = 0; ok && work_item(p, i, it); ++i) {
-                const int wt = it.tile / p.m_tiles;
-                for (int c = it.c0; c < it.c1 && ok; ++c, ++qw) {
+            for (int tile = blockIdx.x; tile < p.tiles && ok; tile += G) {
+                const int wt = tile / p.m_tiles;
+                for (int c = 0; c < chunks && ok; ++c, ++qw) {
                     const int sw = qw % kWStages;
                     if (qw >= kWStages && !(ok = ptx::mbar_wait(&w_empty[sw], ((qw / kWStages) & 1) ^ 1u, ctl, 11)))
                         break;
@@ -308,10 +206,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p
             ptx::prefetch_tmap(&xmap);
             uint32_t qx = 0;
             bool ok = true;
-            WorkItem it;
-            for (int i = 0; ok && work_item(p, i, it); ++i) {
-                const int mt = it.tile % p.m_tiles;
-                for (int c = it.c0; c < it.c1 && ok; ++c) {
+            for (int tile = blockIdx.x; tile < p.tiles && ok; tile += G) {
+                const int wt = tile / p.m_tiles, mt = tile - wt * p.m_tiles;
+                (void)wt;
+                for (int c = 0; c < chunks && ok; ++c) {
                     for (int st = 0; st < kStepsPerChunk; ++st, ++qx) {
                         const int sx = qx % kXStages;
                         if (qx >= kXStages &&
@@ -333,11 +231,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p
         if (lane == 0) {
             uint32_t qx = 0, qa = 0, nt = 0;
             bool ok = true;
-            WorkItem it;
-            for (int i = 0; ok && work_item(p, i, it); ++i, ++nt) {
+            for (int tile = blockIdx.x; tile < p.tiles && ok; tile += G, ++nt) {
                 if (nt > 0 && !(ok = ptx::mbar_wait(d_empty, (nt - 1) & 1, ctl, 13))) break;
                 ptx::tc_fence_after();
-                for (int c = it.c0; c < it.c1 && ok; ++c) {
+                for (int c = 0; c < chunks && ok; ++c) {
                     for (int st = 0; st < kStepsPerChunk; ++st, ++qx, ++qa) {
                         const int sx = qx % kXStages, sa = qa % kAStages;
                         if (!(ok = ptx::mbar_wait(&x_full[sx], (qx / kXStages) & 1, ctl, 14))) break;
@@ -347,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p
 #pragma unroll
                         for (int kk = 0; kk < kKS / 16; ++kk)
                             ptx::mma_ts_f16(tmem + kColD, tmem + sa * 32 + kk * 8, ptx::desc_sw128_kmajor(xb + kk * 32),
-                                            IDESC, (c == it.c0 && st == 0 && kk == 0) ? 0u : 1u);
+                                            IDESC, (c == 0 && st == 0 && kk == 0) ? 0u : 1u);
                         ptx::mma_commit(&x_empty[sx]);
                         ptx::mma_commit(&a_empty[sa]);
                     }
@@ -365,9 +262,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p
         const int h = wg & 1, par = wg >> 1;
         uint32_t qw = 0, qa = 0;
         bool ok = true;
-        WorkItem it;
-        for (int i = 0; ok && work_item(p, i, it); ++i) {
-            for (int c = it.c0; c < it.c1 && ok; ++c, ++qw) {
+        for (int tile = blockIdx.x; tile < p.tiles && ok; tile += G) {
+            for (int c = 0; c < chunks && ok; ++c, ++qw) {
                 const int sw = qw % kWStages;
                 if (!(ok = warp_wait(&w_full[sw], (qw / kWStages) & 1, ctl, 16))) break;
                 const uint8_t* stage = ws + sw * WB;
@@ -394,21 +290,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p
     } else {
         // Epilogue: warp (quad, sub) reads TMEM lanes 32 quad .. (its lane
         // quadrant) = weight row n, and token columns 128 sub .. 128 sub + 127.
-        // Stream-K partials are [token][row] in the CTA's slot: a warp's 32
-        // lanes (rows) store or load 128 contiguous bytes per token.
         const int ew = warp - kWarpEpi0, quad = warp & 3, r = quad * 32 + lane, sub = ew >> 2;
         const int64_t M = p.M, N = p.s.N;
         uint32_t nt = 0;
-        WorkItem it;
-        for (int i = 0; work_item(p, i, it); ++i, ++nt) {
+        for (int tile = blockIdx.x; tile < p.tiles; tile += G, ++nt) {
             if (!warp_wait(d_full, nt & 1, ctl, 18)) break;
             ptx::tc_fence_after();
-            const int wt = it.tile / p.m_tiles, mt = it.tile - wt * p.m_tiles;
+            const int wt = tile / p.m_tiles, mt = tile - wt * p.m_tiles;
             const int64_t n = (int64_t)wt * TILE_ROWS + r;
-            // A finisher first waits (bounded) for the sharers' counts: one
-            // per epilogue warp of each.
-            const bool finish = it.mode == kFinish &&
-                                count_wait(p.cnt + it.sk, (unsigned)(kEpiWarps * it.nshare), ctl, p.status, 19);
 #pragma unroll 1
             for (int cb = 0; cb < 4; ++cb) {
                 uint32_t v[32];
@@ -417,22 +306,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p
                 ptx::tmem_ld16(ta, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
                 ptx::tmem_ld16(ta + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
                 ptx::tmem_wait_ld();
-                if (it.mode == kPublish) {
-                    float* dst = p.part + (size_t)blockIdx.x * kPartFloats + (size_t)c0 * TILE_ROWS + r;
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) __stcg(dst + j * TILE_ROWS, __uint_as_float(v[j]));
-                    continue;
-                }
-                if (it.mode == kFinish) {
-                    if (!finish) continue;
-                    for (int sh = 1; sh <= it.nshare; ++sh) {
-                        const float* src =
-                            p.part + (size_t)(blockIdx.x + sh) * kPartFloats + (size_t)c0 * TILE_ROWS + r;
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            v[j] = __float_as_uint(__uint_as_float(v[j]) + __ldcg(src + j * TILE_ROWS));
-                    }
-                }
                 const int64_t m0 = (int64_t)mt * kNT + c0;
                 const int cnt = M - m0 >= 32 ? 32 : (int)(M - m0);
                 if (n < N && cnt > 0) {
@@ -443,20 +316,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(const GemmParams p
                     else
                         store_col<float>(p.y, m0 * N + n, N, cnt, v);
                 }
-            }
-            if (it.mode == kPublish) {
-                // The warp's partial (ordered by the warp barrier) before its count.
-                __syncwarp();
-                if (lane == 0) {
-                    __threadfence();
-                    const unsigned hooks = *reinterpret_cast<const volatile unsigned*>(&p.status->hooks);
-                    if (!(hooks & kHookStreamKSkipCount)) atomicAdd(p.cnt + it.sk, 1u);
-                }
-            } else if (finish && lane == 0) {
-                // The last of the finisher's warps to pass its wait clears the
-                // count for the next launch.
-                const unsigned need = (unsigned)(kEpiWarps * it.nshare);
-                if (atomicAdd(p.cnt + it.sk, 1u) == need + kEpiWarps - 1) atomicExch(p.cnt + it.sk, 0u);
             }
             ptx::tc_fence_before();
             __syncwarp();
@@ -477,7 +336,6 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn g_encode = nullptr;
 bool g_gemm_enabled = true;
-bool g_gemm_streamk = true;  // NXQ_PREFILL_SPLIT=tiles: whole tiles only
 
 template <int TYPE>
 size_t smem_bytes() {
@@ -502,32 +360,9 @@ int launch(const Weight* w, const CUtensorMap& tmap, void* y, int y_dtype, int64
     p.y_dtype = y_dtype;
     p.m_tiles = (int)((M + kNT - 1) / kNT);
     p.tiles = (int)(w->shape.tiles * p.m_tiles);
-    p.sk_tiles = 0;
-    p.sk_units = 0;
-    p.part = nullptr;
-    p.cnt = nullptr;
     p.status = context_status();
-    const int G = context_sm_count(), C = (int)w->shape.chunks;
-    int grid = G < p.tiles ? G : p.tiles;
-    // Stream-K when whole tiles would leave SMs idle in the last wave for at
-    // least two tile-chunks per CTA on average: the tiles of the last partial
-    // wave (with one full wave more when they are fewer than half the grid, so
-    // that no CTA's run is much shorter than a tile; all tiles when there is
-    // less than one wave) are split by tile-chunks over all CTAs.  The
-    // partials need the stream's workspace; a stream being captured whose
-    // workspace is still too small runs whole tiles.
-    const int rem = p.tiles % G;
-    if (g_gemm_streamk && rem != 0 && (int64_t)(G - rem) * C >= 2 * (int64_t)G) {
-        StreamScratch* sc = nullptr;
-        if (int rc = scratch_try(st, (size_t)G * kPartFloats, (size_t)3 * G, &sc)) return rc;
-        if (sc) {
-            p.sk_tiles = p.tiles < G ? p.tiles : 2 * rem >= G ? rem : rem + G;
-            p.sk_units = p.sk_tiles * C;
-            p.part = sc->ws;
-            p.cnt = sc->counters + G;  // [0, G) belong to the decode GEMV
-            grid = p.tiles >= G || p.sk_units >= G ? G : p.sk_units;
-        }
-    }
+    int grid = context_sm_count();
+    if (grid > p.tiles) grid = p.tiles;
     tc_gemm_kernel<TYPE><<<grid, kThreads, smem_bytes<TYPE>(), st>>>(p, tmap);
     cudaError_t e = cudaGetLastError();
     note_launches(1);
@@ -546,8 +381,6 @@ bool type_ok(int type) {
 int gemm_init(int) {
     const char* env = getenv("NXQ_PREFILL_KERNEL");
     g_gemm_enabled = !(env && env[0] == 's');  // "simt" selects the CUDA-core kernel
-    const char* split = getenv("NXQ_PREFILL_SPLIT");
-    g_gemm_streamk = !(split && split[0] == 't');
     if (!g_gemm_enabled) return NXQ_OK;
     // The activation boxes are TMA copies described by a tensor map, which
     // only the driver can encode.  Without that entry point the tensor-core

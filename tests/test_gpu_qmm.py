@@ -272,12 +272,10 @@ def test_split_k_is_deterministic_and_streams_are_independent(gpu, t):
 
 
 @pytest.mark.parametrize("t", MAIN_TYPES, ids=lambda t: NAMES[t])
-def test_prefill_stream_k_is_deterministic_and_streams_are_independent(gpu, t):
-    """Prefill with tiles split over CTAs by tile-chunks (stream-K: 32 row
-    tiles x 2 token tiles x 56 chunks over all SMs, about 24 chunks per CTA,
-    so most tiles are shared by three CTAs): the finishing CTA adds the
-    partials in CTA order, so repeated calls give identical bits, also on a
-    second stream, and the result matches the oracle."""
+def test_prefill_is_deterministic_and_streams_are_independent(gpu, t):
+    """Prefill (32 row tiles x 2 token tiles of the persistent tensor-core
+    GEMM, K = 14336): repeated calls give identical bits, also on a second
+    stream, and the result matches the oracle."""
     torch = _torch()
     N, K, M = 4096, 14336 if t != 8 else 4096, 512
     blocks = synth.make_blocks(t, N, K, seed=23)
@@ -434,19 +432,16 @@ def test_rmsnorm_output_beyond_f16_range_is_reported(gpu):
         w.release()
 
 
-@pytest.mark.parametrize("N,M", [(14336, 1), (1024, 64)], ids=["decode_gemv", "prefill_gemm"])
-def test_streamk_wait_runs_out_and_the_context_recovers(gpu, N, M):
+def test_streamk_wait_runs_out_and_the_context_recovers(gpu):
     """Failure detection on the GPU without a fault: with a 2 ms wait limit
     and the stream-K publishers told not to count themselves in, the CTA that
-    finishes a shared tile waits for counts that never come; its bounded
+    finishes a shared row tile waits for counts that never come; its bounded
     wait runs out, the kernel ends, and the next synchronization reports
     NXQ_ERR_TIMEOUT.  With the hook off and the limit back to default, the
     next ordinary call on the same stream is correct (the host cleared the
-    tile counters when it reported the timeout).  Decode: 112 row tiles x 16
-    chunks over the SMs; prefill: 8 row tiles x 16 chunks, one chunk per
-    CTA, each tile finished by one CTA for 15 publishers."""
+    tile counters when it reported the timeout)."""
     torch = _torch()
-    t, K = 12, 4096
+    t, N, K, M = 12, 14336, 4096, 1  # 112 row tiles x 16 chunks over 148 SMs: stream-K
     blocks = synth.make_blocks(t, N, K, seed=95)
     w = gpu.Weight.register(blocks, t, N, K)
     stream = torch.cuda.Stream()
