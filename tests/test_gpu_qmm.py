@@ -121,6 +121,51 @@ def test_host_call_output_buffers(gpu, M):
         w.release()
 
 
+def test_host_calls_from_several_threads(gpu):
+    """nxq_qmatmul_host from four threads at once (ctypes releases the GIL
+    around the call): each thread has its own stream and buffers inside the
+    library, so concurrent calls of different weights and batch sizes
+    (decode and prefill) all return their own correct results, repeatedly."""
+    import threading
+
+    t, K = 12, 2048
+    cases = [(1024, 1), (1536, 8), (512, 32), (1280, 64)]  # (N, M) per thread
+    weights, xs, wants = [], [], []
+    for i, (N, M) in enumerate(cases):
+        blocks = synth.make_blocks(t, N, K, seed=300 + i)
+        weights.append(gpu.Weight.register(blocks, t, N, K))
+        xs.append(synth.make_activations(M, K, seed=310 + i).astype(np.float32))
+        wants.append(loader.qmatmul(t, blocks, N, K, xs[-1]))
+    errors, results = [], [None] * len(cases)
+
+    def worker(i):
+        try:
+            out = np.empty_like(wants[i])
+            for _ in range(25):
+                out.fill(np.nan)
+                gpu.qmatmul_host(weights[i], xs[i], out=out)
+                if not synth.rel_l2(out, wants[i]) < TOL:
+                    raise AssertionError(f"thread {i}: rel-L2 {synth.rel_l2(out, wants[i])}")
+            results[i] = out.copy()
+        except Exception as e:  # reported by the main thread
+            errors.append(e)
+
+    try:
+        threads = [threading.Thread(target=worker, args=(i,)) for i in range(len(cases))]
+        for th in threads:
+            th.start()
+        for th in threads:
+            th.join(timeout=120)
+        assert not any(th.is_alive() for th in threads)
+        assert errors == []
+        # The same bits as a call from the main thread.
+        for i in range(len(cases)):
+            assert np.array_equal(results[i], gpu.qmatmul_host(weights[i], xs[i]))
+    finally:
+        for w in weights:
+            w.release()
+
+
 @pytest.mark.parametrize("t", ALL_TYPES, ids=lambda t: NAMES[t])
 @pytest.mark.parametrize("M", [1, 2, 3, 4, 7, 8, 16, 31, 32])
 def test_qmm_batch_sizes(gpu, t, M):
