@@ -283,6 +283,7 @@ const char* type_name(int type) {
 
 int context_sm_count() { return g_ctx.sm_count; }
 DeviceStatus* context_status() { return g_ctx.status; }
+int context_ready() { return check_ready(); }
 
 // Runs y = x W^T on `st` through the best kernel for (type, M, dtypes).
 int qmatmul_dispatch(const Weight* w, const void* x, int x_dtype, void* y, int y_dtype, int64_t M,

@@ -88,6 +88,9 @@ __device__ __forceinline__ void raise_range(DeviceStatus* st, unsigned where) {
 
 // The context's device status word and SM count (nxq_api.cu).
 DeviceStatus* context_status();
+// NXQ_OK once nxq_init has run, with the context's device made current on the
+// calling thread; else the status (and message) the C ABI returns.
+int context_ready();
 int context_sm_count();
 
 // Process-wide count of kernels launched by the library (nxq_launch_count).

@@ -56,6 +56,7 @@
 #include "qmm_mma.h"
 #include "sm100_ptx.cuh"
 #include "stream_scratch.h"
+#include "tp_p2p.h"
 
 namespace nxq {
 
@@ -485,6 +486,7 @@ struct MmaParams {
     DeviceStatus* status;
     float* part;    // C = 1, gran = 1: a partial-sum slot per CTA
     unsigned* cnt;  // ... and a counter per CTA (zero between launches)
+    TpExchange tp;  // tp.on: row-split tensor parallelism, partial tiles exchanged over peer memory
 };
 
 __device__ __forceinline__ void store_y(void* y, int dt, int64_t i, float v) {
@@ -527,7 +529,7 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
 // offsets of the kernel parameters.  Grouped launches need the lookup; single
 // ones use it too up to 16 tokens (measured 1-3 % faster there), but not at
 // 32 tokens, where it is 4 % slower (registers at the 96 cap).
-template <int TYPE, int MT, bool LOOKUP, bool PAIR = false>
+template <int TYPE, int MT, bool LOOKUP, bool PAIR = false, bool TPX = false>
 __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(const MmaParams p) {
     using Cf = Cfg<TYPE, MT, PAIR>;
     constexpr int S = Cf::S, WB = Cf::WB, XB = Cf::XB, NT = Cf::NT, PB = Cf::PB;
@@ -748,9 +750,33 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
         const int gi = warp >> 3, wg = warp & 7;
         const int r0 = 16 * wg + g;  // the fragment rows r0, r0 + 8 of a tile
         bool dead = false;
+        // Row-split tensor parallelism (single C = 1 launches): this rank's
+        // partial sums of a finished tile go to its slot in every rank's
+        // exchange buffer (remote stores over NVLink); the sum over ranks is
+        // taken after the tile loop.  The epoch is stable for the whole
+        // launch: the last CTA to finish advances it.
+        unsigned long long tp_e = 0ull;
+        if constexpr (TPX) tp_e = *reinterpret_cast<volatile unsigned long long*>(p.tp.ctl);
+        int tp_n = 0, tp_tiles[TPX ? kTpxCtaTiles : 1];
+        auto tp_slot = [&](int q, int src, int t) {
+            return p.tp.recv[q] + ((size_t)(tp_e & 1ull) * p.tp.world + src) * kTpxSlotFloats +
+                   (size_t)t * TILE_ROWS * RS;
+        };
         // Stores a tile's sums A (PAIR: gate; AU: up): y = A, or silu(A) * AU,
         // plus the residual.
         auto store_vals = [&](int t, const auto& A, const auto& AU) {
+            if constexpr (TPX) {
+                for (int q = 0; q < p.tp.world; ++q) {
+                    float* sl = tp_slot(q, p.tp.rank, t);
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        *reinterpret_cast<float2*>(sl + r0 * RS + 8 * nt + 2 * tq) = make_float2(A[nt][0], A[nt][1]);
+                        *reinterpret_cast<float2*>(sl + (r0 + 8) * RS + 8 * nt + 2 * tq) = make_float2(A[nt][2], A[nt][3]);
+                    }
+                }
+                if (tp_n < kTpxCtaTiles) tp_tiles[tp_n++] = t;
+                return;
+            }
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -975,9 +1001,81 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
                 }
             }
         }
+        if (TPX && gi == 0) {
+            // ---- the exchange: group 0 held every tile this CTA finished.
+            // Each thread's partials (local and remote stores) are made visible
+            // system-wide before thread 0 raises this rank's flag for each of
+            // those tiles in every peer; threads 0 .. world-1 then wait
+            // (bounded) for the peers' flags of the same tiles, and the group
+            // adds the slots in rank order (the same bits on every rank). ----
+            __threadfence_system();
+            named_sync(4, kThreads);
+            const unsigned long long want = tp_e + 1ull;
+            if (tid == 0 && !s_abort)
+                for (int i = 0; i < tp_n; ++i)
+                    for (int q = 0; q < p.tp.world; ++q)
+                        if (q != p.tp.rank)
+                            asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(
+                                             p.tp.flags[q] + (size_t)p.tp.rank * kTpxMaxTiles + tp_tiles[i]),
+                                         "l"(want)
+                                         : "memory");
+            if (tid < p.tp.world && tid != p.tp.rank && !s_abort) {
+                const long long w0 = clock64(), lim = ptx::wait_limit(p.status);
+                for (int i = 0; i < tp_n && !*ctl.abort; ++i) {
+                    const unsigned long long* f = p.tp.flags[p.tp.rank] + (size_t)tid * kTpxMaxTiles + tp_tiles[i];
+                    for (;;) {
+                        unsigned long long v;
+                        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(f) : "memory");
+                        if (v >= want) break;
+                        if (*ctl.abort || clock64() - w0 > lim) {
+                            if (!*ctl.abort) ptx::raise_timeout(ctl, 35);
+                            break;
+                        }
+                        __nanosleep(64);
+                    }
+                }
+            }
+            named_sync(4, kThreads);
+            if (!s_abort)
+                for (int i = 0; i < tp_n; ++i) {
+                    const int t = tp_tiles[i];
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        float2 a = make_float2(0.0f, 0.0f), b = make_float2(0.0f, 0.0f);
+                        for (int src = 0; src < p.tp.world; ++src) {
+                            const float* sl = tp_slot(p.tp.rank, src, t);
+                            const float2 x0 = __ldcg(reinterpret_cast<const float2*>(sl + r0 * RS + 8 * nt + 2 * tq));
+                            const float2 x1 = __ldcg(reinterpret_cast<const float2*>(sl + (r0 + 8) * RS + 8 * nt + 2 * tq));
+                            a.x += x0.x;
+                            a.y += x0.y;
+                            b.x += x1.x;
+                            b.y += x1.y;
+                        }
+                        const float v[4] = {a.x, a.y, b.x, b.y};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int tok = 8 * nt + 2 * tq + (e & 1);
+                            const int64_t row = (int64_t)t * TILE_ROWS + r0 + 8 * (e >> 1);
+                            if (tok < M && row < N) store_y(I.y, p.y_dtype, tok * N + row, v[e]);
+                        }
+                    }
+                }
+        }
     }
 
     __syncthreads();
+    if (TPX && tid == 0) {
+        // The last CTA of the launch advances the exchange epoch (every CTA
+        // read it at its start).
+        __threadfence();
+        unsigned int* done = reinterpret_cast<unsigned int*>(p.tp.ctl + 1);
+        if (atomicAdd(done, 1u) == gridDim.x - 1) {
+            *reinterpret_cast<volatile unsigned int*>(done) = 0u;
+            __threadfence();
+            volatile unsigned long long* ep = reinterpret_cast<volatile unsigned long long*>(p.tp.ctl);
+            *ep = *ep + 1ull;  // no other CTA writes it during the launch
+        }
+    }
     if (s_abort) {
         // Let the copies still in flight land (bounded) before the CTA's shared
         // memory goes away: only the last S tile-chunks issued can be pending.
@@ -1015,6 +1113,9 @@ int set_attr() {
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(mma_gemv_kernel<TYPE, MT, false, true>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg<TYPE, MT, true>::smem);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(mma_gemv_kernel<TYPE, MT, false, false, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cf::smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute (mma_gemv)");
     int* mq = max_clusters<TYPE, MT>();
     mq[0] = g_sm_count;
@@ -1136,10 +1237,18 @@ int pick_split(const HostItem* it, int n, const int* maxq, int cmax, int sk_marg
     return cl;
 }
 
+// tp: row-split tensor parallelism with the partial tiles exchanged over peer
+// memory inside the launch (one item, no pairing, no residual); the split is
+// then C = 1 only, and a CTA may finish at most kTpxCtaTiles tiles.
 template <int TYPE, int MT, bool PAIR = false>
-int launch(const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st) {
+int launch(const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st, const TpExchange* tp = nullptr) {
     using Cf = Cfg<TYPE, MT, PAIR>;
     MmaParams p;
+    p.tp = TpExchange{};
+    if (tp) {
+        if (PAIR || n != 1 || it[0].res || it[0].w->shape.tiles > kTpxMaxTiles) return NXQ_ERR_UNSUPPORTED;
+        p.tp = *tp;
+    }
     for (int i = 0; i < n; ++i)
         if (it[i].w->shape.tile_chunk_bytes != Cf::WB)
             return fail(NXQ_ERR_SHAPE, "mma_gemv: tile-chunk of %lld bytes, kernel stage %d",
@@ -1156,7 +1265,14 @@ int launch(const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st)
     // Measured (Q4_K, Q3_K, 4096 - 16384 rows): stream-K pays when it takes
     // more than 2 units off the busiest CTA at 8 tokens, 1 at 16, any at 32.
     const int margin = sc == nullptr ? -1 : MT == 8 ? 2 : MT == 16 ? 1 : 0;
-    const int clusters = pick_split(it, n, max_clusters<TYPE, MT>(), Cf::CMAX, margin, &p);
+    const int clusters = pick_split(it, n, max_clusters<TYPE, MT>(), tp ? 1 : Cf::CMAX, margin, &p);
+    if (tp) {
+        const MmaItem& m = p.it[0];
+        const int kun = m.chunks;
+        const int run = m.ub + (m.ur ? 1 : 0);  // tiles (whole-tile split) or units (stream-K) per CTA
+        const int held = m.gran == kun ? run : (run + kun - 1) / kun + 1;
+        if (p.C != 1 || held > kTpxCtaTiles) return NXQ_ERR_UNSUPPORTED;
+    }
     p.part = sc ? sc->ws : nullptr;
     p.cnt = sc ? sc->counters : nullptr;
     p.x_dtype = x_dtype;
@@ -1178,7 +1294,8 @@ int launch(const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st)
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = p.C > 1 ? 2 : 1;
-    cudaError_t e = PAIR                    ? cudaLaunchKernelEx(&cfg, mma_gemv_kernel<TYPE, MT, false, true>, p)
+    cudaError_t e = PAIR ? cudaLaunchKernelEx(&cfg, mma_gemv_kernel<TYPE, MT, false, true>, p)
+                    : tp ? cudaLaunchKernelEx(&cfg, mma_gemv_kernel<TYPE, MT, false, false, true>, p)
                     : (n == 1 && MT == 32) ? cudaLaunchKernelEx(&cfg, mma_gemv_kernel<TYPE, MT, false>, p)
                                            : cudaLaunchKernelEx(&cfg, mma_gemv_kernel<TYPE, MT, true>, p);
     note_launches(1);
@@ -1192,7 +1309,8 @@ bool type_ok(int type) {
            type == T_Q5_K || type == T_Q4_1 || type == T_Q2_K || is_i4g(type) || type == T_NXF_I8;
 }
 
-int launch_items(int type, int mt, const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st) {
+int launch_items(int type, int mt, const HostItem* it, int n, int x_dtype, int y_dtype, cudaStream_t st,
+                 const TpExchange* tp = nullptr) {
     const bool pair = n == 1 && it[0].w_up;
 #define NXQ_CASE(T)                                                                                   \
     case T:                                                                                           \
@@ -1200,9 +1318,9 @@ int launch_items(int type, int mt, const HostItem* it, int n, int x_dtype, int y
             return mt == 8    ? launch<T, 8, true>(it, n, x_dtype, y_dtype, st)                       \
                    : mt == 16 ? launch<T, 16, true>(it, n, x_dtype, y_dtype, st)                      \
                               : launch<T, 32, true>(it, n, x_dtype, y_dtype, st);                     \
-        return mt == 8    ? launch<T, 8>(it, n, x_dtype, y_dtype, st)                                 \
-               : mt == 16 ? launch<T, 16>(it, n, x_dtype, y_dtype, st)                                \
-                          : launch<T, 32>(it, n, x_dtype, y_dtype, st);
+        return mt == 8    ? launch<T, 8>(it, n, x_dtype, y_dtype, st, tp)                             \
+               : mt == 16 ? launch<T, 16>(it, n, x_dtype, y_dtype, st, tp)                            \
+                          : launch<T, 32>(it, n, x_dtype, y_dtype, st, tp);
     switch (type) {
         NXQ_CASE(T_Q4_K)
         NXQ_CASE(T_Q4_0)
@@ -1283,6 +1401,28 @@ int mma_qmatmul(const Weight* w, const void* x, int x_dtype, void* y, int y_dtyp
     HostItem item{w, xh, y, M};
     item.res = res;
     return launch_items(s.type, mt, &item, 1, xdt, y_dtype, st);
+}
+
+int mma_qmatmul_tp(const Weight* w, const void* x, int x_dtype, float* y, int64_t M, cudaStream_t st,
+                   const TpExchange& tp) {
+    const TiledShape& s = w->shape;
+    if (!mma_supported(s, M) || !tp.on) return NXQ_ERR_UNSUPPORTED;
+    const int mt = M <= 8 ? 8 : M <= 16 ? 16 : 32;
+    const bool aligned = ((uintptr_t)x % 16) == 0;
+    const bool direct = aligned && (x_dtype == NXQ_F16 || (M <= 2 && (x_dtype == NXQ_F32 || x_dtype == NXQ_BF16)));
+    const void* xh = x;
+    int xdt = x_dtype;
+    if (!direct) {
+        StreamScratch* sc = nullptr;
+        int rc = scratch_for(st, 0, 0, (size_t)(M * s.K), &sc);
+        if (rc) return rc;
+        cudaError_t e = launch_to_half(x, x_dtype, sc->xh, M * s.K, st);
+        if (e != cudaSuccess) return cuda_fail(e, "to_half launch");
+        xh = sc->xh;
+        xdt = NXQ_F16;
+    }
+    HostItem item{w, xh, y, M};
+    return launch_items(s.type, mt, &item, 1, xdt, NXQ_F32, st, &tp);
 }
 
 int mma_qmatmul_swiglu(const Weight* wg, const Weight* wu, const void* x, int x_dtype, void* h, int h_dtype,

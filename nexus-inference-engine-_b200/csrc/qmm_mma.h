@@ -26,5 +26,13 @@ int mma_qmatmul_swiglu(const Weight* wg, const Weight* wu, const void* x, int x_
 // and activations the kernel reads as they are.
 int mma_qmatmul_grouped(const Weight* const* w, int n, const void* const* x, int x_dtype, void* const* y,
                         int y_dtype, const int64_t* M, cudaStream_t st);
+// Row-split tensor parallelism in one launch: y (fp32 [M][N], every rank) =
+// the sum over ranks of x_r W_r^T, each rank's partial tiles pushed into the
+// others' exchange buffers over peer memory as they finish (tp_p2p.h).
+// NXQ_ERR_UNSUPPORTED (the caller then multiplies and allreduces) when the
+// shape or the split does not fit the exchange.
+struct TpExchange;
+int mma_qmatmul_tp(const Weight* w, const void* x, int x_dtype, float* y, int64_t M, cudaStream_t st,
+                   const TpExchange& tp);
 
 }  // namespace nxq

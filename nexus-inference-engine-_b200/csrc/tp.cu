@@ -31,6 +31,7 @@
 #include <vector>
 
 #include "nxq_internal.h"
+#include "qmm_mma.h"
 #include "tp_p2p.h"
 
 namespace nxq {
@@ -65,14 +66,30 @@ std::atomic<bool> g_hook_stream_pending{false};  // NXQ_HOOK_TP_STREAM_PENDING
 
 // The peer-memory allreduce (tp_p2p.cu): this rank's symmetric buffer, the
 // peers' buffers mapped through CUDA IPC, and the launch parameters.
-struct P2PState {
-    bool on = false;
+// A device buffer on every rank, mapped into every other rank through CUDA
+// IPC (handles exchanged once through the communicator): `at[q]` addresses
+// rank q's buffer from this rank (the own one locally).
+struct SymBuf {
     void* base = nullptr;
     void* peer[kP2PMaxWorld] = {};
+    void* at[kP2PMaxWorld] = {};
+};
+
+struct P2PState {
+    bool on = false;
+    SymBuf buf;
     P2PParams tmpl{};
 };
 P2PState g_p2p;
 constexpr int64_t kP2PCap = 1 << 21;  // floats per data half: allreduces up to 8 MB use peer memory
+
+// The fused row split: the decode GEMV exchanges partial tiles itself.
+struct TpxState {
+    bool on = false;
+    SymBuf buf;
+    TpExchange tmpl{};
+};
+TpxState g_tpx;
 
 int load_nccl() {
     if (g_nccl.lib) return NXQ_OK;
@@ -130,101 +147,128 @@ int check_comm() {
     return NXQ_OK;
 }
 
-void p2p_teardown() {
+void sym_unmap(SymBuf* sb) {
     for (int r = 0; r < kP2PMaxWorld; ++r)
-        if (g_p2p.peer[r]) cudaIpcCloseMemHandle(g_p2p.peer[r]);
-    if (g_p2p.base) cudaFree(g_p2p.base);
-    g_p2p = P2PState{};
+        if (sb->peer[r]) cudaIpcCloseMemHandle(sb->peer[r]);
+    if (sb->base) cudaFree(sb->base);
+    *sb = SymBuf{};
 }
 
-// Maps every rank's symmetric buffer (caller holds g_tp_mu, communicator
-// up) when NXQ_TP_ALLREDUCE=p2p asks for the peer-memory allreduce.  It is
+// Every rank's element is 1 after a ncclMin over ranks of `mine` (1 = ok).
+bool all_ranks_ok(bool mine) {
+    uint8_t* d = nullptr;
+    uint8_t v = mine ? 1 : 0, all = 0;
+    if (cudaMalloc(&d, 1) != cudaSuccess) {
+        cudaGetLastError();
+        return false;  // in practice every rank fails the same tiny allocation
+    }
+    cudaMemcpy(d, &v, 1, cudaMemcpyHostToDevice);
+    if (g_nccl.AllReduce(d, d, 1, ncclUint8, ncclMin, g_comm, 0) == ncclSuccess && cudaStreamSynchronize(0) == cudaSuccess)
+        cudaMemcpy(&all, d, 1, cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    return all == 1;
+}
+
+// Allocates `bytes` (zeroed) on every rank and maps every peer's buffer;
+// collective over the communicator (caller holds g_tp_mu).  Either every rank
+// succeeds or none keeps anything.
+bool sym_map(size_t bytes, SymBuf* sb) {
+    *sb = SymBuf{};
+    bool ok = cudaMalloc(&sb->base, bytes) == cudaSuccess && cudaMemset(sb->base, 0, bytes) == cudaSuccess &&
+              cudaDeviceSynchronize() == cudaSuccess;
+    cudaIpcMemHandle_t mine{};
+    ok = ok && cudaIpcGetMemHandle(&mine, sb->base) == cudaSuccess;
+    // Every rank takes part in the exchange, whatever happened above (a rank
+    // that failed sends a zero handle and all of them then give up).
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    uint8_t* dh = nullptr;
+    if (cudaMalloc(&dh, (size_t)g_world * hb) != cudaSuccess) {
+        cudaGetLastError();
+        sym_unmap(sb);
+        return false;
+    }
+    cudaMemcpy(dh + (size_t)g_rank * hb, &mine, hb, cudaMemcpyHostToDevice);
+    std::vector<cudaIpcMemHandle_t> hs((size_t)g_world);
+    bool got = g_nccl.AllGather(dh + (size_t)g_rank * hb, dh, hb, ncclUint8, g_comm, 0) == ncclSuccess &&
+               cudaStreamSynchronize(0) == cudaSuccess &&
+               cudaMemcpy(hs.data(), dh, g_world * hb, cudaMemcpyDeviceToHost) == cudaSuccess;
+    cudaFree(dh);
+    if (!all_ranks_ok(ok && got)) {
+        cudaGetLastError();
+        sym_unmap(sb);
+        return false;
+    }
+    for (int q = 0; q < g_world && ok; ++q) {
+        if (q == g_rank) {
+            sb->at[q] = sb->base;
+            continue;
+        }
+        ok = cudaIpcOpenMemHandle(&sb->peer[q], hs[q], cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+        sb->at[q] = sb->peer[q];
+    }
+    // Whether every rank could map every peer decides for all of them.
+    if (!all_ranks_ok(ok)) {
+        cudaGetLastError();
+        sym_unmap(sb);
+        return false;
+    }
+    return true;
+}
+
+// The peer-memory allreduce, when NXQ_TP_ALLREDUCE=p2p asks for it.  It is
 // not the default: on two B200 it took 16-19 us per call for 16 KB - 2 MB
 // against NCCL's 12 us (measured in a CUDA graph of the benchmark's calls).
 // Any failure leaves it off; the allreduce then runs on NCCL.
 void p2p_setup() {
-    const char* env = getenv("NXQ_TP_ALLREDUCE");
-    if (g_world < 2 || g_world > kP2PMaxWorld || !(env && strcmp(env, "p2p") == 0)) return;
-    int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess) {
-        cudaGetLastError();
-        return;
-    }
-    const size_t bytes = p2p_bytes(g_world, kP2PCap);
-    bool ok = cudaMalloc(&g_p2p.base, bytes) == cudaSuccess && cudaMemset(g_p2p.base, 0, bytes) == cudaSuccess;
-    cudaIpcMemHandle_t mine{};
-    ok = ok && cudaIpcGetMemHandle(&mine, g_p2p.base) == cudaSuccess;
-    // Every rank takes part in the exchange, whatever happened above (a rank
-    // that failed sends a zero handle and all of them then keep NCCL).
-    const size_t hb = sizeof(cudaIpcMemHandle_t);
-    uint8_t* dh = nullptr;
-    if (cudaMalloc(&dh, (g_world + 1) * hb) != cudaSuccess) {
-        cudaGetLastError();
-        p2p_teardown();
-        return;  // no exchange possible: all ranks fail the same allocation in practice
-    }
-    uint8_t flag = ok ? 1 : 0;
-    cudaMemcpy(dh + (size_t)g_rank * hb, &mine, hb, cudaMemcpyHostToDevice);
-    cudaMemcpy(dh + (size_t)g_world * hb, &flag, 1, cudaMemcpyHostToDevice);
-    ncclResult_t r = g_nccl.AllGather(dh + (size_t)g_rank * hb, dh, hb, ncclUint8, g_comm, 0);
-    if (r == ncclSuccess) r = g_nccl.AllReduce(dh + (size_t)g_world * hb, dh + (size_t)g_world * hb, 1, ncclUint8, ncclMin, g_comm, 0);
-    std::vector<cudaIpcMemHandle_t> hs((size_t)g_world);
-    uint8_t all_ok = 0;
-    if (r == ncclSuccess && cudaStreamSynchronize(0) == cudaSuccess) {
-        cudaMemcpy(hs.data(), dh, g_world * hb, cudaMemcpyDeviceToHost);
-        cudaMemcpy(&all_ok, dh + (size_t)g_world * hb, 1, cudaMemcpyDeviceToHost);
-    }
-    cudaFree(dh);
-    if (!all_ok) {
-        cudaGetLastError();
-        p2p_teardown();
-        return;
-    }
+    if (!sym_map(p2p_bytes(g_world, kP2PCap), &g_p2p.buf)) return;
     P2PParams& t = g_p2p.tmpl;
     t.rank = g_rank;
     t.world = g_world;
     t.cap = kP2PCap;
-    for (int q = 0; q < g_world && ok; ++q) {
-        void* ptr = g_p2p.base;
-        if (q != g_rank) {
-            ok = cudaIpcOpenMemHandle(&g_p2p.peer[q], hs[q], cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
-            ptr = g_p2p.peer[q];
-        }
-        t.data[q] = static_cast<float*>(ptr);
-        t.flags[q] = reinterpret_cast<unsigned long long*>(static_cast<char*>(ptr) + 2 * kP2PCap * sizeof(float));
-    }
-    // Whether every rank could map every peer decides for all of them.
-    uint8_t* dflag = nullptr;
-    flag = ok ? 1 : 0;
-    all_ok = 0;
-    if (cudaMalloc(&dflag, 1) == cudaSuccess) {
-        cudaMemcpy(dflag, &flag, 1, cudaMemcpyHostToDevice);
-        if (g_nccl.AllReduce(dflag, dflag, 1, ncclUint8, ncclMin, g_comm, 0) == ncclSuccess &&
-            cudaStreamSynchronize(0) == cudaSuccess)
-            cudaMemcpy(&all_ok, dflag, 1, cudaMemcpyDeviceToHost);
-        cudaFree(dflag);
-    }
-    if (!all_ok) {
-        cudaGetLastError();
-        p2p_teardown();
-        return;
+    for (int q = 0; q < g_world; ++q) {
+        t.data[q] = static_cast<float*>(g_p2p.buf.at[q]);
+        t.flags[q] = reinterpret_cast<unsigned long long*>(static_cast<char*>(g_p2p.buf.at[q]) +
+                                                           2 * kP2PCap * sizeof(float));
     }
     t.ctl = t.flags[g_rank] + (size_t)g_world * kP2PBlocks;
     g_p2p.on = true;
 }
 
-// All ranks' queued work is done before any rank unmaps or frees its buffer
-// (a peer's kernel may still read it): a device synchronize and a one-byte
-// NCCL allreduce as a barrier.
-void p2p_shutdown() {
-    if (!g_p2p.base) return;
-    cudaDeviceSynchronize();
-    uint8_t* d = nullptr;
-    if (!g_dead && cudaMalloc(&d, 1) == cudaSuccess) {
-        if (g_nccl.AllReduce(d, d, 1, ncclUint8, ncclMin, g_comm, 0) == ncclSuccess) cudaStreamSynchronize(0);
-        cudaFree(d);
+// The fused row split (NXQ_TP_ALLREDUCE=fused): decode-size row-split calls
+// exchange their partial tiles inside the GEMV launch; other calls use NCCL.
+void tpx_setup() {
+    if (!sym_map(tpx_bytes(g_world), &g_tpx.buf)) return;
+    TpExchange& t = g_tpx.tmpl;
+    t.on = 1;
+    t.rank = g_rank;
+    t.world = g_world;
+    const size_t recv_bytes = (size_t)2 * g_world * kTpxSlotFloats * sizeof(float);
+    for (int q = 0; q < g_world; ++q) {
+        t.recv[q] = static_cast<float*>(g_tpx.buf.at[q]);
+        t.flags[q] = reinterpret_cast<unsigned long long*>(static_cast<char*>(g_tpx.buf.at[q]) + recv_bytes);
     }
-    p2p_teardown();
+    t.ctl = t.flags[g_rank] + (size_t)g_world * kTpxMaxTiles;
+    g_tpx.on = true;
+}
+
+void peer_setup() {
+    const char* env = getenv("NXQ_TP_ALLREDUCE");
+    if (g_world < 2 || g_world > kP2PMaxWorld || !env) return;
+    if (strcmp(env, "p2p") == 0) p2p_setup();
+    if (strcmp(env, "fused") == 0) tpx_setup();
+}
+
+// All ranks' queued work is done before any rank unmaps or frees its buffers
+// (a peer's kernel may still read or write them): a device synchronize and a
+// one-byte NCCL allreduce as a barrier.
+void peer_shutdown() {
+    if (!g_p2p.buf.base && !g_tpx.buf.base) return;
+    cudaDeviceSynchronize();
+    if (!g_dead) all_ranks_ok(true);
+    sym_unmap(&g_p2p.buf);
+    sym_unmap(&g_tpx.buf);
+    g_p2p = P2PState{};
+    g_tpx = TpxState{};
 }
 
 int check_weight_ptr(nxq_weight_t h, const Weight** out) {
@@ -270,21 +314,21 @@ NXQ_API int nxq_tp_init(int rank, int world, const void* unique_id, size_t n) {
     g_world = world;
     g_dead = false;
     g_dead_why[0] = 0;
-    p2p_setup();
+    peer_setup();
     return NXQ_OK;
 }
 
 NXQ_API int nxq_tp_p2p_enabled(int* on) {
     if (!on) return fail(NXQ_ERR_ARG, "null argument");
     std::lock_guard<std::mutex> lk(g_tp_mu);
-    *on = g_p2p.on ? 1 : 0;
+    *on = g_p2p.on ? 1 : g_tpx.on ? 2 : 0;
     return NXQ_OK;
 }
 
 NXQ_API int nxq_tp_shutdown(void) {
     std::lock_guard<std::mutex> lk(g_tp_mu);
     if (!g_comm) return NXQ_OK;
-    p2p_shutdown();
+    peer_shutdown();
     ncclResult_t r = ncclSuccess;
     if (!g_dead) {
         ncclResult_t async_err = ncclSuccess;
@@ -371,6 +415,12 @@ NXQ_API int nxq_tp_qmatmul(nxq_weight_t shard, const void* x_dev, int x_dtype, v
     }
     if (split == NXQ_SPLIT_ROW && y_dtype != NXQ_F32)
         return fail(NXQ_ERR_ARG, "ROW split produces fp32 partial sums; y_dtype must be NXQ_F32");
+    if (split == NXQ_SPLIT_ROW && g_tpx.on && M > 0 && x_dev && y_dev &&
+        (x_dtype == NXQ_F32 || x_dtype == NXQ_F16 || x_dtype == NXQ_BF16)) {
+        if ((rc = context_ready())) return rc;
+        rc = mma_qmatmul_tp(w, x_dev, x_dtype, static_cast<float*>(y_dev), M, (cudaStream_t)stream, g_tpx.tmpl);
+        if (rc != NXQ_ERR_UNSUPPORTED) return rc;
+    }
     rc = nxq_qmatmul(shard, x_dev, x_dtype, y_dev, y_dtype, M, stream);
     if (rc || split == NXQ_SPLIT_COL) return rc;
     return nxq_tp_allreduce_f32((float*)y_dev, M * w->shape.N, stream);

@@ -705,11 +705,13 @@ def tp_qmatmul(shard: Weight, x, out, split: int, stream=None):
     return out
 
 
-def tp_p2p_enabled() -> bool:
-    """Whether allreduces up to 8 MB run over NVLink peer memory (else NCCL)."""
+def tp_p2p_enabled() -> int:
+    """Peer-memory path of this rank: 1 = allreduces up to 8 MB over NVLink
+    peer memory, 2 = decode row-split calls fused with their reduction, 0 =
+    NCCL only (NXQ_TP_ALLREDUCE at nxq_tp_init)."""
     v = ctypes.c_int()
     _check(lib().nxq_tp_p2p_enabled(ctypes.byref(v)))
-    return bool(v.value)
+    return v.value
 
 
 def tp_wait(stream=None, timeout_ms: int = 10000) -> None:

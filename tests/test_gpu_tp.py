@@ -230,3 +230,127 @@ def test_tp_allreduce_peer_memory_two_gpus():
     for key in out[0]:
         if key != "p2p" and key[0] != "graph":
             assert out[0][key][2] == out[1][key][2], key  # every rank holds the same sum
+
+
+def _fused_worker(rank, world, port, cases, q):
+    sys.path.insert(0, str(ROOT))
+    sys.path.insert(0, str(ROOT / "nexus-inference-engine-_b200"))
+    import datetime
+    import hashlib
+
+    import torch
+    import torch.distributed as dist
+
+    import nxq
+    from nxq import synth
+    from oracle import loader
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    joined = False
+    try:
+        os.environ["NXQ_TP_ALLREDUCE"] = "fused"
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        nxq.init(rank)
+        uid = [nxq.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        nxq.tp_init(rank, world, uid[0])
+        joined = True
+        res = {"mode": nxq.tp_p2p_enabled()}
+        digest = lambda a: hashlib.sha256(a.tobytes()).hexdigest()
+        for t, N, K, Ms in cases:
+            blocks = synth.make_blocks(t, N, K, seed=400 + t)
+            k_loc = K // world
+            w = nxq.Weight.register_shard(blocks, t, N, K, nxq.SPLIT_ROW, rank, world)
+            for M in Ms:
+                xh = torch.from_numpy(synth.make_activations(M, K, seed=410 + M).astype(np.float32)).half()
+                full = loader.qmatmul(t, blocks, N, K, xh.float().numpy(), nthreads=4)
+                xs = xh[:, rank * k_loc:(rank + 1) * k_loc].contiguous().to(dev)
+                outs = []
+                for call in range(3):  # both halves of the exchange buffer, advancing epochs
+                    y = torch.full((M, N), float("nan"), dtype=torch.float32, device=dev)
+                    nxq.tp_qmatmul(w, xs, y, nxq.SPLIT_ROW)
+                    nxq.tp_wait(None, 20000)
+                    outs.append(y.cpu().numpy())
+                res[(t, N, K, M)] = (synth.rel_l2(outs[0], full),
+                                     all(np.array_equal(o, outs[0]) for o in outs), digest(outs[0]))
+            if Ms[0] <= 32:
+                # Two calls captured in a CUDA graph, replayed twice: the epoch
+                # is a device counter, so replays keep exchanging correctly.
+                M = Ms[0]
+                xh = torch.from_numpy(synth.make_activations(M, K, seed=410 + M).astype(np.float32)).half()
+                xs = xh[:, rank * k_loc:(rank + 1) * k_loc].contiguous().to(dev)
+                s = torch.cuda.Stream()
+                ys = [torch.empty(M, N, dtype=torch.float32, device=dev) for _ in range(2)]
+                with torch.cuda.stream(s):
+                    nxq.tp_qmatmul(w, xs, ys[0], nxq.SPLIT_ROW, stream=s)  # outside capture first
+                s.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s):
+                    for yy in ys:
+                        nxq.tp_qmatmul(w, xs, yy, nxq.SPLIT_ROW, stream=s)
+                eager = None
+                for rep in range(2):
+                    for yy in ys:
+                        yy.fill_(float("nan"))
+                    with torch.cuda.stream(s):
+                        g.replay()
+                    s.synchronize()
+                    got = [yy.cpu().numpy() for yy in ys]
+                    eager = eager if eager is not None else got[0]
+                    res[("graph", t, N, K, rep)] = all(np.array_equal(a, eager) for a in got)
+                del g
+                nxq.stream_sync(s)
+            w.release()
+        q.put((rank, res))
+    finally:
+        if joined:
+            nxq.tp_shutdown()
+        dist.destroy_process_group()
+
+
+def test_tp_row_split_fused_exchange_two_gpus():
+    """NXQ_TP_ALLREDUCE=fused on two GPUs: decode-size ROW calls run as one
+    GEMV launch per rank that pushes its partial tiles into the peer's
+    exchange buffer over NVLink and sums the ranks' tiles itself.  Within the
+    parity bar of the unsharded oracle (Q4_K and Q3_K; a shape with few row
+    tiles and a long K, so stream-K splits tiles across CTAs), the same bits
+    on both ranks, the same bits on three consecutive calls and on CUDA-graph
+    replays; a prefill-size call (M = 40) takes the GEMM and NCCL path."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    world = 2
+    cases = [(12, 1024, 4096, (1, 8, 32)), (11, 4096, 14336, (1, 8, 32)), (12, 14336, 4096, (8,)),
+             (12, 1024, 4096, (40,))]
+    procs = [ctx.Process(target=_fused_worker, args=(r, world, port, cases, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        for p in procs:
+            p.join(300)
+            assert p.exitcode == 0
+    finally:
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+    out = dict(q.get(timeout=5) for _ in range(world))
+    for rank in range(world):
+        assert out[rank]["mode"] == 2, "fused row split not enabled on two NVLink GPUs"
+        for key, val in out[rank].items():
+            if key == "mode":
+                continue
+            if key[0] == "graph":
+                assert val, (rank, key)
+                continue
+            err, repeat, _ = val
+            assert err < TOL and repeat, (rank, key, err, repeat)
+    for key, val in out[0].items():
+        if key != "mode" and key[0] != "graph":
+            assert val[2] == out[1][key][2], key  # every rank holds the same bits
