@@ -13,10 +13,11 @@ weight replica and the replicas of a projection span more than 4x the
 126 MB L2, so each call streams its weights from HBM.
 
 N = 1: the step on one GPU.  N > 1 (torchrun, one process per GPU): the same
-step split tensor-parallel over the N GPUs - gate/up by column, down by row
-with the library's NCCL allreduce of the partial outputs - so the whole job
-is fixed as N grows (strong scaling); the matmul and allreduce times of the
-step are also reported on their own (tp_split).
+step split tensor-parallel over the N GPUs - gate/up by column, down by row,
+its partial outputs summed over the ranks inside the GEMV launch (tiles
+exchanged over NVLink peer memory) - so the whole job is fixed as N grows
+(strong scaling); the matmuls alone and NCCL allreduces of the same sizes are
+also timed on their own (tp_split).
 
 value      = algorithmic bytes of the whole step (packed weight blocks + x + y)
              times K steps over the device time of the K timed steps (CUDA
@@ -515,12 +516,14 @@ def bench_tp_layer(dev, stream, pk, rank: int, world: int) -> dict:
     (hidden 16384, FFN 53248, 128 query / 8 KV heads of dim 128), decode M in
     {1, 8, 32}, tensor-parallel over the `world` ranks: q/k/v/gate/up split by
     column (each rank holds N/world rows), o/down split by row (K/world of every
-    row) and summed with the library's NCCL allreduce.  Each rank generates its
-    own shard (synthetic data of the config's distribution).  The timed step is
-    the layer's 7 matmuls + 2 allreduces (attention and SwiGLU are not part of
-    the path), captured in one CUDA graph; time = max over ranks.  The 7
-    matmuls alone and the 2 allreduces alone are timed the same way.  Keys are
-    flat (M<m>_...) so that records keep them."""
+    row) and summed over the ranks by the library (at decode sizes inside the
+    GEMV launch, tiles exchanged over NVLink; NXQ_TP_ALLREDUCE=nccl: an NCCL
+    allreduce).  Each rank generates its own shard (synthetic data of the
+    config's distribution).  The timed step is the layer's 7 row/column-split
+    matmuls (attention and SwiGLU are not part of the path), captured in one
+    CUDA graph; time = max over ranks.  The 7 matmuls alone and 2 NCCL
+    allreduces of the row splits' outputs alone are timed the same way.  Keys
+    are flat (M<m>_...) so that records keep them."""
     import torch
 
     import nxq
@@ -830,6 +833,7 @@ def headline_tp(args, dev, stream, pk, rank: int, world: int) -> dict:
     uid = [nxq.tp_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(uid, src=0)
     nxq.tp_init(rank, world, uid[0])
+    tp_mode = nxq.tp_p2p_enabled()
     # name, K, N, split; the shard's local K and N.
     proj = [(name, K, N, nxq.SPLIT_ROW if name == "down" else nxq.SPLIT_COL) for name, K, N in PROJ]
     loc = {name: ((K, N // world) if sp == nxq.SPLIT_COL else (K // world, N)) for name, K, N, sp in proj}
@@ -946,11 +950,22 @@ def headline_tp(args, dev, stream, pk, rank: int, world: int) -> dict:
             "tp_split": {"matmul_us_per_step": round(ms_mm / args.steps * 1e3, 2),
                          "allreduce_us_per_step": round(ms_ar / args.steps * 1e3, 2),
                          "step_us": round(ms / args.steps * 1e3, 2), "allreduces_per_step": len(GEMV_MS),
-                         "allreduce_bytes": [M * 4096 * 4 for M in GEMV_MS]},
+                         "allreduce_bytes": [M * 4096 * 4 for M in GEMV_MS],
+                         "row_reduction": tp_mode_name(tp_mode),
+                         "reduction_us_per_step": round((ms - ms_mm) / args.steps * 1e3, 2),
+                         "how": "matmul_us: the step's matmuls alone; allreduce_us: NCCL allreduces of the "
+                                "down outputs alone; reduction_us = step_us - matmul_us, the cost of the "
+                                "row_reduction the step used"},
             "l2": f"inputs larger than L2: {reps} replicas of each shard per rank; every call of a step reads its "
                   f"own replica",
-            "parallelism": f"tp{world}: gate/up column split, down row split + NCCL allreduce (fp32)",
+            "parallelism": f"tp{world}: gate/up column split, down row split summed by "
+                           f"{tp_mode_name(tp_mode)} (fp32)",
             "scaling": "strong"}
+
+
+def tp_mode_name(mode: int) -> str:
+    return {0: "NCCL allreduce", 1: "peer-memory allreduce",
+            2: "the fused GEMV tile exchange over NVLink (NCCL allreduce for prefill sizes)"}.get(mode, str(mode))
 
 
 def run_gpu_arm(args, rank, world, local):

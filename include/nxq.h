@@ -329,15 +329,17 @@ NXQ_API int nxq_tp_shutdown(void);
  *   ROW: x_dev is this rank's [M][K/T] slice; y_dev receives the full [M][N]
  *        sum over ranks (in-place NCCL allreduce of the fp32 partials).
  * y_dtype NXQ_F32 only for ROW (the allreduce runs in fp32).
- * With NXQ_TP_ALLREDUCE=fused set when nxq_tp_init runs, a ROW call of
- * 1 <= M <= 32 tokens and at most 65536 output rows runs as ONE kernel per
- * rank instead: the decode GEMV pushes each finished 128-row tile's fp32
- * partial into every peer's exchange buffer (plain NVLink stores into a
- * buffer mapped through CUDA IPC at nxq_tp_init), raises a per-tile flag
- * there, waits (bounded by nxq_set_wait_limit; NXQ_ERR_TIMEOUT) for the
- * peers' flags of the tiles it finished, and stores the sum over ranks in
- * rank order (the same bits on every rank).  Every rank must issue the same
- * sequence of ROW calls, on one stream per rank. */
+ * By default (NXQ_TP_ALLREDUCE unset or "fused" when nxq_tp_init runs, 2 to
+ * 8 ranks), a ROW call of 1 <= M <= 32 tokens and at most 65536 output rows
+ * runs as ONE kernel per rank instead of a matmul and an allreduce: the
+ * decode GEMV writes each finished 128-row tile's fp32 partials into every
+ * rank's exchange buffer (plain NVLink stores into buffers mapped through
+ * CUDA IPC at nxq_tp_init; each value with the launch's tag in one 8-byte
+ * word), then reads the ranks' partials of its tiles from its own buffer,
+ * waiting (bounded by nxq_set_wait_limit; NXQ_ERR_TIMEOUT) until each word
+ * carries the launch's tag, and stores their sum in rank order (the same bits
+ * on every rank).  Every rank must issue the same sequence of ROW calls, on
+ * one stream per rank.  NXQ_TP_ALLREDUCE=nccl keeps every ROW call on NCCL. */
 NXQ_API int nxq_tp_qmatmul(nxq_weight_t shard, const void* x_dev, int x_dtype, void* y_dev,
                            int y_dtype, int64_t M, int split, void* stream);
 
@@ -355,9 +357,10 @@ NXQ_API int nxq_tp_qmatmul(nxq_weight_t shard, const void* x_dev, int x_dtype, v
  * collective that fails to enqueue aborts the communicator (NXQ_ERR_NCCL). */
 NXQ_API int nxq_tp_allreduce_f32(float* buf_dev, int64_t count, void* stream);
 
-/* Which peer-memory path this rank uses: 1 = allreduces up to 8 MB over peer
- * memory (NXQ_TP_ALLREDUCE=p2p), 2 = decode ROW calls fused with their
- * reduction (NXQ_TP_ALLREDUCE=fused), 0 = NCCL only. */
+/* Which peer-memory path this rank uses: 2 = decode ROW calls fused with
+ * their reduction (the default), 1 = allreduces up to 8 MB over peer memory
+ * (NXQ_TP_ALLREDUCE=p2p), 0 = NCCL only (NXQ_TP_ALLREDUCE=nccl, one rank, or
+ * buffers that could not be mapped). */
 NXQ_API int nxq_tp_p2p_enabled(int* on);
 
 /* Failure detection for the TP group (the reference has one device and

@@ -752,26 +752,32 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
         bool dead = false;
         // Row-split tensor parallelism (single C = 1 launches): this rank's
         // partial sums of a finished tile go to its slot in every rank's
-        // exchange buffer (remote stores over NVLink); the sum over ranks is
-        // taken after the tile loop.  The epoch is stable for the whole
-        // launch: the last CTA to finish advances it.
+        // exchange buffer as tagged words (remote stores over NVLink); the sum
+        // over ranks is taken after the tile loop.  The epoch is stable for
+        // the whole launch: the last CTA to finish advances it.
         unsigned long long tp_e = 0ull;
         if constexpr (TPX) tp_e = *reinterpret_cast<volatile unsigned long long*>(p.tp.ctl);
+        const unsigned long long tp_tag = (tp_e + 1ull) << 32;
         int tp_n = 0, tp_tiles[TPX ? kTpxCtaTiles : 1];
         auto tp_slot = [&](int q, int src, int t) {
-            return p.tp.recv[q] + ((size_t)(tp_e & 1ull) * p.tp.world + src) * kTpxSlotFloats +
+            return p.tp.recv[q] + ((size_t)(tp_e & 1ull) * p.tp.world + src) * kTpxSlotWords +
                    (size_t)t * TILE_ROWS * RS;
+        };
+        auto tp_put = [&](unsigned long long* w, float a, float b) {
+            asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(w),
+                         "l"(tp_tag | __float_as_uint(a)), "l"(tp_tag | __float_as_uint(b))
+                         : "memory");
         };
         // Stores a tile's sums A (PAIR: gate; AU: up): y = A, or silu(A) * AU,
         // plus the residual.
         auto store_vals = [&](int t, const auto& A, const auto& AU) {
             if constexpr (TPX) {
                 for (int q = 0; q < p.tp.world; ++q) {
-                    float* sl = tp_slot(q, p.tp.rank, t);
+                    unsigned long long* sl = tp_slot(q, p.tp.rank, t);
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt) {
-                        *reinterpret_cast<float2*>(sl + r0 * RS + 8 * nt + 2 * tq) = make_float2(A[nt][0], A[nt][1]);
-                        *reinterpret_cast<float2*>(sl + (r0 + 8) * RS + 8 * nt + 2 * tq) = make_float2(A[nt][2], A[nt][3]);
+                        tp_put(sl + r0 * RS + 8 * nt + 2 * tq, A[nt][0], A[nt][1]);
+                        tp_put(sl + (r0 + 8) * RS + 8 * nt + 2 * tq, A[nt][2], A[nt][3]);
                     }
                 }
                 if (tp_n < kTpxCtaTiles) tp_tiles[tp_n++] = t;
@@ -1001,65 +1007,50 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
                 }
             }
         }
-        if (TPX && gi == 0) {
+        if (TPX && gi == 0 && !s_abort) {
             // ---- the exchange: group 0 held every tile this CTA finished.
-            // Each thread's partials (local and remote stores) are made visible
-            // system-wide before thread 0 raises this rank's flag for each of
-            // those tiles in every peer; threads 0 .. world-1 then wait
-            // (bounded) for the peers' flags of the same tiles, and the group
-            // adds the slots in rank order (the same bits on every rank). ----
-            __threadfence_system();
-            named_sync(4, kThreads);
-            const unsigned long long want = tp_e + 1ull;
-            if (tid == 0 && !s_abort)
-                for (int i = 0; i < tp_n; ++i)
-                    for (int q = 0; q < p.tp.world; ++q)
-                        if (q != p.tp.rank)
-                            asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(
-                                             p.tp.flags[q] + (size_t)p.tp.rank * kTpxMaxTiles + tp_tiles[i]),
-                                         "l"(want)
-                                         : "memory");
-            if (tid < p.tp.world && tid != p.tp.rank && !s_abort) {
-                const long long w0 = clock64(), lim = ptx::wait_limit(p.status);
-                for (int i = 0; i < tp_n && !*ctl.abort; ++i) {
-                    const unsigned long long* f = p.tp.flags[p.tp.rank] + (size_t)tid * kTpxMaxTiles + tp_tiles[i];
-                    for (;;) {
-                        unsigned long long v;
-                        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(f) : "memory");
-                        if (v >= want) break;
-                        if (*ctl.abort || clock64() - w0 > lim) {
-                            if (!*ctl.abort) ptx::raise_timeout(ctl, 35);
-                            break;
-                        }
-                        __nanosleep(64);
+            // Each thread reads back its own fragment positions of every
+            // rank's slot in this rank's buffer, spinning (bounded) on each
+            // word until it carries this launch's tag, and adds the ranks in
+            // rank order (the same bits on every rank).  No fence or flag: a
+            // word and its tag travel in one 8-byte store (measured: per-tile
+            // flags behind a system-scope fence cost about 12 us per call). ----
+            const long long w0 = clock64(), lim = ptx::wait_limit(p.status);
+            bool ok = true;
+            auto tp_get = [&](const unsigned long long* w, float& a, float& b) {
+                unsigned long long u, v;
+                for (;;) {
+                    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(u), "=l"(v) : "l"(w) : "memory");
+                    if ((u & ~0xFFFFFFFFull) == tp_tag && (v & ~0xFFFFFFFFull) == tp_tag) break;
+                    if (*ctl.abort || clock64() - w0 > lim) {
+                        if (!*ctl.abort) ptx::raise_timeout(ctl, 35);
+                        ok = false;
+                        return;
+                    }
+                    __nanosleep(32);
+                }
+                a += __uint_as_float((unsigned)u);
+                b += __uint_as_float((unsigned)v);
+            };
+            for (int i = 0; i < tp_n && ok; ++i) {
+                const int t = tp_tiles[i];
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    for (int src = 0; src < p.tp.world && ok; ++src) {
+                        const unsigned long long* sl = tp_slot(p.tp.rank, src, t);
+                        tp_get(sl + r0 * RS + 8 * nt + 2 * tq, v[0], v[1]);
+                        tp_get(sl + (r0 + 8) * RS + 8 * nt + 2 * tq, v[2], v[3]);
+                    }
+                    if (!ok) break;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int tok = 8 * nt + 2 * tq + (e & 1);
+                        const int64_t row = (int64_t)t * TILE_ROWS + r0 + 8 * (e >> 1);
+                        if (tok < M && row < N) store_y(I.y, p.y_dtype, tok * N + row, v[e]);
                     }
                 }
             }
-            named_sync(4, kThreads);
-            if (!s_abort)
-                for (int i = 0; i < tp_n; ++i) {
-                    const int t = tp_tiles[i];
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt) {
-                        float2 a = make_float2(0.0f, 0.0f), b = make_float2(0.0f, 0.0f);
-                        for (int src = 0; src < p.tp.world; ++src) {
-                            const float* sl = tp_slot(p.tp.rank, src, t);
-                            const float2 x0 = __ldcg(reinterpret_cast<const float2*>(sl + r0 * RS + 8 * nt + 2 * tq));
-                            const float2 x1 = __ldcg(reinterpret_cast<const float2*>(sl + (r0 + 8) * RS + 8 * nt + 2 * tq));
-                            a.x += x0.x;
-                            a.y += x0.y;
-                            b.x += x1.x;
-                            b.y += x1.y;
-                        }
-                        const float v[4] = {a.x, a.y, b.x, b.y};
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int tok = 8 * nt + 2 * tq + (e & 1);
-                            const int64_t row = (int64_t)t * TILE_ROWS + r0 + 8 * (e >> 1);
-                            if (tok < M && row < N) store_y(I.y, p.y_dtype, tok * N + row, v[e]);
-                        }
-                    }
-                }
         }
     }
 

@@ -143,8 +143,7 @@ size_t p2p_bytes(int world, int64_t cap) {
 }
 
 size_t tpx_bytes(int world) {
-    return (size_t)2 * world * kTpxSlotFloats * sizeof(float) +
-           (size_t)world * kTpxMaxTiles * sizeof(unsigned long long) + 2 * sizeof(unsigned long long);
+    return ((size_t)2 * world * kTpxSlotWords + 2) * sizeof(unsigned long long);
 }
 
 cudaError_t launch_p2p_allreduce(const P2PParams& p, cudaStream_t st) {

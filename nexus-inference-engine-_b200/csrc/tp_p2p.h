@@ -30,21 +30,21 @@ struct P2PParams {
 size_t p2p_bytes(int world, int64_t cap);
 
 // ---- tile exchange of the fused row-split decode GEMV (qmm_mma.cu) ----------
-// Each rank's symmetric buffer holds recv [2][world][kTpxSlotFloats] fp32 - a
+// Each rank's symmetric buffer holds words [2][world][kTpxSlotWords] u64 - a
 // slot per launch parity and source rank, tile t of a launch at
 // [t][TILE_ROWS rows][RS tokens] (RS = the kernel's 8, 16 or 32 token
-// columns) - then flags [world][kTpxMaxTiles] u64 (flag (src, t) = e + 1 once
-// src's partial of tile t for the launch of epoch e has landed here), then the
-// control pair {epoch, done-CTA counter}.
+// columns) - then the control pair {epoch, done-CTA counter}.  A word carries
+// one fp32 partial in its low half and the tag (epoch + 1, 32 bits) of the
+// launch that wrote it in its high half: one 8-byte store, so a reader that
+// sees the tag it expects sees the value with it, without a fence or flag.
 constexpr int kTpxMaxTiles = 512;  // rows per call: 512 x 128 = 65536
 constexpr int kTpxCtaTiles = 16;   // finished tiles one CTA can hold for the exchange
-constexpr int64_t kTpxSlotFloats = (int64_t)kTpxMaxTiles * TILE_ROWS * 32;
+constexpr int64_t kTpxSlotWords = (int64_t)kTpxMaxTiles * TILE_ROWS * 32;
 
 struct TpExchange {
     int on, rank, world;
-    float* recv[kP2PMaxWorld];                // rank q's buffer (own: local pointer)
-    unsigned long long* flags[kP2PMaxWorld];  // rank q's flag array
-    unsigned long long* ctl;                  // this rank's control pair
+    unsigned long long* recv[kP2PMaxWorld];  // rank q's words (own: local pointer)
+    unsigned long long* ctl;                 // this rank's control pair
 };
 
 // Bytes of one rank's tile-exchange buffer.

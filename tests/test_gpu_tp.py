@@ -1,9 +1,10 @@
 """GPU, world_size 2 (skipped with fewer than two GPUs): the tensor-parallel
-entry point nxq_tp_qmatmul over NCCL against the unsharded oracle output.
+entry point nxq_tp_qmatmul against the unsharded oracle output, with the ROW
+split's reduction fused into the decode GEMV (the default) or on NCCL.
 
 Each rank registers its shard with nxq_weight_register_shard and runs the COL
 split (the full x, its [M][N/2] slice of y) and the ROW split (its K/2 slice
-of x; the library's fp32 NCCL allreduce leaves the full [M][N] on every rank).
+of x; the library's fp32 reduction leaves the full [M][N] on every rank).
 The COL slices are gathered over gloo; both results must be within the parity
 bar (rel-L2 <= 1e-3, fp32 accumulation) of loader.qmatmul on the whole weight,
 for decode (M <= 32, mma_gemv) and prefill (M > 32, tc_gemm) batch sizes.
@@ -34,7 +35,7 @@ def _free_port() -> int:
     return port
 
 
-def _worker(rank, world, port, t, N, K, Ms, q):
+def _worker(rank, world, port, t, N, K, Ms, q, mode):
     sys.path.insert(0, str(ROOT))
     sys.path.insert(0, str(ROOT / "nexus-inference-engine-_b200"))
     import datetime
@@ -51,6 +52,7 @@ def _worker(rank, world, port, t, N, K, Ms, q):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     joined = False
     try:
+        os.environ["NXQ_TP_ALLREDUCE"] = mode
         torch.cuda.set_device(rank)
         dev = torch.device("cuda", rank)
         nxq.init(rank)
@@ -88,8 +90,9 @@ def _worker(rank, world, port, t, N, K, Ms, q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("mode", ["fused", "nccl"])
 @pytest.mark.parametrize("t", [11, 12], ids=["Q3_K", "Q4_K"])
-def test_tp_qmatmul_two_gpus_matches_full(t):
+def test_tp_qmatmul_two_gpus_matches_full(t, mode):
     import torch
 
     if torch.cuda.device_count() < 2:
@@ -98,7 +101,7 @@ def test_tp_qmatmul_two_gpus_matches_full(t):
     q = ctx.Queue()
     port = _free_port()
     world, N, K, Ms = 2, 1024, 4096, (1, 8, 40)
-    procs = [ctx.Process(target=_worker, args=(r, world, port, t, N, K, Ms, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, t, N, K, Ms, q, mode)) for r in range(world)]
     for p in procs:
         p.start()
     try:
