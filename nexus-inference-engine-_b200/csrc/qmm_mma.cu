@@ -763,10 +763,18 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
             return p.tp.recv[q] + ((size_t)(tp_e & 1ull) * p.tp.world + src) * kTpxSlotWords +
                    (size_t)t * TILE_ROWS * RS;
         };
-        auto tp_put = [&](unsigned long long* w, float a, float b) {
-            asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(w),
-                         "l"(tp_tag | __float_as_uint(a)), "l"(tp_tag | __float_as_uint(b))
-                         : "memory");
+        // Words of (row, tokens tok, tok + 1): both when tok + 1 < M, the first
+        // when only tok < M, none past M or past the last row (writer and
+        // reader use the same rule).
+        auto tp_words = [&](int64_t row, int tok) { return row >= N || tok >= M ? 0 : tok + 1 < M ? 2 : 1; };
+        auto tp_put = [&](unsigned long long* w, int n, float a, float b) {
+            if (n == 2)
+                asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(w),
+                             "l"(tp_tag | __float_as_uint(a)), "l"(tp_tag | __float_as_uint(b))
+                             : "memory");
+            else if (n == 1)
+                asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(w), "l"(tp_tag | __float_as_uint(a))
+                             : "memory");
         };
         // Stores a tile's sums A (PAIR: gate; AU: up): y = A, or silu(A) * AU,
         // plus the residual.
@@ -776,8 +784,10 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
                     unsigned long long* sl = tp_slot(q, p.tp.rank, t);
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt) {
-                        tp_put(sl + r0 * RS + 8 * nt + 2 * tq, A[nt][0], A[nt][1]);
-                        tp_put(sl + (r0 + 8) * RS + 8 * nt + 2 * tq, A[nt][2], A[nt][3]);
+                        const int tok = 8 * nt + 2 * tq;
+                        const int64_t row = (int64_t)t * TILE_ROWS + r0;
+                        tp_put(sl + r0 * RS + tok, tp_words(row, tok), A[nt][0], A[nt][1]);
+                        tp_put(sl + (r0 + 8) * RS + tok, tp_words(row + 8, tok), A[nt][2], A[nt][3]);
                     }
                 }
                 if (tp_n < kTpxCtaTiles) tp_tiles[tp_n++] = t;
@@ -1017,10 +1027,14 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
             // flags behind a system-scope fence cost about 12 us per call). ----
             const long long w0 = clock64(), lim = ptx::wait_limit(p.status);
             bool ok = true;
-            auto tp_get = [&](const unsigned long long* w, float& a, float& b) {
-                unsigned long long u, v;
+            auto tp_get = [&](const unsigned long long* w, int n, float& a, float& b) {
+                if (n == 0) return;
+                unsigned long long u, v = tp_tag;
                 for (;;) {
-                    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(u), "=l"(v) : "l"(w) : "memory");
+                    if (n == 2)
+                        asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(u), "=l"(v) : "l"(w) : "memory");
+                    else
+                        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(u) : "l"(w) : "memory");
                     if ((u & ~0xFFFFFFFFull) == tp_tag && (v & ~0xFFFFFFFFull) == tp_tag) break;
                     if (*ctl.abort || clock64() - w0 > lim) {
                         if (!*ctl.abort) ptx::raise_timeout(ctl, 35);
@@ -1030,17 +1044,20 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
                     __nanosleep(32);
                 }
                 a += __uint_as_float((unsigned)u);
-                b += __uint_as_float((unsigned)v);
+                if (n == 2) b += __uint_as_float((unsigned)v);
             };
             for (int i = 0; i < tp_n && ok; ++i) {
                 const int t = tp_tiles[i];
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    const int tok = 8 * nt + 2 * tq;
+                    const int64_t row = (int64_t)t * TILE_ROWS + r0;
+                    const int n0 = tp_words(row, tok), n1 = tp_words(row + 8, tok);
                     for (int src = 0; src < p.tp.world && ok; ++src) {
                         const unsigned long long* sl = tp_slot(p.tp.rank, src, t);
-                        tp_get(sl + r0 * RS + 8 * nt + 2 * tq, v[0], v[1]);
-                        tp_get(sl + (r0 + 8) * RS + 8 * nt + 2 * tq, v[2], v[3]);
+                        tp_get(sl + r0 * RS + tok, n0, v[0], v[1]);
+                        tp_get(sl + (r0 + 8) * RS + tok, n1, v[2], v[3]);
                     }
                     if (!ok) break;
 #pragma unroll
@@ -1398,6 +1415,10 @@ int mma_qmatmul_tp(const Weight* w, const void* x, int x_dtype, float* y, int64_
                    const TpExchange& tp) {
     const TiledShape& s = w->shape;
     if (!mma_supported(s, M) || !tp.on) return NXQ_ERR_UNSUPPORTED;
+    // Each rank sends its whole partial to every peer: beyond kTpxMaxBytes a
+    // bandwidth-bound exchange loses to NCCL's allreduce.
+    if ((int64_t)(tp.world - 1) * s.N * M * (int64_t)sizeof(unsigned long long) > kTpxMaxBytes)
+        return NXQ_ERR_UNSUPPORTED;
     const int mt = M <= 8 ? 8 : M <= 16 ? 16 : 32;
     const bool aligned = ((uintptr_t)x % 16) == 0;
     const bool direct = aligned && (x_dtype == NXQ_F16 || (M <= 2 && (x_dtype == NXQ_F32 || x_dtype == NXQ_BF16)));

@@ -39,6 +39,12 @@ size_t p2p_bytes(int world, int64_t cap);
 // sees the tag it expects sees the value with it, without a fence or flag.
 constexpr int kTpxMaxTiles = 512;  // rows per call: 512 x 128 = 65536
 constexpr int kTpxCtaTiles = 16;   // finished tiles one CTA can hold for the exchange
+// Largest exchange a rank sends per call ((world - 1) x N x M words).  Every
+// rank sends its whole partial to every peer, so the volume grows with the
+// world; measured against GEMV + NCCL allreduce on B200 (405B-shaped rows,
+// N = 16384): fused faster at 7.3 MB (8 ranks, M = 8) and 4.2 MB (2 ranks,
+// M = 32), slower at 12.6 MB (4 ranks, M = 32) and 29 MB (8 ranks, M = 32).
+constexpr int64_t kTpxMaxBytes = 8 << 20;
 constexpr int64_t kTpxSlotWords = (int64_t)kTpxMaxTiles * TILE_ROWS * 32;
 
 struct TpExchange {
