@@ -781,6 +781,7 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
         auto store_vals = [&](int t, const auto& A, const auto& AU) {
             if constexpr (TPX) {
                 for (int q = 0; q < p.tp.world; ++q) {
+                    if (p.tp.owner && q != t % p.tp.world) continue;  // owner exchange: to tile t's owner only
                     unsigned long long* sl = tp_slot(q, p.tp.rank, t);
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt) {
@@ -1046,28 +1047,44 @@ __global__ void __launch_bounds__(Cfg<TYPE, MT, PAIR>::kAll, 1) mma_gemv_kernel(
                 a += __uint_as_float((unsigned)u);
                 if (n == 2) b += __uint_as_float((unsigned)v);
             };
-            for (int i = 0; i < tp_n && ok; ++i) {
-                const int t = tp_tiles[i];
+            // All-to-all exchange: every rank sums every tile it finished.
+            // Owner exchange (tile t owned by rank t mod world): the owner sums
+            // the ranks' partials of its tiles and sends the sum to the other
+            // ranks' slot (owner, t); the others store that sum.  Owned tiles
+            // go first, so that the sums leave as early as they can.
+            const int W = p.tp.world, me = p.tp.rank;
+            for (int pass = 0; pass < (p.tp.owner ? 2 : 1) && ok; ++pass)
+                for (int i = 0; i < tp_n && ok; ++i) {
+                    const int t = tp_tiles[i], o = t % W;
+                    if (p.tp.owner && (pass == 0) != (o == me)) continue;
+                    const bool sums = !p.tp.owner || o == me;
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                    const int tok = 8 * nt + 2 * tq;
-                    const int64_t row = (int64_t)t * TILE_ROWS + r0;
-                    const int n0 = tp_words(row, tok), n1 = tp_words(row + 8, tok);
-                    for (int src = 0; src < p.tp.world && ok; ++src) {
-                        const unsigned long long* sl = tp_slot(p.tp.rank, src, t);
-                        tp_get(sl + r0 * RS + tok, n0, v[0], v[1]);
-                        tp_get(sl + (r0 + 8) * RS + tok, n1, v[2], v[3]);
-                    }
-                    if (!ok) break;
+                    for (int nt = 0; nt < NT; ++nt) {
+                        float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                        const int tok = 8 * nt + 2 * tq;
+                        const int64_t row = (int64_t)t * TILE_ROWS + r0;
+                        const int n0 = tp_words(row, tok), n1 = tp_words(row + 8, tok);
+                        for (int src = sums ? 0 : o; src < (sums ? W : o + 1) && ok; ++src) {
+                            const unsigned long long* sl = tp_slot(me, src, t);
+                            tp_get(sl + r0 * RS + tok, n0, v[0], v[1]);
+                            tp_get(sl + (r0 + 8) * RS + tok, n1, v[2], v[3]);
+                        }
+                        if (!ok) break;
+                        if (p.tp.owner && sums)
+                            for (int q = 0; q < W; ++q)
+                                if (q != me) {
+                                    unsigned long long* sl = tp_slot(q, me, t);
+                                    tp_put(sl + r0 * RS + tok, n0, v[0], v[1]);
+                                    tp_put(sl + (r0 + 8) * RS + tok, n1, v[2], v[3]);
+                                }
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int tok = 8 * nt + 2 * tq + (e & 1);
-                        const int64_t row = (int64_t)t * TILE_ROWS + r0 + 8 * (e >> 1);
-                        if (tok < M && row < N) store_y(I.y, p.y_dtype, tok * N + row, v[e]);
+                        for (int e = 0; e < 4; ++e) {
+                            const int tk = tok + (e & 1);
+                            const int64_t rw = row + 8 * (e >> 1);
+                            if (tk < M && rw < N) store_y(I.y, p.y_dtype, tk * N + rw, v[e]);
+                        }
                     }
                 }
-            }
         }
     }
 
@@ -1415,10 +1432,12 @@ int mma_qmatmul_tp(const Weight* w, const void* x, int x_dtype, float* y, int64_
                    const TpExchange& tp) {
     const TiledShape& s = w->shape;
     if (!mma_supported(s, M) || !tp.on) return NXQ_ERR_UNSUPPORTED;
-    // Each rank sends its whole partial to every peer: beyond kTpxMaxBytes a
-    // bandwidth-bound exchange loses to NCCL's allreduce.
-    if ((int64_t)(tp.world - 1) * s.N * M * (int64_t)sizeof(unsigned long long) > kTpxMaxBytes)
-        return NXQ_ERR_UNSUPPORTED;
+    // Words a rank sends: all-to-all, its whole partial to every peer; owner
+    // exchange, 1/world of the tiles out and back to each peer.  Beyond
+    // kTpxMaxBytes a bandwidth-bound exchange loses to NCCL's allreduce.
+    const int64_t words = (int64_t)(tp.world - 1) * s.N * M;
+    const int64_t bytes = (tp.owner ? 2 * words / tp.world : words) * (int64_t)sizeof(unsigned long long);
+    if (bytes > kTpxMaxBytes) return NXQ_ERR_UNSUPPORTED;
     const int mt = M <= 8 ? 8 : M <= 16 ? 16 : 32;
     const bool aligned = ((uintptr_t)x % 16) == 0;
     const bool direct = aligned && (x_dtype == NXQ_F16 || (M <= 2 && (x_dtype == NXQ_F32 || x_dtype == NXQ_BF16)));

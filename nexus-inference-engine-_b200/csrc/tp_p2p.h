@@ -49,6 +49,7 @@ constexpr int64_t kTpxSlotWords = (int64_t)kTpxMaxTiles * TILE_ROWS * 32;
 
 struct TpExchange {
     int on, rank, world;
+    int owner;  // 1: owner exchange (tile t summed by rank t mod world, two hops); 0: all-to-all (one hop)
     unsigned long long* recv[kP2PMaxWorld];  // rank q's words (own: local pointer)
     unsigned long long* ctl;                 // this rank's control pair
 };

@@ -235,7 +235,7 @@ def test_tp_allreduce_peer_memory_two_gpus():
             assert out[0][key][2] == out[1][key][2], key  # every rank holds the same sum
 
 
-def _fused_worker(rank, world, port, cases, q):
+def _fused_worker(rank, world, port, cases, q, exchange):
     sys.path.insert(0, str(ROOT))
     sys.path.insert(0, str(ROOT / "nexus-inference-engine-_b200"))
     import datetime
@@ -254,6 +254,7 @@ def _fused_worker(rank, world, port, cases, q):
     joined = False
     try:
         os.environ["NXQ_TP_ALLREDUCE"] = "fused"
+        os.environ["NXQ_TP_EXCHANGE"] = exchange
         torch.cuda.set_device(rank)
         dev = torch.device("cuda", rank)
         nxq.init(rank)
@@ -314,10 +315,13 @@ def _fused_worker(rank, world, port, cases, q):
         dist.destroy_process_group()
 
 
-def test_tp_row_split_fused_exchange_two_gpus():
+@pytest.mark.parametrize("exchange", ["all", "owner"])
+def test_tp_row_split_fused_exchange_two_gpus(exchange):
     """NXQ_TP_ALLREDUCE=fused on two GPUs: decode-size ROW calls run as one
     GEMV launch per rank that pushes its partial tiles into the peer's
-    exchange buffer over NVLink and sums the ranks' tiles itself.  Within the
+    exchange buffer over NVLink and sums the ranks' tiles itself (all: every
+    rank sums every tile; owner: the owner of a tile, rank t mod 2, sums it
+    and sends the sum back, the exchange used from four ranks on).  Within the
     parity bar of the unsharded oracle (Q4_K and Q3_K; a shape with few row
     tiles and a long K, so stream-K splits tiles across CTAs), the same bits
     on both ranks, the same bits on three consecutive calls and on CUDA-graph
@@ -332,7 +336,7 @@ def test_tp_row_split_fused_exchange_two_gpus():
     world = 2
     cases = [(12, 1024, 4096, (1, 8, 32)), (11, 4096, 14336, (1, 8, 32)), (12, 14336, 4096, (8,)),
              (12, 1024, 4096, (40,))]
-    procs = [ctx.Process(target=_fused_worker, args=(r, world, port, cases, q)) for r in range(world)]
+    procs = [ctx.Process(target=_fused_worker, args=(r, world, port, cases, q, exchange)) for r in range(world)]
     for p in procs:
         p.start()
     try:
