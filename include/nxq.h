@@ -338,11 +338,11 @@ NXQ_API int nxq_tp_shutdown(void);
  * word), then reads the ranks' partials of its tiles from its own buffer,
  * waiting (bounded by nxq_set_wait_limit; NXQ_ERR_TIMEOUT) until each word
  * carries the launch's tag, and stores their sum in rank order (the same bits
- * on every rank).  From 4 ranks on the exchange has tile owners instead:
- * rank r sends its partials of tile t only to rank t mod world, which sums
- * the ranks' partials in rank order and sends the sum back (2 (world-1)/world
- * of the output per rank instead of world-1 times it, over two hops;
- * NXQ_TP_EXCHANGE=all / owner forces either).  Calls whose exchange would
+ * on every rank).  With NXQ_TP_EXCHANGE=owner the exchange has tile owners
+ * instead: rank r sends its partials of tile t only to rank t mod world,
+ * which sums the ranks' partials in rank order and sends the sum back
+ * (2 (world-1)/world of the output per rank instead of world-1 times it,
+ * over two hops).  Calls whose exchange would
  * exceed 8 MB per rank use NCCL.  Every rank must issue the same sequence of
  * ROW calls, on one stream per rank.  NXQ_TP_ALLREDUCE=nccl keeps every ROW
  * call on NCCL. */

@@ -242,12 +242,12 @@ void tpx_setup() {
     t.on = 1;
     t.rank = g_rank;
     t.world = g_world;
-    // Owner exchange from 4 ranks on (an all-to-all's volume grows with the
-    // world, the owner exchange's stays under twice the output; at 2 ranks
-    // both move one copy and the all-to-all takes one hop fewer).
-    // NXQ_TP_EXCHANGE=all / owner forces either.
+    // NXQ_TP_EXCHANGE=owner: the owner exchange (an all-to-all's volume grows
+    // with the world, the owner exchange's stays under twice the output, at
+    // the cost of a second hop).  Opt-in: verified on two GPUs, not yet
+    // measured at 4 or 8 ranks, where the all-to-all default was measured.
     const char* ex = getenv("NXQ_TP_EXCHANGE");
-    t.owner = ex && strcmp(ex, "owner") == 0 ? 1 : ex && strcmp(ex, "all") == 0 ? 0 : g_world >= 4 ? 1 : 0;
+    t.owner = ex && strcmp(ex, "owner") == 0 ? 1 : 0;
     for (int q = 0; q < g_world; ++q) t.recv[q] = static_cast<unsigned long long*>(g_tpx.buf.at[q]);
     t.ctl = t.recv[g_rank] + (size_t)2 * g_world * kTpxSlotWords;
     g_tpx.on = true;

@@ -321,7 +321,7 @@ def test_tp_row_split_fused_exchange_two_gpus(exchange):
     GEMV launch per rank that pushes its partial tiles into the peer's
     exchange buffer over NVLink and sums the ranks' tiles itself (all: every
     rank sums every tile; owner: the owner of a tile, rank t mod 2, sums it
-    and sends the sum back, the exchange used from four ranks on).  Within the
+    and sends the sum back, NXQ_TP_EXCHANGE=owner).  Within the
     parity bar of the unsharded oracle (Q4_K and Q3_K; a shape with few row
     tiles and a long K, so stream-K splits tiles across CTAs), the same bits
     on both ranks, the same bits on three consecutive calls and on CUDA-graph
